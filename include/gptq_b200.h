@@ -1,0 +1,197 @@
+/*
+ * gptq_b200.h -- C ABI of the B200 (sm_100a) GPTQ calibration library.
+ *
+ * Drop-in compute boundary for Stage A of the mlx_gptq calibration engine:
+ * Hessian accumulation -> damped Cholesky / H^-1 factor -> GPTQ column loop on
+ * the MLX affine, MXFP4 or MXFP8 grid -> code/scale packing. Each entry point
+ * names the reference interface (file:line, paths inside the mlx_gptq project)
+ * whose computation it replaces.
+ *
+ * Conventions
+ *  - Every pointer argument is DEVICE memory unless its comment says "host".
+ *  - Tensors are dense row-major with the shapes given; B = batch (experts),
+ *    R = out_features (rows), C = in_features (columns), G = group size.
+ *  - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *    Calls only enqueue work unless a comment says the call synchronizes.
+ *  - Return value: GQ_OK or one of the GQ_ERR_* codes; gq_last_error() gives a
+ *    message for the last failing call on the calling host thread.
+ *  - Re-entrant: no mutable global state; the library allocates no device memory.
+ *    Scratch is caller-provided ("workspace"), sized by the *_workspace_size
+ *    queries.
+ *  - Device-side waits are bounded (2 s); a kernel that gives up writes
+ *    GQ_ERR_TIMEOUT to the optional device word `status` and returns.
+ */
+#ifndef GPTQ_B200_H_
+#define GPTQ_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GQ_ABI_VERSION 1
+
+/* status codes */
+#define GQ_OK 0
+#define GQ_ERR_ARG 1      /* bad argument (shape, dtype, alignment, mode)      */
+#define GQ_ERR_NOT_PD 2   /* Hessian not positive definite after escalation    */
+#define GQ_ERR_CUDA 3     /* CUDA runtime / driver error                       */
+#define GQ_ERR_TIMEOUT 4  /* a bounded device-side wait gave up                */
+
+/* element types */
+#define GQ_F32 0
+#define GQ_BF16 1
+#define GQ_F16 2
+
+/* quantization modes (mlx_gptq/grid.py:20) */
+#define GQ_AFFINE 0
+#define GQ_MXFP4 1
+#define GQ_MXFP8 2
+
+/* affine clip search (mlx_gptq/grid.py:167-212) */
+#define GQ_CLIP_MINMAX 0
+#define GQ_CLIP_MSE 1
+
+/* MXFP GPTQ algorithm (mlx_gptq/gptq.py:90-92) */
+#define GQ_MX_GROUPWISE 0
+#define GQ_MX_SAFE_SCALE_SEARCH 1
+
+int gq_abi_version(void);
+const char* gq_status_string(int status);
+const char* gq_last_error(void);
+
+/* ------------------------------------------------------------------------
+ * Hessian accumulation
+ * ------------------------------------------------------------------------ */
+
+/* H = beta * H + alpha * X^T X.
+ * X: bf16 [n, c] with row stride ldx elements (ldx % 8 == 0, X 16-byte aligned).
+ * H: fp32 [c, c] with row stride ldh elements. Products of bf16 values are
+ * accumulated in fp32 on the tensor cores (tcgen05, TMEM accumulators); only
+ * tiles on or above the diagonal are computed and the result is mirrored, so
+ * the written H is exactly symmetric.
+ * Replaces Stash.hessian (mlx_gptq/capture.py:68-76), which is the case
+ * alpha = 1, beta = 0 (first chunk) / 1 (later chunks). */
+int gq_hessian_bf16(const void* X, int64_t n, int64_t c, int64_t ldx, float* H, int64_t ldh, float alpha,
+                    float beta, int32_t* status, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Solver pieces (mlx_gptq/gptq.py)
+ * ------------------------------------------------------------------------ */
+
+/* Dead columns (gptq.py:216-222): for every (b, j) with H[b, j, j] <= 0 set
+ * H[b, j, j] = 1 (in place) and dead[b, j] = 1, else dead[b, j] = 0.
+ * H: fp32 [B, C, C]; dead: uint8 [B, C]. */
+int gq_dead_columns(float* H, int64_t B, int64_t C, uint8_t* dead, void* stream);
+
+/* Upper Cholesky factor of the damped inverse of every 32x32 diagonal block:
+ * U[b, g] = chol((H[b, g, g] + damp * mean(diag) * I)^-1, upper), with the damping
+ * escalated x10 per block on failure, at most 6 attempts (gptq.py:27-66 as
+ * called per group by gptq.py:99-100).
+ * H: fp32 [B, C, C] (C % 32 == 0); U: fp32 [B, C/32, 32, 32];
+ * info: int32 [B, C/32], 0 = factored, else 1 + number of failed attempts (7 =
+ * gave up); damp_used: fp32 [B, C/32] (nullable). */
+int gq_mx_prepare_hinv(const float* H, int64_t B, int64_t C, float damp, float* U, int32_t* info,
+                       float* damp_used, void* stream);
+
+/* Upper Cholesky factor of the damped inverse of the full H (gptq.py:27-66):
+ * U[b] = chol((H[b] + damp_b * mean(diag H[b]) * I)^-1, upper); damp_b starts at
+ * `damp` and is escalated x10 for items whose factorization fails, at most 6
+ * attempts. SYNCHRONIZES `stream` after each attempt to read the per-item
+ * status. Returns GQ_ERR_NOT_PD if an item still fails (info[b] != 0).
+ * H: fp32 [B, C, C] (C % 64 == 0); U: fp32 [B, C, C] (upper; lower part zero);
+ * info: int32 [B]; damp_used: fp32 [B] (nullable). */
+size_t gq_prepare_hinv_workspace_size(int64_t B, int64_t C);
+int gq_prepare_hinv(const float* H, int64_t B, int64_t C, float damp, float* U, int32_t* info, float* damp_used,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* MXFP GPTQ (gptq.py:69-180): per 32-column group, sequential GPTQ with a fixed
+ * E8M0 scale (groupwise: the RTN scale; safe-scale-search: the scale offset with
+ * the smallest e^T H_g e, then GPTQ kept only if its objective is <= the best
+ * RTN objective), range guard |dq| <= max(32 * max|w|, 2^-126).
+ * W: [B, R, C] of w_dtype (GQ_F32/GQ_BF16/GQ_F16), the original weights;
+ *    columns with dead[b, j] != 0 are treated as zero (dead: uint8 [B, C], nullable).
+ * H: fp32 [B, C, C] (after gq_dead_columns); U: from gq_mx_prepare_hinv;
+ * info: from gq_mx_prepare_hinv (groups with info != 0 are skipped; nullable).
+ * Outputs (each nullable except scales): q uint8 [B, R, C] codes (E2M1 nibble
+ * code or E4M3 byte); q_packed uint8 [B, R, C/2] two E2M1 codes per byte, low
+ * nibble first (mxfp4 only; the MLX uint32 words are these bytes read
+ * little-endian); scales uint8 [B, R, C/32] E8M0 bytes; w_dq [B, R, C] of
+ * wdq_dtype (GQ_F32 / GQ_BF16); rel_err fp32 [B] = ||W_dq - W||_F / ||W||_F
+ * (solve_gptq, gptq.py:300-302; needs workspace).
+ * Replaces gptq_quantize / solve_gptq for mode mxfp4 / mxfp8. */
+size_t gq_gptq_mxfp_workspace_size(int64_t B, int64_t R, int64_t C);
+int gq_gptq_mxfp(const void* W, int w_dtype, const float* H, const float* U, const uint8_t* dead,
+                 const int32_t* info, int64_t B, int64_t R, int64_t C, int mode, int algorithm, uint8_t* q,
+                 uint8_t* q_packed, uint8_t* scales, void* w_dq, int wdq_dtype, float* rel_err, void* workspace,
+                 size_t workspace_bytes, void* stream);
+
+/* Affine GPTQ (gptq.py:183-272): blocked column loop (block = max(block_size, G)
+ * rounded down to a multiple of G) with the MSE/minmax clip search at each group
+ * start on the compensated weights, bf16/fp16/fp32-rounded scale and bias
+ * before error feedback, in-block rank-1 updates and the lazy trailing update
+ * W[:, :, i2:] -= Err * U[i1:i2, i2:] after every block.
+ * W: fp32 [B, R, C] working weights, overwritten with W_dq (dead columns must
+ *    already be zero, see gq_prepare_weights); W_orig: [B, R, C] of w_dtype, the
+ *    untouched originals for rel_err (nullable).
+ * U: from gq_prepare_hinv. q: uint8 [B, R, C]; scales / biases: [B, R, C/G] of
+ * storage_dtype (GQ_BF16 / GQ_F16 / GQ_F32); rel_err fp32 [B] (nullable).
+ * G % 32 == 0 and G <= 256. */
+size_t gq_gptq_affine_workspace_size(int64_t B, int64_t R, int64_t C, int group_size, int block_size);
+int gq_gptq_affine(float* W, const void* W_orig, int w_dtype, const float* U, int64_t B, int64_t R, int64_t C,
+                   int bits, int group_size, int block_size, int clip, int storage_dtype, uint8_t* q, void* scales,
+                   void* biases, float* rel_err, void* workspace, size_t workspace_bytes, void* stream);
+
+/* W_out (fp32 [B, R, C]) = W_in converted to fp32, with columns where
+ * dead[b, j] != 0 set to zero (the W.float().clone() + dead-column zeroing of
+ * gptq.py:288 and gptq.py:219-221). dead is nullable. */
+int gq_prepare_weights(const void* W_in, int w_dtype, const uint8_t* dead, int64_t B, int64_t R, int64_t C,
+                       float* W_out, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Grids (mlx_gptq/grid.py)
+ * ------------------------------------------------------------------------ */
+
+/* RTN on the MLX affine grid (rtn_quantize, grid.py:224-246 with choose_qparams
+ * grid.py:167-212 and quantize_with_params grid.py:215-221).
+ * W: [rows, C] of w_dtype; q uint8 [rows, C]; scales / biases [rows, C/G] of
+ * storage_dtype; w_dq [rows, C] of wdq_dtype (nullable). */
+int gq_rtn_affine(const void* W, int w_dtype, int64_t rows, int64_t C, int bits, int group_size, int clip,
+                  int storage_dtype, uint8_t* q, void* scales, void* biases, void* w_dq, int wdq_dtype,
+                  void* stream);
+
+/* Native MXFP RTN (rtn_quantize_mxfp, grid.py:142-151 with choose_mxfp_scale
+ * grid.py:61-79 and quantize_mxfp_with_scale grid.py:108-124).
+ * W: [rows, C] (C % 32 == 0); q uint8 [rows, C]; scales uint8 [rows, C/32];
+ * q_packed uint8 [rows, C/2] (mxfp4 only, nullable); w_dq nullable. */
+int gq_rtn_mxfp(const void* W, int w_dtype, int64_t rows, int64_t C, int mode, uint8_t* q, uint8_t* q_packed,
+                uint8_t* scales, void* w_dq, int wdq_dtype, void* stream);
+
+/* dequantize_artifact (grid.py:154-164, dequantize_mxfp grid.py:127-139):
+ * affine: out = q * scale + bias (scales/biases [rows, C/G] of scale_dtype);
+ * mxfp: out = value(q) * 2^(scale_byte - 127) (scales uint8 [rows, C/32]). */
+int gq_dequantize(const uint8_t* q, const void* scales, const void* biases, int scale_dtype, int64_t rows,
+                  int64_t C, int mode, int group_size, float* out, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Packing (mlx_gptq/packing.py, mlx_gptq/artifacts.py)
+ * ------------------------------------------------------------------------ */
+
+/* pack_q (packing.py:15-26): words[r, i] = sum_k q[r, i*per + k] << (bits*k),
+ * per = 32/bits, bits in {2, 4, 8}; q uint8 [rows, C] (C % per == 0). */
+int gq_pack_q(const uint8_t* q, int64_t rows, int64_t C, int bits, uint32_t* words, void* stream);
+/* unpack_q (packing.py:33-39): q[r, j] for j < out_cols from words [rows, n_words]. */
+int gq_unpack_q(const uint32_t* words, int64_t rows, int64_t n_words, int bits, int64_t out_cols, uint8_t* q,
+                void* stream);
+/* pack_nibbles (artifacts.py:30-32): out[r, i] = q[r, 2i] | q[r, 2i+1] << 4. */
+int gq_pack_nibbles(const uint8_t* q, int64_t rows, int64_t C, uint8_t* out, void* stream);
+/* unpack_nibbles (artifacts.py:35-39). */
+int gq_unpack_nibbles(const uint8_t* packed, int64_t rows, int64_t n_bytes, uint8_t* q, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GPTQ_B200_H_ */

@@ -1,0 +1,640 @@
+// Affine GPTQ (mlx_gptq/gptq.py:183-272) and the full-size damped factor
+// U = chol((H + damp*mean(diag H)*I)^-1, upper) (gptq.py:27-66).
+//
+// Factor. With J the index reversal, if J Hd J = L L^T (lower Cholesky) then
+// Hd = V V^T with V = J L J upper and Hd^-1 = U^T U for U = V^-1 = J L^-1 J. So
+// the upper Cholesky factor of the inverse is the reversed inverse of the
+// Cholesky factor of the reversed matrix: one factorization and one triangular
+// inversion (C^3/3 each) instead of factor + cholesky_inverse + factor. Both run
+// blocked on 64x64 tiles in float32: the factorization right-looking (diagonal
+// block factor + inverse, panel solve, trailing SYRK), the inversion by
+// doubling (inverses of 2^k-blocks combined pairwise with two GEMMs).
+//
+// Column loop. One warp per weight row owns one block of bs columns in
+// registers (lane l holds columns l, l+32, ...): the clip search at each group
+// start, the per-column quantize / error / in-block rank-1 update. Err [B, R, bs]
+// goes to the workspace and the trailing update W[:, :, i2:] -= Err * U[i1:i2, i2:]
+// is a batched float32 GEMM.
+#include <vector>
+
+#include "gq_affine_grid.cuh"
+
+namespace gq {
+namespace aff {
+
+constexpr int NB = 64;  // factorization block
+
+// ---------------------------------------------------------------------------
+// 64x64 float32 tile GEMM building block (256 threads, 4x4 outputs each)
+// acc[r][c] += sum_t A(r, t) * B(t, c) over K, with
+//   A(r, t) = TRANS_A ? A[t * lda + r] : A[r * lda + t]
+//   B(t, c) = TRANS_B ? B[c * ldb + t] : B[t * ldb + c]
+// Rows >= m_lim / columns >= n_lim read as zero.
+// ---------------------------------------------------------------------------
+template <bool TRANS_A, bool TRANS_B>
+__device__ __forceinline__ void tile_gemm(const float* __restrict__ A, int64_t lda, const float* __restrict__ Bm,
+                                          int64_t ldb, int K, int m_lim, int n_lim, float (&acc)[4][4],
+                                          float (*As)[68], float (*Bs)[68]) {
+  const int tid = threadIdx.x;
+  const int ty = tid >> 4, tx = tid & 15;
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    // A chunk 64 x 16 into As[t][r]
+    if (TRANS_A) {
+      const int t = tid >> 4, r4 = (tid & 15) * 4;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int r = r4 + u;
+        As[t][r] = (r < m_lim && k0 + t < K) ? A[int64_t(k0 + t) * lda + r] : 0.0f;
+      }
+    } else {
+      const int r = tid >> 2, t4 = (tid & 3) * 4;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int t = k0 + t4 + u;
+        As[t4 + u][r] = (r < m_lim && t < K) ? A[int64_t(r) * lda + t] : 0.0f;
+      }
+    }
+    if (TRANS_B) {
+      const int cc = tid >> 2, t4 = (tid & 3) * 4;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int t = k0 + t4 + u;
+        Bs[t4 + u][cc] = (cc < n_lim && t < K) ? Bm[int64_t(cc) * ldb + t] : 0.0f;
+      }
+    } else {
+      const int t = tid >> 4, c4 = (tid & 15) * 4;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int cc = c4 + u;
+        Bs[t][cc] = (cc < n_lim && k0 + t < K) ? Bm[int64_t(k0 + t) * ldb + cc] : 0.0f;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+      const float4 a = *reinterpret_cast<const float4*>(&As[t][ty * 4]);
+      const float4 b = *reinterpret_cast<const float4*>(&Bs[t][tx * 4]);
+      const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+}
+
+// C(r, c) = alpha * acc + beta * C(r, c) for the thread's 4x4 outputs.
+__device__ __forceinline__ void tile_store(float* __restrict__ Cm, int64_t ldc, int m_lim, int n_lim,
+                                           const float (&acc)[4][4], float alpha, float beta) {
+  const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = ty * 4 + i;
+    if (r >= m_lim) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int cc = tx * 4 + j;
+      if (cc >= n_lim) continue;
+      float* p = Cm + int64_t(r) * ldc + cc;
+      const float v = alpha * acc[i][j];
+      *p = beta == 0.0f ? v : beta * *p + v;
+    }
+  }
+}
+
+// Batched GEMM C = alpha*A*B + beta*C on 64x64 tiles; batch index z = outer*n_inner + inner.
+struct GemmBatch {
+  const float* A;
+  const float* Bm;
+  float* Cm;
+  int64_t lda, ldb, ldc;
+  int64_t sa_o, sb_o, sc_o;  // outer strides (elements)
+  int64_t sa_i, sb_i, sc_i;  // inner strides
+  int n_inner;
+  int M, N, K;
+  float alpha, beta;
+  const int32_t* skip;  // per outer item: nonzero = skip (nullable)
+};
+
+template <bool TRANS_A, bool TRANS_B>
+__global__ void __launch_bounds__(256) gemm_kernel(GemmBatch p) {
+  __shared__ __align__(16) float As[16][68];
+  __shared__ __align__(16) float Bs[16][68];
+  const int64_t z = blockIdx.z;
+  const int64_t o = z / p.n_inner, in = z % p.n_inner;
+  if (p.skip && p.skip[o]) return;
+  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  const float* A = p.A + o * p.sa_o + in * p.sa_i + (TRANS_A ? int64_t(m0) : int64_t(m0) * p.lda);
+  const float* Bm = p.Bm + o * p.sb_o + in * p.sb_i + (TRANS_B ? int64_t(n0) * p.ldb : int64_t(n0));
+  float* Cm = p.Cm + o * p.sc_o + in * p.sc_i + int64_t(m0) * p.ldc + n0;
+  float acc[4][4] = {};
+  tile_gemm<TRANS_A, TRANS_B>(A, p.lda, Bm, p.ldb, p.K, p.M - m0, p.N - n0, acc, As, Bs);
+  tile_store(Cm, p.ldc, p.M - m0, p.N - n0, acc, p.alpha, p.beta);
+}
+
+static int launch_gemm(const GemmBatch& p, bool trans_a, bool trans_b, int64_t batches, cudaStream_t s) {
+  if (batches <= 0 || p.M <= 0 || p.N <= 0) return GQ_OK;
+  const dim3 grid(unsigned((p.N + 63) / 64), unsigned((p.M + 63) / 64), unsigned(batches));
+  if (trans_a && trans_b)
+    gemm_kernel<true, true><<<grid, 256, 0, s>>>(p);
+  else if (trans_a)
+    gemm_kernel<true, false><<<grid, 256, 0, s>>>(p);
+  else if (trans_b)
+    gemm_kernel<false, true><<<grid, 256, 0, s>>>(p);
+  else
+    gemm_kernel<false, false><<<grid, 256, 0, s>>>(p);
+  return check_launch("gemm_kernel");
+}
+
+// ---------------------------------------------------------------------------
+// factorization kernels (blockIdx.y = batch item; items with skip[b] != 0 idle)
+// ---------------------------------------------------------------------------
+struct FactorState {
+  float* diag_mean;  // [B]
+  float* cur_damp;   // [B]
+  int32_t* info;     // [B] 0 = ok, else failing column + 1
+  int32_t* skip;     // [B] 1 = do not (re)factor this item
+};
+
+__global__ void diag_mean_kernel(const float* __restrict__ H, int64_t C, float damp, FactorState st) {
+  const int64_t b = blockIdx.x;
+  float s = 0.0f;
+  for (int64_t i = threadIdx.x; i < C; i += blockDim.x) s += H[(b * C + i) * C + i];
+  __shared__ float red[256];
+  red[threadIdx.x] = s;
+  __syncthreads();
+  for (int k = blockDim.x / 2; k > 0; k >>= 1) {
+    if (threadIdx.x < k) red[threadIdx.x] += red[threadIdx.x + k];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    st.diag_mean[b] = fmaxf(red[0] / float(C), 1e-8f);
+    st.cur_damp[b] = damp;
+    st.info[b] = 0;
+    st.skip[b] = 0;
+  }
+}
+
+// Hr[b] = J (H[b] + lam_b I) J, lower triangle (incl. diagonal), lam_b = diag_mean * cur_damp.
+__global__ void build_reversed_kernel(const float* __restrict__ H, int64_t C, float* __restrict__ Hr, FactorState st) {
+  const int64_t b = blockIdx.y;
+  if (st.skip[b]) return;
+  const float lam = st.diag_mean[b] * st.cur_damp[b];
+  const int64_t n = C * C;
+  for (int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; idx < n; idx += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t i = idx / C, j = idx % C;
+    if (j > i) continue;
+    float v = H[(b * C + (C - 1 - i)) * C + (C - 1 - j)];
+    if (i == j) v = v + lam;
+    Hr[(b * C + i) * C + j] = v;
+  }
+}
+
+// Factor the 64x64 diagonal block k of Hr[b] (lower) in shared memory and store
+// its inverse (lower, zeros above) in Dinv[b][k]. Records the failing column.
+__global__ void __launch_bounds__(256) potrf_diag_kernel(float* __restrict__ Hr, int64_t C, int k,
+                                                         float* __restrict__ Dinv, FactorState st) {
+  __shared__ float S[NB][NB + 1];
+  __shared__ float X[NB][NB + 1];
+  __shared__ int fail;
+  const int64_t b = blockIdx.x;
+  if (st.skip[b] || st.info[b]) return;
+  const int tid = threadIdx.x;
+  float* blk = Hr + (b * C + int64_t(k) * NB) * C + int64_t(k) * NB;
+  for (int i = tid; i < NB * NB; i += 256) S[i / NB][i % NB] = blk[int64_t(i / NB) * C + (i % NB)];
+  if (tid == 0) fail = 0;
+  __syncthreads();
+  for (int kk = 0; kk < NB; ++kk) {
+    if (tid == 0) {
+      const float piv = S[kk][kk];
+      if (!(piv > 0.0f))
+        fail = kk + 1;
+      else
+        S[kk][kk] = sqrtf(piv);
+    }
+    __syncthreads();
+    if (fail) break;
+    const float d = S[kk][kk];
+    if (tid > kk && tid < NB) S[tid][kk] = S[tid][kk] / d;
+    __syncthreads();
+    // trailing update of the lower triangle: rows i > kk, columns kk < j <= i
+    const int m = NB - kk - 1;
+    for (int e = tid; e < m * m; e += 256) {
+      const int i = kk + 1 + e / m, j = kk + 1 + e % m;
+      if (j <= i) S[i][j] = S[i][j] - S[i][kk] * S[j][kk];
+    }
+    __syncthreads();
+  }
+  if (fail) {
+    if (tid == 0) st.info[b] = k * NB + fail;
+    return;
+  }
+  // write L_kk back (lower) and invert it: thread t < 64 solves column t
+  for (int i = tid; i < NB * NB; i += 256) {
+    const int r = i / NB, c = i % NB;
+    if (c <= r) blk[int64_t(r) * C + c] = S[r][c];
+  }
+  if (tid < NB) {
+    const int j = tid;
+    for (int i = 0; i < NB; ++i) {
+      float x = 0.0f;
+      if (i == j) {
+        x = 1.0f / S[i][i];
+      } else if (i > j) {
+        float acc = 0.0f;
+        for (int t = j; t < i; ++t) acc = fmaf(S[i][t], X[t][j], acc);
+        x = -acc / S[i][i];
+      }
+      X[i][j] = x;
+    }
+  }
+  __syncthreads();
+  float* D = Dinv + (b * (C / NB) + k) * NB * NB;
+  for (int i = tid; i < NB * NB; i += 256) D[i] = X[i / NB][i % NB];
+}
+
+// Panel solve: A[i][k] = A[i][k] * L_kk^-T for block rows i > k (in place, one CTA per block).
+__global__ void __launch_bounds__(256) trsm_panel_kernel(float* __restrict__ Hr, int64_t C, int k,
+                                                         const float* __restrict__ Dinv, FactorState st) {
+  __shared__ __align__(16) float As[16][68];
+  __shared__ __align__(16) float Bs[16][68];
+  const int64_t b = blockIdx.y;
+  if (st.skip[b] || st.info[b]) return;
+  const int i = k + 1 + blockIdx.x;
+  float* blk = Hr + (b * C + int64_t(i) * NB) * C + int64_t(k) * NB;
+  const float* D = Dinv + (b * (C / NB) + k) * NB * NB;
+  float acc[4][4] = {};
+  tile_gemm<false, true>(blk, C, D, NB, NB, NB, NB, acc, As, Bs);  // out(r,c) = sum_t A(r,t) * D(c,t)
+  // all reads of blk are done (tile_gemm ends with a barrier): store in place
+  tile_store(blk, C, NB, NB, acc, 1.0f, 0.0f);
+}
+
+// Trailing update on block tiles (i, j) with k < j <= i: A_ij -= A_ik A_jk^T.
+__global__ void __launch_bounds__(256) syrk_kernel(float* __restrict__ Hr, int64_t C, int k, FactorState st) {
+  __shared__ __align__(16) float As[16][68];
+  __shared__ __align__(16) float Bs[16][68];
+  const int64_t b = blockIdx.y;
+  if (st.skip[b] || st.info[b]) return;
+  // linear tile index -> (ii, jj), 0 <= jj <= ii < m
+  const int t = blockIdx.x;
+  int ii = int((sqrtf(8.0f * float(t) + 1.0f) - 1.0f) * 0.5f);
+  while ((ii + 1) * (ii + 2) / 2 <= t) ++ii;
+  while (ii * (ii + 1) / 2 > t) --ii;
+  const int jj = t - ii * (ii + 1) / 2;
+  const int i = k + 1 + ii, j = k + 1 + jj;
+  const float* Aik = Hr + (b * C + int64_t(i) * NB) * C + int64_t(k) * NB;
+  const float* Ajk = Hr + (b * C + int64_t(j) * NB) * C + int64_t(k) * NB;
+  float* Aij = Hr + (b * C + int64_t(i) * NB) * C + int64_t(j) * NB;
+  float acc[4][4] = {};
+  tile_gemm<false, true>(Aik, C, Ajk, C, NB, NB, NB, acc, As, Bs);
+  tile_store(Aij, C, NB, NB, acc, -1.0f, 1.0f);
+}
+
+// Linv initialisation: diagonal blocks = Dinv, everything else zero.
+__global__ void init_linv_kernel(float* __restrict__ Li, int64_t C, const float* __restrict__ Dinv, FactorState st) {
+  const int64_t b = blockIdx.y;
+  if (st.info[b]) return;
+  const int64_t n = C * C;
+  for (int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; idx < n; idx += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t i = idx / C, j = idx % C;
+    float v = 0.0f;
+    if (i / NB == j / NB) v = Dinv[((b * (C / NB) + i / NB) * NB + (i % NB)) * NB + (j % NB)];
+    Li[b * n + idx] = v;
+  }
+}
+
+// In-place 180-degree rotation: U[i][j] <- Li[C-1-i][C-1-j] (Li lower -> U upper).
+__global__ void rotate_kernel(float* __restrict__ M, int64_t C, FactorState st) {
+  const int64_t b = blockIdx.y;
+  if (st.info[b]) return;
+  const int64_t n = C * C, half = n / 2;
+  float* m = M + b * n;
+  for (int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; idx < half; idx += int64_t(gridDim.x) * blockDim.x) {
+    const float a = m[idx], c = m[n - 1 - idx];
+    m[idx] = c;
+    m[n - 1 - idx] = a;
+  }
+}
+
+__global__ void escalate_kernel(int64_t B, FactorState st) {
+  const int64_t b = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  if (st.info[b]) {
+    st.cur_damp[b] = st.cur_damp[b] * 10.0f;
+    st.info[b] = 0;
+    st.skip[b] = 0;
+  } else {
+    st.skip[b] = 1;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// affine column loop: one warp per (row, item); block columns [i1, i1 + 32*VPB)
+// ---------------------------------------------------------------------------
+template <int VPL, int VPB>
+__global__ void __launch_bounds__(256) affine_block_kernel(float* __restrict__ W, const float* __restrict__ U,
+                                                           int64_t R, int64_t C, int64_t i1, int bits, int nshrink,
+                                                           int storage, uint8_t* __restrict__ q,
+                                                           void* __restrict__ scales, void* __restrict__ biases,
+                                                           float* __restrict__ Err) {
+  constexpr int G = 32 * VPL, BS = 32 * VPB;
+  __shared__ float pr[kMaxShrinks], pf[kMaxShrinks];
+  if (threadIdx.x < kMaxShrinks) shrink_factors(threadIdx.x, bits, pr[threadIdx.x], pf[threadIdx.x]);
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int64_t b = blockIdx.y;
+  const int64_t r = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (r >= R) return;
+  const int64_t ng = C / G;
+  float* wrow = W + (b * R + r) * C + i1;
+  const float* Ub = U + b * C * C + i1 * C + i1;  // U1 = U[i1:i2, i1:i2], row stride C
+  float w[VPB], dqv[VPB], ev[VPB], qv[VPB];
+#pragma unroll
+  for (int k = 0; k < VPB; ++k) w[k] = wrow[lane + 32 * k];
+  const float maxq = float((1 << bits) - 1);
+  float s = 0.0f, bb = 0.0f;
+#pragma unroll
+  for (int k = 0; k < VPB; ++k) {  // slot k = columns 32k .. 32k+31 of the block
+    if ((32 * k) % G == 0) {       // group start (gptq.py:250-256)
+      float v[VPL];
+#pragma unroll
+      for (int t = 0; t < VPL; ++t) v[t] = w[k + t];
+      warp_choose_qparams<VPL>(v, maxq, pr, pf, nshrink, storage, s, bb);
+      if (lane == 0) {
+        const int64_t g = (i1 + 32 * k) / G;
+        store_any(scales, (b * R + r) * ng + g, s, storage);
+        store_any(biases, (b * R + r) * ng + g, bb, storage);
+      }
+    }
+#pragma unroll 1
+    for (int l = 0; l < 32; ++l) {
+      const int j = 32 * k + l;
+      const float wj = __shfl_sync(0xFFFFFFFFu, w[k], l);
+      float qj;
+      const float dq = affine_quant(wj, s, bb, maxq, qj);
+      const float* urow = Ub + int64_t(j) * C;
+      const float e = (wj - dq) / __ldg(urow + j);
+      if (lane == l) {
+        dqv[k] = dq;
+        ev[k] = e;
+        qv[k] = qj;
+      }
+#pragma unroll
+      for (int kk = k; kk < VPB; ++kk) {
+        const int col = 32 * kk + lane;
+        if (col > j) w[kk] = w[kk] - e * __ldg(urow + col);
+      }
+    }
+  }
+  uint8_t* qrow = q + (b * R + r) * C + i1;
+  float* erow = Err + (b * R + r) * BS;
+#pragma unroll
+  for (int k = 0; k < VPB; ++k) {
+    wrow[lane + 32 * k] = dqv[k];
+    qrow[lane + 32 * k] = uint8_t(qv[k]);
+    erow[lane + 32 * k] = ev[k];
+  }
+}
+
+// rel_err partial sums over rows: partials[b][row-block] = (sum (dq-w)^2, sum w^2)
+template <typename Tin>
+__global__ void rel_partials_kernel(const float* __restrict__ Wdq, const Tin* __restrict__ W0, int64_t RC,
+                                    float* __restrict__ partials) {
+  const int64_t b = blockIdx.y;
+  float n = 0.0f, d = 0.0f;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < RC; i += int64_t(gridDim.x) * blockDim.x) {
+    const float w = to_f32<Tin>(W0[b * RC + i]);
+    const float e = Wdq[b * RC + i] - w;
+    n = fmaf(e, e, n);
+    d = fmaf(w, w, d);
+  }
+  n = warp_sum(n);
+  d = warp_sum(d);
+  __shared__ float rn[8], rd[8];
+  if ((threadIdx.x & 31) == 0) {
+    rn[threadIdx.x >> 5] = n;
+    rd[threadIdx.x >> 5] = d;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float sn = 0.0f, sd = 0.0f;
+    for (int w = 0; w < 8; ++w) sn += rn[w], sd += rd[w];
+    partials[(b * gridDim.x + blockIdx.x) * 2] = sn;
+    partials[(b * gridDim.x + blockIdx.x) * 2 + 1] = sd;
+  }
+}
+
+}  // namespace aff
+
+int launch_rel_err(const float* partials, int64_t B, int64_t per_b, float* rel, cudaStream_t s);
+
+}  // namespace gq
+
+using namespace gq;
+using namespace gq::aff;
+
+static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+extern "C" size_t gq_prepare_hinv_workspace_size(int64_t B, int64_t C) {
+  if (B <= 0 || C <= 0) return 0;
+  return align256(size_t(B) * C * C * 4) + align256(size_t(B) * C * NB * 4) + 4 * align256(size_t(B) * 4);
+}
+
+extern "C" int gq_prepare_hinv(const float* H, int64_t B, int64_t C, float damp, float* U, int32_t* info,
+                               float* damp_used, void* workspace, size_t workspace_bytes, void* stream) {
+  GQ_REQUIRE(H && U && info, "gq_prepare_hinv: null pointer");
+  GQ_REQUIRE(B > 0 && C > 0 && C % NB == 0, "gq_prepare_hinv: C=%lld must be a positive multiple of %d",
+             (long long)C, NB);
+  GQ_REQUIRE(B < 65536, "gq_prepare_hinv: batch too large");
+  const size_t need = gq_prepare_hinv_workspace_size(B, C);
+  GQ_REQUIRE(workspace && workspace_bytes >= need, "gq_prepare_hinv: workspace too small (%zu < %zu)",
+             workspace_bytes, need);
+  cudaStream_t s = (cudaStream_t)stream;
+  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  float* Hr = reinterpret_cast<float*>(ws);
+  ws += align256(size_t(B) * C * C * 4);
+  float* Dinv = reinterpret_cast<float*>(ws);
+  ws += align256(size_t(B) * C * NB * 4);
+  FactorState st;
+  st.diag_mean = reinterpret_cast<float*>(ws);
+  ws += align256(size_t(B) * 4);
+  st.cur_damp = reinterpret_cast<float*>(ws);
+  ws += align256(size_t(B) * 4);
+  st.info = reinterpret_cast<int32_t*>(ws);
+  ws += align256(size_t(B) * 4);
+  st.skip = reinterpret_cast<int32_t*>(ws);
+
+  const int nb = int(C / NB);
+  const unsigned ew_blocks = unsigned(std::min<int64_t>((C * C + 255) / 256, 4096));
+  diag_mean_kernel<<<unsigned(B), 256, 0, s>>>(H, C, damp, st);
+  std::vector<int32_t> hinfo(B);
+  bool ok = false;
+  for (int attempt = 0; attempt < 6; ++attempt) {
+    build_reversed_kernel<<<dim3(ew_blocks, unsigned(B)), 256, 0, s>>>(H, C, Hr, st);
+    for (int k = 0; k < nb; ++k) {
+      potrf_diag_kernel<<<unsigned(B), 256, 0, s>>>(Hr, C, k, Dinv, st);
+      const int m = nb - k - 1;
+      if (m > 0) {
+        trsm_panel_kernel<<<dim3(unsigned(m), unsigned(B)), 256, 0, s>>>(Hr, C, k, Dinv, st);
+        syrk_kernel<<<dim3(unsigned(m * (m + 1) / 2), unsigned(B)), 256, 0, s>>>(Hr, C, k, st);
+      }
+    }
+    int stl = check_launch("cholesky kernels");
+    if (stl != GQ_OK) return stl;
+    GQ_CUDA_TRY(cudaMemcpyAsync(hinfo.data(), st.info, size_t(B) * 4, cudaMemcpyDeviceToHost, s));
+    GQ_CUDA_TRY(cudaStreamSynchronize(s));
+    bool any_fail = false;
+    for (int64_t b = 0; b < B; ++b) any_fail |= hinfo[b] != 0;
+    if (!any_fail) {
+      ok = true;
+      break;
+    }
+    if (attempt < 5) escalate_kernel<<<unsigned((B + 255) / 256), 256, 0, s>>>(B, st);
+  }
+  if (damp_used) GQ_CUDA_TRY(cudaMemcpyAsync(damp_used, st.cur_damp, size_t(B) * 4, cudaMemcpyDeviceToDevice, s));
+  GQ_CUDA_TRY(cudaMemcpyAsync(info, st.info, size_t(B) * 4, cudaMemcpyDeviceToDevice, s));
+  if (!ok) {
+    GQ_CUDA_TRY(cudaStreamSynchronize(s));
+    set_last_error("Hessian not positive definite after damping escalation");
+    return GQ_ERR_NOT_PD;
+  }
+  // L^-1 by doubling. At level sz every diagonal block of size sz starting at a
+  // multiple of sz is already inverted (in U); a pair [A 0; Bk D] gets the
+  // off-diagonal block -D^-1 * Bk * A^-1 of its inverse. X = Bk * A^-1 is kept
+  // transposed (sz x dsz) in the unused strict upper triangle of Hr (rows c0..,
+  // columns r0..), so a trailing partial pair (dsz < sz) stays inside the matrix.
+  init_linv_kernel<<<dim3(ew_blocks, unsigned(B)), 256, 0, s>>>(U, C, Dinv, st);
+  for (int64_t sz = NB; sz < C; sz *= 2) {
+    const int64_t full = C / (2 * sz);
+    const bool partial = (C % (2 * sz)) > sz;
+    for (int part = 0; part < 2; ++part) {
+      const int64_t npairs = part == 0 ? full : (partial ? 1 : 0);
+      if (npairs == 0) continue;
+      const int64_t c0 = part == 0 ? 0 : full * 2 * sz, r0 = c0 + sz;
+      const int64_t dsz = part == 0 ? sz : C - r0;
+      const int64_t pstride = 2 * sz * (C + 1);  // next pair down the diagonal
+      GemmBatch g1{};  // Xt(r, c) = sum_t Ainv[t][r] * Bk[c][t]   (Xt = (Bk Ainv)^T)
+      g1.A = U + c0 * C + c0;
+      g1.lda = C;
+      g1.Bm = Hr + r0 * C + c0;
+      g1.ldb = C;
+      g1.Cm = Hr + c0 * C + r0;
+      g1.ldc = C;
+      g1.sa_o = g1.sb_o = g1.sc_o = C * C;
+      g1.sa_i = g1.sb_i = g1.sc_i = pstride;
+      g1.n_inner = int(npairs);
+      g1.M = int(sz);
+      g1.N = int(dsz);
+      g1.K = int(sz);
+      g1.alpha = 1.0f;
+      g1.beta = 0.0f;
+      g1.skip = st.info;
+      int r = launch_gemm(g1, true, true, B * npairs, s);
+      if (r != GQ_OK) return r;
+      GemmBatch g2 = g1;  // Linv(r0.., c0..) = -Dinv * X, X(t, c) = Xt[c][t]
+      g2.A = U + r0 * C + r0;
+      g2.Bm = Hr + c0 * C + r0;
+      g2.Cm = U + r0 * C + c0;
+      g2.M = int(dsz);
+      g2.N = int(sz);
+      g2.K = int(dsz);
+      g2.alpha = -1.0f;
+      r = launch_gemm(g2, false, true, B * npairs, s);
+      if (r != GQ_OK) return r;
+    }
+  }
+  rotate_kernel<<<dim3(ew_blocks, unsigned(B)), 256, 0, s>>>(U, C, st);
+  return check_launch("prepare_hinv tail");
+}
+
+extern "C" size_t gq_gptq_affine_workspace_size(int64_t B, int64_t R, int64_t C, int group_size, int block_size) {
+  if (B <= 0 || R <= 0 || C <= 0 || group_size <= 0) return 0;
+  int64_t bs = std::max<int64_t>(block_size, group_size);
+  bs -= bs % group_size;
+  return align256(size_t(B) * R * bs * 4) + align256(size_t(B) * 1024 * 2 * 4);
+}
+
+extern "C" int gq_gptq_affine(float* W, const void* W_orig, int w_dtype, const float* U, int64_t B, int64_t R,
+                              int64_t C, int bits, int group_size, int block_size, int clip, int storage_dtype,
+                              uint8_t* q, void* scales, void* biases, float* rel_err, void* workspace,
+                              size_t workspace_bytes, void* stream) {
+  GQ_REQUIRE(W && U && q && scales && biases, "gq_gptq_affine: null pointer");
+  GQ_REQUIRE(bits >= 1 && bits <= 8, "gq_gptq_affine: bits %d", bits);
+  GQ_REQUIRE(group_size == 32 || group_size == 64 || group_size == 128 || group_size == 256,
+             "gq_gptq_affine: group size %d unsupported (32/64/128/256)", group_size);
+  GQ_REQUIRE(C % group_size == 0, "in_features %lld not divisible by group %d", (long long)C, group_size);
+  GQ_REQUIRE(clip == GQ_CLIP_MSE || clip == GQ_CLIP_MINMAX, "gq_gptq_affine: clip");
+  GQ_REQUIRE(storage_dtype == GQ_F32 || storage_dtype == GQ_BF16 || storage_dtype == GQ_F16, "storage dtype");
+  GQ_REQUIRE(B > 0 && R >= 0 && B < 65536, "gq_gptq_affine: sizes");
+  GQ_REQUIRE(!rel_err || (W_orig && (w_dtype == GQ_F32 || w_dtype == GQ_BF16 || w_dtype == GQ_F16)),
+             "gq_gptq_affine: rel_err needs W_orig");
+  int64_t bs = std::max<int64_t>(block_size, group_size);
+  bs -= bs % group_size;
+  GQ_REQUIRE(bs == 128 || bs == 256, "gq_gptq_affine: block of %lld columns unsupported (128/256)", (long long)bs);
+  const size_t need = gq_gptq_affine_workspace_size(B, R, C, group_size, block_size);
+  GQ_REQUIRE(workspace && workspace_bytes >= need, "gq_gptq_affine: workspace too small (%zu < %zu)",
+             workspace_bytes, need);
+  if (R == 0 || C == 0) return GQ_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  float* Err = reinterpret_cast<float*>(workspace);
+  float* partials = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + align256(size_t(B) * R * bs * 4));
+  const int nshrink = clip == GQ_CLIP_MSE ? kMaxShrinks : 1;
+  const dim3 cgrid(unsigned((R + 7) / 8), unsigned(B));
+  for (int64_t i1 = 0; i1 < C; i1 += bs) {
+    const int64_t n = std::min<int64_t>(bs, C - i1);
+    // C % G == 0 and bs % G == 0: a trailing partial block is a whole number of groups,
+    // and VPB must match it; only full blocks reach the templated kernel below.
+    GQ_REQUIRE(n == bs, "gq_gptq_affine: C=%lld must be a multiple of the block (%lld)", (long long)C,
+               (long long)bs);
+#define AB(VPL, VPB)                                                                                            \
+  affine_block_kernel<VPL, VPB><<<cgrid, 256, 0, s>>>(W, U, R, C, i1, bits, nshrink, storage_dtype, q, scales, \
+                                                      biases, Err)
+    if (bs == 128) {
+      switch (group_size) {
+        case 32: AB(1, 4); break;
+        case 64: AB(2, 4); break;
+        default: AB(4, 4); break;
+      }
+    } else {
+      AB(8, 8);
+    }
+#undef AB
+    int r = check_launch("affine_block_kernel");
+    if (r != GQ_OK) return r;
+    const int64_t i2 = i1 + n;
+    if (i2 < C) {
+      GemmBatch g{};
+      g.A = Err;
+      g.lda = bs;
+      g.sa_o = R * bs;
+      g.Bm = U + i1 * C + i2;
+      g.ldb = C;
+      g.sb_o = C * C;
+      g.Cm = W + i2;
+      g.ldc = C;
+      g.sc_o = R * C;
+      g.n_inner = 1;
+      g.M = int(R);
+      g.N = int(C - i2);
+      g.K = int(bs);
+      g.alpha = -1.0f;
+      g.beta = 1.0f;
+      r = launch_gemm(g, false, false, B, s);
+      if (r != GQ_OK) return r;
+    }
+  }
+  if (rel_err) {
+    const dim3 pg(1024, unsigned(B));
+    if (w_dtype == GQ_F32)
+      rel_partials_kernel<float><<<pg, 256, 0, s>>>(W, (const float*)W_orig, R * C, partials);
+    else if (w_dtype == GQ_BF16)
+      rel_partials_kernel<__nv_bfloat16><<<pg, 256, 0, s>>>(W, (const __nv_bfloat16*)W_orig, R * C, partials);
+    else
+      rel_partials_kernel<__half><<<pg, 256, 0, s>>>(W, (const __half*)W_orig, R * C, partials);
+    int r = check_launch("rel_partials_kernel");
+    if (r != GQ_OK) return r;
+    return launch_rel_err(partials, B, 1024, rel_err, s);
+  }
+  return GQ_OK;
+}

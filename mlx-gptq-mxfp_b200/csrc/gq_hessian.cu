@@ -1,0 +1,253 @@
+// Hessian accumulation H = beta*H + alpha * X^T X on the 5th-generation tensor
+// cores (replaces mlx_gptq/capture.py:68-76, Stash.hessian).
+//
+// X is bf16 [n tokens, c channels], row-major. Both GEMM operands are X itself:
+// A[m][k] = X[k][i0 + m] and B[j][k] = X[k][j0 + j], i.e. both "MN-major" (the
+// output index is the contiguous one), which tcgen05 consumes directly from
+// 128-byte-swizzled shared memory -- no transpose pass.
+//
+// One CTA per 128 x 256 output tile on or above the diagonal (H is symmetric;
+// the epilogue mirrors). Warp roles: warp 0 = TMA producer, warp 1 = TMEM owner
+// and MMA issuer, warps 2-5 = epilogue (TMEM lanes 32*(warp%4) .. +31).
+// Pipeline: 4 stages x (A 128x64 + B 256x64 bf16) = 192 KB of shared memory,
+// fp32 accumulators in 256 TMEM columns.
+#include <mutex>
+
+#include "gq_common.cuh"
+
+namespace gq {
+namespace hess {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4, THREADS = 192;
+constexpr uint32_t BOX_BYTES = 64 * 64 * 2;          // one 64-channel x 64-token TMA box
+constexpr uint32_t A_BYTES = BM * BK * 2;            // 16 KB
+constexpr uint32_t B_BYTES = BN * BK * 2;            // 32 KB
+constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;  // 48 KB
+constexpr uint32_t TMEM_COLS = 256;
+constexpr size_t SMEM_BYTES = size_t(STAGES) * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+
+// Tiles (tm, tn) with tm <= 2*tn + 1 touch the upper triangle; enumerate them
+// column-panel by column-panel (neighbouring CTAs share the B panel in L2).
+__host__ __device__ inline int64_t tiles_in_panel(int64_t tn, int64_t mt) { return 2 * tn + 2 < mt ? 2 * tn + 2 : mt; }
+
+__host__ inline int64_t num_tiles(int64_t c) {
+  const int64_t mt = (c + BM - 1) / BM, nt = (c + BN - 1) / BN;
+  int64_t t = 0;
+  for (int64_t tn = 0; tn < nt; ++tn) t += tiles_in_panel(tn, mt);
+  return t;
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    hessian_kernel(const __grid_constant__ CUtensorMap tmap, int64_t n, int64_t c, float* __restrict__ H,
+                   int64_t ldh, float alpha, float beta, int32_t* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accum = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t mt = (c + BM - 1) / BM;
+  int64_t t = blockIdx.x, tn = 0;
+  while (t >= tiles_in_panel(tn, mt)) {
+    t -= tiles_in_panel(tn, mt);
+    ++tn;
+  }
+  const int64_t tm = t;
+  const int KT = int((n + BK - 1) / BK);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap)) : "memory");
+      int issued = 0;
+      for (int kt = 0; kt < KT; ++kt) {
+        const int s = kt % STAGES;
+        const uint32_t ph = (kt / STAGES) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, status)) break;
+        mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+        uint8_t* st = smem + s * STAGE_BYTES;
+        const int y = kt * BK;
+        const int xa = int(tm * BM), xb = int(tn * BN);
+        tma_load_2d(st, &tmap, xa, y, &full[s]);
+        tma_load_2d(st + BOX_BYTES, &tmap, xa + 64, y, &full[s]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) tma_load_2d(st + A_BYTES + i * BOX_BYTES, &tmap, xb + 64 * i, y, &full[s]);
+        issued = kt + 1;
+      }
+      if (*abort_flag) {  // let copies already in flight land before the CTA exits
+        volatile int never = 0;
+        for (int kt = issued > STAGES ? issued - STAGES : 0; kt < issued; ++kt)
+          mbar_wait(&full[kt % STAGES], (kt / STAGES) & 1, &never, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(BM, BN, true, true);
+      for (int kt = 0; kt < KT; ++kt) {
+        const int s = kt % STAGES;
+        const uint32_t ph = (kt / STAGES) & 1;
+        if (!mbar_wait(&full[s], ph, abort_flag, status)) break;
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(smem + s * STAGE_BYTES), b0 = a0 + A_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          // K advances 16 rows of 128 B inside the swizzled boxes; LBO = next
+          // 64-channel box, SBO = next 8-row core-matrix group.
+          const uint64_t ad = umma_desc_sw128(a0 + kk * 2048, BOX_BYTES, 1024);
+          const uint64_t bd = umma_desc_sw128(b0 + kk * 2048, BOX_BYTES, 1024);
+          umma_f16(tmem, ad, bd, idesc, (kt | kk) != 0);
+        }
+        umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+      }
+      umma_commit(accum);
+    }
+  } else {
+    // epilogue: TMEM -> registers -> H (upper part) and its mirror
+    const bool ok = mbar_wait(accum, 0, abort_flag, status);
+    tc_fence_after();
+    if (ok && !*abort_flag && KT > 0) {
+      const int qw = warp & 3;
+      const int64_t gr = tm * BM + qw * 32 + lane;
+      const int64_t cb = tn * BN;
+      const bool all_upper = cb > tm * BM + BM - 1;
+#pragma unroll 1
+      for (int ch = 0; ch < BN / 32; ++ch) {
+        uint32_t acc[32];
+        tmem_ld32(tmem + (uint32_t(qw * 32) << 16) + uint32_t(ch * 32), acc);
+        tmem_ld_wait();
+        const int64_t c0 = cb + ch * 32;
+        if (c0 >= c) break;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = alpha * __uint_as_float(acc[j]);
+        // direct (upper) part: row gr, columns c0..c0+31 with column >= row
+        if (gr < c) {
+          float* hp = H + gr * ldh + c0;
+          if (all_upper && c0 + 32 <= c) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+              if (beta != 0.0f) {
+                const float4 h = *reinterpret_cast<const float4*>(hp + j);
+                o.x = beta * h.x + o.x, o.y = beta * h.y + o.y, o.z = beta * h.z + o.z, o.w = beta * h.w + o.w;
+              }
+              *reinterpret_cast<float4*>(hp + j) = o;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int64_t gc = c0 + j;
+              if (gc >= gr && gc < c) hp[j] = beta != 0.0f ? beta * hp[j] + v[j] : v[j];
+            }
+          }
+        }
+        // mirror (strictly lower) part: H[gc][gr] for gc > gr; lanes hold consecutive gr
+#pragma unroll 4
+        for (int j = 0; j < 32; ++j) {
+          const int64_t gc = c0 + j;
+          if (gc > gr && gc < c && gr < c) {
+            float* hp = H + gc * ldh + gr;
+            *hp = beta != 0.0f ? beta * *hp + v[j] : v[j];
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// H = beta * H for the empty-token case
+__global__ void scale_kernel(float* H, int64_t c, int64_t ldh, float beta) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= c * c) return;
+  float* p = H + (i / c) * ldh + (i % c);
+  *p = beta == 0.0f ? 0.0f : beta * *p;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map over X [rows, cols] (row stride ld elements), 64 x 64 boxes, 128B swizzle.
+int make_x_map(CUtensorMap* map, const void* X, int64_t rows, int64_t cols, int64_t ld) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) {
+    set_last_error("cuTensorMapEncodeTiled unavailable");
+    return GQ_ERR_CUDA;
+  }
+  cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(ld) * 2};
+  cuuint32_t box[2] = {64, 64};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(X), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_last_error("cuTensorMapEncodeTiled failed (%d)", int(r));
+    return GQ_ERR_CUDA;
+  }
+  return GQ_OK;
+}
+
+}  // namespace hess
+}  // namespace gq
+
+using namespace gq;
+
+extern "C" int gq_hessian_bf16(const void* X, int64_t n, int64_t c, int64_t ldx, float* H, int64_t ldh, float alpha,
+                               float beta, int32_t* status, void* stream) {
+  GQ_REQUIRE(H && (X || n == 0), "gq_hessian_bf16: null pointer");
+  GQ_REQUIRE(n >= 0 && c > 0 && n < (int64_t(1) << 31) && c < (int64_t(1) << 31), "gq_hessian_bf16: sizes");
+  GQ_REQUIRE(ldh >= c && ldh % 4 == 0 && aligned16(H), "gq_hessian_bf16: H must be 16-byte aligned, ldh %% 4 == 0");
+  cudaStream_t s = (cudaStream_t)stream;
+  if (n == 0) {
+    if (beta == 1.0f) return GQ_OK;
+    hess::scale_kernel<<<unsigned((c * c + 255) / 256), 256, 0, s>>>(H, c, ldh, beta);
+    return check_launch("hessian scale_kernel");
+  }
+  GQ_REQUIRE(ldx >= c && ldx % 8 == 0 && aligned16(X), "gq_hessian_bf16: X must be 16-byte aligned, ldx %% 8 == 0");
+  CUtensorMap map;
+  int st = hess::make_x_map(&map, X, n, c, ldx);
+  if (st != GQ_OK) return st;
+  GQ_CUDA_TRY(cudaFuncSetAttribute(hess::hessian_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   int(hess::SMEM_BYTES)));
+  const int64_t tiles = hess::num_tiles(c);
+  hess::hessian_kernel<<<unsigned(tiles), hess::THREADS, hess::SMEM_BYTES, s>>>(map, n, c, H, ldh, alpha, beta,
+                                                                                status);
+  return check_launch("hessian_kernel");
+}

@@ -1,0 +1,503 @@
+// MXFP GPTQ (mlx_gptq/gptq.py:69-180) and the solver pieces it shares with the
+// affine path: dead columns, weight preparation, block-diagonal 32x32 factors,
+// rel_err reduction.
+//
+// Layout: W / W_dq / q [B, R, C] row-major, H [B, C, C], U_g [B, C/32, 32, 32].
+// The column loop runs one thread per weight row and one CTA per
+// (32-column group, 128-row tile, batch item); the group's H_g and U_g sit in
+// shared memory and are read by all 128 threads as broadcasts.
+#include "gq_affine_grid.cuh"
+
+namespace gq {
+
+// --------------------------------------------------------------------------
+// dead columns / weight preparation
+// --------------------------------------------------------------------------
+__global__ void dead_columns_kernel(float* __restrict__ H, int64_t B, int64_t C, uint8_t* __restrict__ dead) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= B * C) return;
+  const int64_t b = i / C, j = i % C;
+  float* d = H + (b * C + j) * C + j;
+  const bool is_dead = *d <= 0.0f;
+  if (is_dead) *d = 1.0f;
+  dead[i] = is_dead ? 1 : 0;
+}
+
+template <typename Tin>
+__global__ void prepare_weights_kernel(const Tin* __restrict__ W, const uint8_t* __restrict__ dead, int64_t B,
+                                       int64_t R, int64_t C, float* __restrict__ out) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= B * R * C) return;
+  const int64_t c = i % C, b = i / (R * C);
+  float v = to_f32<Tin>(W[i]);
+  if (dead && dead[b * C + c]) v = 0.0f;
+  out[i] = v;
+}
+
+// --------------------------------------------------------------------------
+// 32x32 damped factor, one warp per diagonal block
+// --------------------------------------------------------------------------
+
+// In-place lower Cholesky of the 32x32 matrix in A (row stride 33), by one warp.
+// Returns false (uniformly) if a pivot is not > 0 (covers NaN), like potrf's info.
+__device__ __forceinline__ bool warp_chol32(float (*A)[33], int lane) {
+  for (int k = 0; k < 32; ++k) {
+    __syncwarp();
+    const float piv = A[k][k];
+    if (!(piv > 0.0f)) return false;
+    const float d = sqrtf(piv);
+    __syncwarp();
+    if (lane > k) A[lane][k] = A[lane][k] / d;
+    if (lane == k) A[k][k] = d;
+    __syncwarp();
+    if (lane > k) {
+      const float lik = A[lane][k];
+      for (int j = k + 1; j <= lane; ++j) A[lane][j] = A[lane][j] - lik * A[j][k];
+    }
+  }
+  __syncwarp();
+  return true;
+}
+
+// gptq.py:27-66 per 32x32 diagonal block (called per group by gptq.py:99-100).
+__global__ void __launch_bounds__(128) mx_hinv_kernel(const float* __restrict__ H, int64_t B, int64_t C, float damp,
+                                                      float* __restrict__ U, int32_t* __restrict__ info,
+                                                      float* __restrict__ damp_used) {
+  __shared__ float sA[4][32][33];
+  __shared__ float sM[4][32][33];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t G = C / 32;
+  const int64_t item = int64_t(blockIdx.x) * 4 + w;
+  if (item >= B * G) return;  // whole warp
+  const int64_t b = item / G, g = item % G;
+  const float* Hg = H + (b * C + g * 32) * C + g * 32;
+  float (*A)[33] = sA[w];
+  float (*M)[33] = sM[w];
+
+  // mean(diag).clamp(min=1e-8)
+  float dm = Hg[int64_t(lane) * C + lane];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) dm += __shfl_xor_sync(0xFFFFFFFFu, dm, o);
+  dm = fmaxf(dm / 32.0f, 1e-8f);
+
+  float cur = damp;
+  bool ok = false;
+  for (int attempt = 0; attempt < 6; ++attempt) {
+    const float lam = dm * cur;
+    for (int i = 0; i < 32; ++i) {
+      float v = Hg[int64_t(i) * C + lane];
+      if (i == lane) v = v + lam;
+      A[i][lane] = v;
+    }
+    ok = warp_chol32(A, lane);
+    if (ok) break;
+    cur = cur * 10.0f;
+  }
+  if (lane == 0) {
+    info[item] = ok ? 0 : 1;
+    if (damp_used) damp_used[item] = cur;
+  }
+  if (!ok) return;
+
+  // Linv = L^-1 (lower): lane j solves L x = e_j (column j).
+  for (int i = 0; i < 32; ++i) {
+    float x = 0.0f;
+    if (i == lane) {
+      x = 1.0f / A[i][i];
+    } else if (i > lane) {
+      float acc = 0.0f;
+      for (int k = 0; k < i; ++k)
+        if (k >= lane) acc = fmaf(A[i][k], M[k][lane], acc);
+      x = -acc / A[i][i];
+    }
+    M[i][lane] = x;
+    __syncwarp();
+  }
+  // Hinv = Linv^T Linv (cholesky_inverse), column `lane`
+  __syncwarp();
+  for (int i = 0; i < 32; ++i) {
+    float acc = 0.0f;
+    const int k0 = i > lane ? i : lane;
+    for (int k = k0; k < 32; ++k) acc = fmaf(M[k][i], M[k][lane], acc);
+    A[i][lane] = acc;
+  }
+  __syncwarp();
+  const bool ok2 = warp_chol32(A, lane);
+  if (!ok2) {
+    if (lane == 0) info[item] = 2;
+    return;
+  }
+  // U = Lh^T (upper)
+  float* Ug = U + item * 1024;
+  for (int i = 0; i < 32; ++i) Ug[i * 32 + lane] = lane >= i ? A[lane][i] : 0.0f;
+}
+
+// --------------------------------------------------------------------------
+// MXFP column loop
+// --------------------------------------------------------------------------
+
+// e^T H e for a 32-vector held in registers (the einsum of gptq.py:123-125, 168).
+// The row index i runs as a rolled loop (bounded register pressure); e_i comes
+// from this thread's column of the staging buffer Es, the 32-wide row dot uses
+// the registers. Four partial accumulators give the FMA pipe independent chains.
+__device__ __forceinline__ float quad32(const float (&e)[32], const float (*Hs)[32], float (*Es)[129], int tid) {
+#pragma unroll
+  for (int c = 0; c < 32; ++c) Es[c][tid] = e[c];
+  float obj = 0.0f;
+#pragma unroll 1
+  for (int i = 0; i < 32; ++i) {
+    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      const float4 h = *reinterpret_cast<const float4*>(&Hs[i][j]);
+      a0 = fmaf(h.x, e[j], a0);
+      a1 = fmaf(h.y, e[j + 1], a1);
+      a2 = fmaf(h.z, e[j + 2], a2);
+      a3 = fmaf(h.w, e[j + 3], a3);
+    }
+    obj = fmaf(Es[i][tid], (a0 + a1) + (a2 + a3), obj);
+  }
+  return obj;
+}
+
+template <typename T>
+__device__ __forceinline__ void load_row32(const T* __restrict__ p, float (&o)[32]);
+template <>
+__device__ __forceinline__ void load_row32<float>(const float* __restrict__ p, float (&o)[32]) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const float4 v = __ldg(reinterpret_cast<const float4*>(p) + k);
+    o[4 * k] = v.x, o[4 * k + 1] = v.y, o[4 * k + 2] = v.z, o[4 * k + 3] = v.w;
+  }
+}
+template <>
+__device__ __forceinline__ void load_row32<__nv_bfloat16>(const __nv_bfloat16* __restrict__ p, float (&o)[32]) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(p) + k);
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      o[8 * k + 2 * t] = __uint_as_float(u[t] << 16);
+      o[8 * k + 2 * t + 1] = __uint_as_float(u[t] & 0xFFFF0000u);
+    }
+  }
+}
+template <>
+__device__ __forceinline__ void load_row32<__half>(const __half* __restrict__ p, float (&o)[32]) {
+#pragma unroll
+  for (int k = 0; k < 32; ++k) o[k] = __half2float(p[k]);
+}
+
+template <typename T>
+__device__ __forceinline__ void store_row32(T* __restrict__ p, const float (&v)[32]);
+template <>
+__device__ __forceinline__ void store_row32<float>(float* __restrict__ p, const float (&v)[32]) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    reinterpret_cast<float4*>(p)[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+}
+template <>
+__device__ __forceinline__ void store_row32<__nv_bfloat16>(__nv_bfloat16* __restrict__ p, const float (&v)[32]) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    uint32_t u[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const __nv_bfloat162 h = __floats2bfloat162_rn(v[8 * k + 2 * t], v[8 * k + 2 * t + 1]);
+      u[t] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    reinterpret_cast<uint4*>(p)[k] = make_uint4(u[0], u[1], u[2], u[3]);
+  }
+}
+
+template <int MODE, bool SAFE, typename Tin, typename Tout>
+__global__ void __launch_bounds__(128) mx_gptq_kernel(const Tin* __restrict__ W, const float* __restrict__ H,
+                                                      const float* __restrict__ U, const uint8_t* __restrict__ dead,
+                                                      const int32_t* __restrict__ info, int64_t R, int64_t C,
+                                                      uint8_t* __restrict__ q, uint8_t* __restrict__ qp,
+                                                      uint8_t* __restrict__ scales, Tout* __restrict__ wdq,
+                                                      float* __restrict__ partials) {
+  __shared__ __align__(16) float Hs[32][32];
+  __shared__ __align__(16) float Us[32][32];
+  __shared__ float Es[32][129];  // per-thread staging of the error vector for quad32
+  __shared__ float red[2][4];
+  __shared__ uint32_t s_dmask;
+  const int64_t G = C / 32;
+  const int64_t g = blockIdx.x, tile = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x;
+  if (info && info[b * G + g] != 0) return;  // factorization failed: host raises
+  const float* Hg = H + (b * C + g * 32) * C + g * 32;
+  const float* Ug = U + (b * G + g) * 1024;
+  for (int i = tid; i < 1024; i += 128) {
+    Hs[i >> 5][i & 31] = Hg[int64_t(i >> 5) * C + (i & 31)];
+    Us[i >> 5][i & 31] = Ug[i];
+  }
+  if (tid < 32) {
+    const bool d = dead ? dead[b * C + g * 32 + tid] != 0 : false;
+    const uint32_t m = __ballot_sync(0xFFFFFFFFu, d);
+    if (tid == 0) s_dmask = m;
+  }
+  __syncthreads();
+  const uint32_t dmask = s_dmask;
+  const int64_t r = tile * 128 + tid;
+  float num = 0.0f, den = 0.0f;
+  if (r < R) {
+    const int64_t off = (b * R + r) * C + g * 32;
+    float o[32];
+    load_row32<Tin>(W + off, o);
+#pragma unroll
+    for (int c = 0; c < 32; ++c) {
+      den = fmaf(o[c], o[c], den);
+      if (dmask & (1u << c)) o[c] = 0.0f;  // gptq.py:219-221 (rel_err keeps the raw value)
+    }
+    constexpr float kFmax = MODE == GQ_MXFP4 ? 6.0f : 448.0f;
+    float amax = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 32; ++c) amax = fmaxf(amax, fabsf(o[c]));
+    const int e0 = mx_scale_exponent(amax, kFmax);
+
+    // scale choice: groupwise = RTN scale; safe-scale-search = min e^T H e over offsets
+    int best_e = e0;
+    float best_obj = 0.0f;
+    if (SAFE) {
+      // offsets (0, -1, -2, -3, -4, +1, +2) for mxfp4, (0, -1, +1) for mxfp8 (gptq.py:92)
+      constexpr int kNoff = MODE == GQ_MXFP4 ? 7 : 3;
+#pragma unroll 1
+      for (int t = 0; t < kNoff; ++t) {
+        const int d = MODE == GQ_MXFP4 ? (t <= 4 ? -t : t - 4) : (t == 0 ? 0 : (t == 1 ? -1 : 1));
+        int e = e0 + d;
+        e = e < -127 ? -127 : (e > 127 ? 127 : e);
+        const float sc = exp2i(e), inv = exp2i(-e);
+        float err[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          uint32_t code;
+          err[c] = mx_quant<MODE>(o[c], inv, sc, code) - o[c];
+        }
+        const float obj = quad32(err, Hs, Es, tid);
+        if (t == 0 || obj < best_obj) {
+          best_obj = obj;
+          best_e = e;
+        }
+      }
+    }
+    const float sc = exp2i(best_e), inv = exp2i(-best_e);
+
+    // sequential GPTQ over the 32 columns with the fixed scale. After column c
+    // is quantized, wv[c] is reused to hold its error gdq[c] - o[c]; dq itself
+    // is re-derived from the code (value(code) * scale is exact and repeatable).
+    float wv[32];
+#pragma unroll
+    for (int c = 0; c < 32; ++c) wv[c] = o[c];
+    uint32_t gcode[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // 4 codes per word (byte lanes)
+#pragma unroll
+    for (int c = 0; c < 32; ++c) {
+      uint32_t code;
+      const float dq = mx_quant<MODE>(wv[c], inv, sc, code);
+      gcode[c >> 2] |= code << (8 * (c & 3));
+      const float err = (wv[c] - dq) / Us[c][c];
+#pragma unroll
+      for (int k = c + 1; k < 32; ++k) wv[k] = wv[k] - err * Us[c][k];
+      wv[c] = dq - o[c];
+    }
+    bool use_gptq = true;
+    if (SAFE) use_gptq = quad32(wv, Hs, Es, tid) <= best_obj;
+    // range guard: |dq| <= max(32 * max|w|, 2^-126), else the RTN baseline
+    const float limit = fmaxf(amax * 32.0f, 1.1754943508222875e-38f);
+    if (use_gptq) {
+      bool valid = true;
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        const uint32_t code = (gcode[c >> 2] >> (8 * (c & 3))) & 0xFFu;
+        valid = valid && (fabsf(mx_value<MODE>(code) * sc) <= limit);
+      }
+      use_gptq = valid;
+    }
+    if (!use_gptq) {  // baseline: RTN with the chosen scale
+#pragma unroll
+      for (int c = 0; c < 8; ++c) gcode[c] = 0;
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        uint32_t code;
+        mx_quant<MODE>(o[c], inv, sc, code);
+        gcode[c >> 2] |= code << (8 * (c & 3));
+      }
+    }
+    float gdq[32];
+#pragma unroll
+    for (int c = 0; c < 32; ++c) gdq[c] = mx_value<MODE>((gcode[c >> 2] >> (8 * (c & 3))) & 0xFFu) * sc;
+    // outputs
+    if (q) {
+      uint4* qd = reinterpret_cast<uint4*>(q + off);
+      qd[0] = make_uint4(gcode[0], gcode[1], gcode[2], gcode[3]);
+      qd[1] = make_uint4(gcode[4], gcode[5], gcode[6], gcode[7]);
+    }
+    if (MODE == GQ_MXFP4 && qp) {
+      uint32_t pk[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        // bytes (c0 | c1<<4), (c2 | c3<<4) from words 2t, 2t+1
+        const uint32_t a = gcode[2 * t], bb = gcode[2 * t + 1];
+        pk[t] = ((a & 0xFu) | ((a >> 4) & 0xF0u)) | (((a >> 16) & 0xFu) << 8) | (((a >> 20) & 0xF0u) << 8) |
+                (((bb & 0xFu) | ((bb >> 4) & 0xF0u)) << 16) | (((bb >> 16) & 0xFu) << 24) |
+                (((bb >> 20) & 0xF0u) << 24);
+      }
+      *reinterpret_cast<uint4*>(qp + off / 2) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    }
+    scales[(b * R + r) * G + g] = uint8_t(best_e + 127);
+    if (wdq) store_row32<Tout>(wdq + off, gdq);
+    if (partials) {
+      if (dmask) {  // dead columns: compare against the raw weights
+#pragma unroll
+        for (int c = 0; c < 32; ++c)
+          if (dmask & (1u << c)) o[c] = to_f32<Tin>(W[off + c]);
+      }
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        const float d = gdq[c] - o[c];
+        num = fmaf(d, d, num);
+      }
+    }
+  }
+  if (partials) {
+    num = warp_sum(num);
+    den = warp_sum(den);
+    if ((tid & 31) == 0) {
+      red[0][tid >> 5] = num;
+      red[1][tid >> 5] = den;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      float* p = partials + ((b * gridDim.y + tile) * G + g) * 2;
+      p[0] = (red[0][0] + red[0][1]) + (red[0][2] + red[0][3]);
+      p[1] = (red[1][0] + red[1][1]) + (red[1][2] + red[1][3]);
+    }
+  }
+}
+
+// rel_err[b] = sqrt(sum num) / max(sqrt(sum den), 1e-12), fixed-order reduction.
+__global__ void rel_err_kernel(const float* __restrict__ partials, int64_t per_b, float* __restrict__ rel) {
+  const int64_t b = blockIdx.x;
+  double n = 0.0, d = 0.0;
+  for (int64_t i = threadIdx.x; i < per_b; i += blockDim.x) {
+    n += partials[(b * per_b + i) * 2];
+    d += partials[(b * per_b + i) * 2 + 1];
+  }
+  __shared__ double sn[256], sd[256];
+  sn[threadIdx.x] = n;
+  sd[threadIdx.x] = d;
+  __syncthreads();
+  for (int s = blockDim.x / 2; s > 0; s >>= 1) {
+    if (threadIdx.x < s) {
+      sn[threadIdx.x] += sn[threadIdx.x + s];
+      sd[threadIdx.x] += sd[threadIdx.x + s];
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) rel[b] = float(sqrt(sn[0]) / fmax(sqrt(sd[0]), 1e-12));
+}
+
+static bool valid_in(int d) { return d == GQ_F32 || d == GQ_BF16 || d == GQ_F16; }
+
+int launch_rel_err(const float* partials, int64_t B, int64_t per_b, float* rel, cudaStream_t s) {
+  rel_err_kernel<<<unsigned(B), 256, 0, s>>>(partials, per_b, rel);
+  return check_launch("rel_err_kernel");
+}
+
+}  // namespace gq
+
+using namespace gq;
+
+extern "C" int gq_dead_columns(float* H, int64_t B, int64_t C, uint8_t* dead, void* stream) {
+  GQ_REQUIRE(H && dead, "gq_dead_columns: null pointer");
+  GQ_REQUIRE(B >= 0 && C >= 0, "gq_dead_columns: negative size");
+  if (B * C == 0) return GQ_OK;
+  dead_columns_kernel<<<unsigned((B * C + 255) / 256), 256, 0, (cudaStream_t)stream>>>(H, B, C, dead);
+  return check_launch("dead_columns_kernel");
+}
+
+extern "C" int gq_prepare_weights(const void* W_in, int w_dtype, const uint8_t* dead, int64_t B, int64_t R, int64_t C,
+                                  float* W_out, void* stream) {
+  GQ_REQUIRE(W_in && W_out && valid_in(w_dtype), "gq_prepare_weights: bad argument");
+  const int64_t n = B * R * C;
+  if (n == 0) return GQ_OK;
+  const unsigned grid = unsigned((n + 255) / 256);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (w_dtype == GQ_F32)
+    prepare_weights_kernel<float><<<grid, 256, 0, s>>>((const float*)W_in, dead, B, R, C, W_out);
+  else if (w_dtype == GQ_BF16)
+    prepare_weights_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)W_in, dead, B, R, C, W_out);
+  else
+    prepare_weights_kernel<__half><<<grid, 256, 0, s>>>((const __half*)W_in, dead, B, R, C, W_out);
+  return check_launch("prepare_weights_kernel");
+}
+
+extern "C" int gq_mx_prepare_hinv(const float* H, int64_t B, int64_t C, float damp, float* U, int32_t* info,
+                                  float* damp_used, void* stream) {
+  GQ_REQUIRE(H && U && info, "gq_mx_prepare_hinv: null pointer");
+  GQ_REQUIRE(B >= 0 && C >= 0 && C % 32 == 0, "gq_mx_prepare_hinv: C=%lld not a multiple of 32", (long long)C);
+  const int64_t items = B * (C / 32);
+  if (items == 0) return GQ_OK;
+  mx_hinv_kernel<<<unsigned((items + 3) / 4), 128, 0, (cudaStream_t)stream>>>(H, B, C, damp, U, info, damp_used);
+  return check_launch("mx_hinv_kernel");
+}
+
+extern "C" size_t gq_gptq_mxfp_workspace_size(int64_t B, int64_t R, int64_t C) {
+  if (B <= 0 || R <= 0 || C <= 0) return 0;
+  return size_t(B) * size_t((R + 127) / 128) * size_t(C / 32) * 2 * sizeof(float);
+}
+
+extern "C" int gq_gptq_mxfp(const void* W, int w_dtype, const float* H, const float* U, const uint8_t* dead,
+                            const int32_t* info, int64_t B, int64_t R, int64_t C, int mode, int algorithm, uint8_t* q,
+                            uint8_t* q_packed, uint8_t* scales, void* w_dq, int wdq_dtype, float* rel_err,
+                            void* workspace, size_t workspace_bytes, void* stream) {
+  GQ_REQUIRE(mode == GQ_MXFP4 || mode == GQ_MXFP8, "gq_gptq_mxfp: not a microscaling mode: %d", mode);
+  GQ_REQUIRE(algorithm == GQ_MX_GROUPWISE || algorithm == GQ_MX_SAFE_SCALE_SEARCH,
+             "unsupported MXFP GPTQ algorithm: %d", algorithm);
+  GQ_REQUIRE(W && H && U && scales, "gq_gptq_mxfp: null pointer");
+  GQ_REQUIRE(w_dtype == GQ_F32 || w_dtype == GQ_BF16 || w_dtype == GQ_F16, "gq_gptq_mxfp: w_dtype");
+  GQ_REQUIRE(!w_dq || wdq_dtype == GQ_F32 || wdq_dtype == GQ_BF16, "gq_gptq_mxfp: wdq_dtype");
+  GQ_REQUIRE(B >= 0 && R >= 0 && C >= 0 && C % 32 == 0, "gq_gptq_mxfp: C=%lld not a multiple of 32", (long long)C);
+  GQ_REQUIRE(aligned16(W) && (!q || aligned16(q)) && (!q_packed || aligned16(q_packed)) && (!w_dq || aligned16(w_dq)),
+             "gq_gptq_mxfp: W, q, q_packed and w_dq must be 16-byte aligned");
+  GQ_REQUIRE(R / 128 < 65535 && B < 65536 && C / 32 < (int64_t(1) << 31), "gq_gptq_mxfp: shape too large");
+  const size_t need = gq_gptq_mxfp_workspace_size(B, R, C);
+  GQ_REQUIRE(!rel_err || (workspace && workspace_bytes >= need), "gq_gptq_mxfp: workspace too small (%zu < %zu)",
+             workspace_bytes, need);
+  if (B * R * C == 0) return GQ_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  float* partials = rel_err ? reinterpret_cast<float*>(workspace) : nullptr;
+  const dim3 grid(unsigned(C / 32), unsigned((R + 127) / 128), unsigned(B));
+  const bool safe = algorithm == GQ_MX_SAFE_SCALE_SEARCH;
+#define MXL(MODE, SAFE, TIN, TOUT)                                                                              \
+  mx_gptq_kernel<MODE, SAFE, TIN, TOUT><<<grid, 128, 0, s>>>((const TIN*)W, H, U, dead, info, R, C, q, q_packed, \
+                                                             scales, (TOUT*)w_dq, partials)
+#define MXL_OUT(MODE, SAFE, TIN)                  \
+  do {                                            \
+    if (wdq_dtype == GQ_BF16)                     \
+      MXL(MODE, SAFE, TIN, __nv_bfloat16);        \
+    else                                          \
+      MXL(MODE, SAFE, TIN, float);                \
+  } while (0)
+#define MXL_IN(MODE, SAFE)                     \
+  do {                                         \
+    if (w_dtype == GQ_F32)                     \
+      MXL_OUT(MODE, SAFE, float);              \
+    else if (w_dtype == GQ_BF16)               \
+      MXL_OUT(MODE, SAFE, __nv_bfloat16);      \
+    else                                       \
+      MXL_OUT(MODE, SAFE, __half);             \
+  } while (0)
+  if (mode == GQ_MXFP4) {
+    if (safe) MXL_IN(GQ_MXFP4, true); else MXL_IN(GQ_MXFP4, false);
+  } else {
+    if (safe) MXL_IN(GQ_MXFP8, true); else MXL_IN(GQ_MXFP8, false);
+  }
+#undef MXL_IN
+#undef MXL_OUT
+#undef MXL
+  int st = check_launch("mx_gptq_kernel");
+  if (st != GQ_OK || !rel_err) return st;
+  return launch_rel_err(partials, B, ((R + 127) / 128) * (C / 32), rel_err, s);
+}

@@ -1,0 +1,84 @@
+"""tcgen05 Hessian kernel vs the reference (golden) and a float64 torch reference.
+
+Tolerance (north star): relative Frobenius error <= 1e-5.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+HESSIAN_RTOL = 1e-5
+
+
+def _rel(a, b):
+    return float((a.double() - b.double()).norm() / b.double().norm())
+
+
+def test_hessian_matches_reference_golden(golden):
+    from mlx_gptq_b200 import Stash
+
+    g = golden("hessian")
+    X = torch.from_numpy(g["X_bits"].view(np.int16).copy()).view(torch.bfloat16)
+    st = Stash("x", 96)
+    st.add(X[:1000])
+    st.add(X[1000:])
+    H = st.hessian("cuda", chunk_rows=512)
+    assert _rel(H.cpu(), torch.from_numpy(g["H"])) < HESSIAN_RTOL
+    assert torch.equal(H, H.T)
+
+
+@pytest.mark.parametrize("n,c", [(1000, 96), (4096, 256), (20000, 768), (65536, 1024), (3, 64), (777, 200)])
+def test_hessian_vs_float64(n, c):
+    from mlx_gptq_b200 import hessian_from_rows
+
+    torch.manual_seed(n + c)
+    X = torch.randn(n, c, device="cuda")
+    X[:, : max(1, c // 64)] *= 20.0  # outlier channels
+    X = X.to(torch.bfloat16)
+    H = hessian_from_rows(X)
+    ref = X.double().T @ X.double()
+    assert _rel(H, ref) < HESSIAN_RTOL
+    assert torch.equal(H, H.T)
+
+
+def test_hessian_accumulate_alpha_beta():
+    from mlx_gptq_b200 import hessian_accumulate
+
+    torch.manual_seed(3)
+    X1 = torch.randn(3000, 256, device="cuda").to(torch.bfloat16)
+    X2 = torch.randn(5000, 256, device="cuda").to(torch.bfloat16)
+    H = torch.full((256, 256), 7.0, device="cuda")
+    hessian_accumulate(X1, H, 1.0, 0.0)
+    hessian_accumulate(X2, H, 0.5, 1.0)
+    ref = X1.double().T @ X1.double() + 0.5 * (X2.double().T @ X2.double())
+    assert _rel(H, ref) < HESSIAN_RTOL
+
+
+def test_hessian_strided_rows_and_zero_tokens():
+    from mlx_gptq_b200 import hessian_accumulate
+
+    torch.manual_seed(4)
+    big = torch.randn(2048, 384, device="cuda").to(torch.bfloat16)
+    X = big[:, :256]  # row stride 384
+    H = torch.empty(256, 256, device="cuda")
+    hessian_accumulate(X, H, 1.0, 0.0)
+    assert _rel(H, X.double().T @ X.double()) < HESSIAN_RTOL
+    H2 = H.clone()
+    hessian_accumulate(X[:0], H2, 1.0, 1.0)  # no tokens: unchanged
+    assert torch.equal(H2, H)
+    hessian_accumulate(X[:0], H2, 1.0, 0.0)  # no tokens, overwrite: zeros
+    assert int(torch.count_nonzero(H2)) == 0
+
+
+def test_hessian_full_size_property():
+    """At the bench's size (K = 4096), H is symmetric, PSD-diagonal and close to fp64."""
+    from mlx_gptq_b200 import hessian_from_rows
+
+    torch.manual_seed(5)
+    X = (torch.randn(131072, 4096, device="cuda")).to(torch.bfloat16)
+    H = hessian_from_rows(X)
+    ref = X[:, :512].double().T @ X.double()
+    assert _rel(H[:512], ref) < HESSIAN_RTOL
+    assert torch.equal(H, H.T)

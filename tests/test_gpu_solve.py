@@ -1,0 +1,237 @@
+"""GPU GPTQ solver vs the reference (golden vectors) and the oracle.
+
+Tolerances (north star): codes agree on >= 99.9% of elements; proxy loss
+tr((W-Q) H (W-Q)^T) within 0.5% of the reference; rel_err within 1e-3
+relative. Batch independence and the MXFP dequant identity are bit-exact, as
+the reference's own tests require (tests/test_gptq.py:44-52, :81-90).
+"""
+
+import zlib
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import gptq as ogptq
+from oracle import grid as ogrid
+
+pytestmark = pytest.mark.gpu
+
+CODE_AGREEMENT = 0.999
+PROXY_RTOL = 0.005
+STORAGE = {"bfloat16": torch.bfloat16, "float16": torch.float16, "float32": torch.float32}
+
+SOLVE_CASES = {
+    "affine4_g64": dict(bits=4, group_size=64, mode="affine"),
+    "affine2_g32": dict(bits=2, group_size=32, mode="affine"),
+    "affine8_g128": dict(bits=8, group_size=128, mode="affine"),
+    "affine4_g64_minmax_f16": dict(bits=4, group_size=64, mode="affine", clip="minmax",
+                                   storage_dtype=torch.float16),
+    "mxfp4_safe": dict(bits=4, group_size=32, mode="mxfp4"),
+    "mxfp4_groupwise": dict(bits=4, group_size=32, mode="mxfp4", mxfp_algorithm="groupwise"),
+    "mxfp8_groupwise": dict(bits=8, group_size=32, mode="mxfp8"),
+    "mxfp8_safe": dict(bits=8, group_size=32, mode="mxfp8", mxfp_algorithm="safe-scale-search"),
+    "mxfp4_bad": dict(bits=4, group_size=32, mode="mxfp4", mxfp_algorithm="safe-scale-search"),
+}
+
+
+def _cuda(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def _check_solution(W, H0, q, Wdq, rel, ref_q, ref_Wdq, ref_rel):
+    agree = (q == ref_q).mean()
+    assert agree >= CODE_AGREEMENT, agree
+    ours = ogptq.proxy_loss(W, Wdq, H0)
+    ref = ogptq.proxy_loss(W, ref_Wdq, H0)
+    np.testing.assert_allclose(ours, ref, rtol=PROXY_RTOL)
+    np.testing.assert_allclose(rel, ref_rel, rtol=1e-3)
+
+
+@pytest.mark.parametrize("name", sorted(SOLVE_CASES))
+def test_solve_gptq_vs_reference_golden(golden, name):
+    from mlx_gptq_b200 import solve_gptq
+
+    g = golden("solve")
+    W = g[f"{name}/W"]
+    H = _cuda(g[f"{name}/H"])
+    q, s, b, Wdq, rel = solve_gptq(_cuda(W), H, **SOLVE_CASES[name])
+    np.testing.assert_array_equal(H.cpu().numpy(), g[f"{name}/H_after"])  # dead-column mutation
+    _check_solution(W, g[f"{name}/H_after"], q.cpu().numpy(), Wdq.cpu().numpy(), rel.cpu().numpy(),
+                    g[f"{name}/q"], g[f"{name}/Wdq"], g[f"{name}/rel"])
+    if SOLVE_CASES[name]["mode"] == "affine":
+        assert s.dtype == SOLVE_CASES[name].get("storage_dtype", torch.bfloat16)
+    else:
+        assert b is None and s.dtype == torch.uint8
+        np.testing.assert_array_equal(s.cpu().numpy(), g[f"{name}/s"])
+
+
+def _correlated(B, R, C, N, seed):
+    rng = np.random.default_rng(seed)
+    base = rng.standard_normal((N, C)).astype(np.float32)
+    X = base + 0.5 * np.roll(base, 1, axis=1)
+    X[:, 3] *= 20.0
+    H = np.repeat((X.T @ X)[None], B, axis=0).astype(np.float32)
+    H[1:] *= 2.0
+    W = (rng.standard_normal((B, R, C)) * 0.02).astype(np.float32)
+    return W, H
+
+
+@pytest.mark.parametrize("mode,algo,bits,gs", [
+    ("mxfp4", "safe-scale-search", 4, 32), ("mxfp4", "groupwise", 4, 32),
+    ("mxfp8", "groupwise", 8, 32), ("affine", "auto", 4, 64), ("affine", "auto", 4, 128)])
+def test_solve_vs_oracle_random(mode, algo, bits, gs):
+    from mlx_gptq_b200 import solve_gptq
+
+    W, H = _correlated(3, 200, 512, 2048, seed=zlib.crc32(f"{mode}{algo}{gs}".encode()) % 1000)
+    oq, os_, ob, oWdq, orel = ogptq.solve_gptq(W, H.copy(), bits, gs, mode=mode, mxfp_algorithm=algo)
+    q, s, b, Wdq, rel = solve_gptq(_cuda(W), _cuda(H), bits, gs, mode=mode, mxfp_algorithm=algo)
+    _check_solution(W, H, q.cpu().numpy(), Wdq.cpu().numpy(), rel.cpu().numpy(), oq, oWdq, orel)
+
+
+@pytest.mark.parametrize("mode", ["affine", "mxfp4", "mxfp8"])
+def test_batch_independent_bit_exact(mode):
+    """tests/test_gptq.py:44-52: batched solve == per-item solves, bit-exact."""
+    from mlx_gptq_b200 import solve_gptq
+
+    W, H = _correlated(3, 64, 256, 1024, seed=7)
+    gs = 64 if mode == "affine" else 32
+    bits = 8 if mode == "mxfp8" else 4
+    qb, sb, _, _, _ = solve_gptq(_cuda(W), _cuda(H), bits, gs, mode=mode)
+    for i in range(3):
+        qi, si, _, _, _ = solve_gptq(_cuda(W[i:i + 1]), _cuda(H[i:i + 1]), bits, gs, mode=mode)
+        assert torch.equal(qb[i], qi[0])
+        assert torch.equal(sb[i], si[0])
+
+
+@pytest.mark.parametrize("mode", ["mxfp4", "mxfp8"])
+def test_mxfp_dequant_consistency(mode):
+    """tests/test_gptq.py:81-90: W_dq == dequantize_artifact(q, scales) exactly."""
+    from mlx_gptq_b200 import solve_gptq
+    from mlx_gptq_b200.grid import dequantize_artifact
+
+    W, H = _correlated(1, 8, 64, 512, seed=11)
+    q, s, b, Wdq, rel = solve_gptq(_cuda(W), _cuda(H), 4 if mode == "mxfp4" else 8, 32, mode=mode)
+    assert b is None and s.dtype == torch.uint8
+    assert torch.equal(dequantize_artifact(q, s, b, mode, 32), Wdq)
+    assert torch.isfinite(Wdq).all() and (rel > 0).all()
+
+
+def test_affine_dequant_consistency():
+    """tests/test_gptq.py:29-41 with float32 storage."""
+    from mlx_gptq_b200 import solve_gptq
+
+    W, H = _correlated(1, 8, 128, 512, seed=12)
+    q, s, b, Wdq, _ = solve_gptq(_cuda(W), _cuda(H), 4, 32, storage_dtype=torch.float32)
+    manual = (q.float().reshape(1, 8, -1, 32) * s.unsqueeze(-1) + b.unsqueeze(-1)).reshape(1, 8, 128)
+    assert torch.allclose(manual, Wdq, atol=1e-5)
+    assert int(q.max()) <= 15
+
+
+def test_gptq_beats_rtn():
+    """tests/test_gptq.py:19-26 and :93-101: output error below RTN."""
+    from mlx_gptq_b200 import solve_gptq
+    from mlx_gptq_b200.grid import rtn_quantize, rtn_quantize_mxfp
+
+    rng = np.random.default_rng(0)
+    base = rng.standard_normal((1024, 128)).astype(np.float32)
+    X = _cuda(base + 0.5 * np.roll(base, 1, axis=1))
+    W = torch.randn(2, 32, 128, device="cuda")
+    H = (X.T @ X).unsqueeze(0).expand(2, 128, 128).contiguous()
+    for mode, bits, gs in (("affine", 4, 32), ("mxfp4", 4, 32), ("mxfp8", 8, 32)):
+        _, _, _, Wq, rel = solve_gptq(W, H.clone(), bits, gs, mode=mode)
+        if mode == "affine":
+            Wr = rtn_quantize(W, bits, gs)[3]
+        else:
+            Wr = rtn_quantize_mxfp(W, mode)[3]
+        eg = ((X @ (Wq - W).transpose(1, 2)) ** 2).mean()
+        er = ((X @ (Wr - W).transpose(1, 2)) ** 2).mean()
+        assert eg < er * (0.9 if mode == "affine" else 1.0), (mode, eg, er)
+
+
+def test_zero_hessian_stays_finite(golden):
+    from mlx_gptq_b200 import solve_gptq
+
+    g = golden("solve")
+    q, s, b, Wdq, rel = solve_gptq(_cuda(g["affine_zeroH/W"]), _cuda(g["affine_zeroH/H"]), 4, 32)
+    assert torch.isfinite(Wdq).all()
+    np.testing.assert_array_equal(q.cpu().numpy(), g["affine_zeroH/q"])
+    np.testing.assert_array_equal(Wdq.cpu().numpy(), g["affine_zeroH/Wdq"])
+
+
+def test_gptq_quantize_in_place():
+    from mlx_gptq_b200 import gptq_quantize, solve_gptq
+
+    W, H = _correlated(2, 16, 128, 512, seed=13)
+    for mode in ("affine", "mxfp4"):
+        Wt = _cuda(W)
+        q, s, b, Wdq, rel = gptq_quantize(Wt, _cuda(H), 4, 32, mode=mode)
+        assert rel is None and Wdq.data_ptr() == Wt.data_ptr()
+        q2, _, _, Wdq2, _ = solve_gptq(_cuda(W), _cuda(H), 4, 32, mode=mode)
+        assert torch.equal(q, q2) and torch.equal(Wdq, Wdq2)
+
+
+def test_not_positive_definite_raises():
+    from mlx_gptq_b200 import solve_gptq
+
+    # strongly indefinite, tiny diagonal: even 1e5 x damping (1e-3 * 0.01 * 1e5 = 1) cannot fix it
+    H = torch.full((1, 64, 64), -10.0, device="cuda")
+    H[0].fill_diagonal_(1e-3)
+    with pytest.raises(RuntimeError, match="not positive definite"):
+        solve_gptq(torch.randn(1, 8, 64, device="cuda"), H, 4, 64)
+
+
+def test_bad_arguments():
+    from mlx_gptq_b200 import solve_gptq
+
+    W = torch.randn(1, 8, 64, device="cuda")
+    H = torch.eye(64, device="cuda").unsqueeze(0)
+    with pytest.raises(ValueError):
+        solve_gptq(W, H, 4, 64, mode="mxfp4")
+    with pytest.raises(ValueError):
+        solve_gptq(W, H, 4, 32, mode="mxfp4", mxfp_algorithm="bogus")
+    with pytest.raises(AssertionError):
+        solve_gptq(W, torch.eye(32, device="cuda").unsqueeze(0), 4, 32)
+
+
+def test_prepare_hinv_vs_reference_golden(golden):
+    from mlx_gptq_b200.gptq import _prepare_hinv
+
+    g = golden("hinv")
+    U = _prepare_hinv(_cuda(g["H"]), 0.01).cpu().numpy()
+    ref = g["U"]
+    rel = np.linalg.norm(U - ref, axis=(1, 2)) / np.linalg.norm(ref, axis=(1, 2))
+    assert (rel < 1e-4).all(), rel
+    assert np.allclose(np.tril(U, -1), 0.0)
+
+
+@pytest.mark.parametrize("C", [128, 192, 320, 448, 1024])
+def test_prepare_hinv_vs_oracle_sizes(C):
+    from mlx_gptq_b200.gptq import _prepare_hinv
+
+    _, H = _correlated(2, 4, C, 4 * C, seed=C)
+    U = _prepare_hinv(_cuda(H), 0.01).cpu().numpy()
+    Uo, _ = ogptq.prepare_hinv(H.copy(), 0.01)
+    rel = np.linalg.norm(U - Uo, axis=(1, 2)) / np.linalg.norm(Uo, axis=(1, 2))
+    assert (rel < 1e-3).all(), rel
+    # U^T U (H + damp) == I
+    Hd = H.astype(np.float64) + np.eye(C) * (0.01 * np.diagonal(H, axis1=1, axis2=2).mean(-1))[:, None, None]
+    prod = np.einsum("bki,bkj->bij", U.astype(np.float64), U.astype(np.float64)) @ Hd
+    assert np.abs(prod - np.eye(C)).max() < 1e-2
+
+
+def test_rtn_grid_identity_on_oracle_random():
+    """Random sweep: GPU RTN == oracle RTN bit-exact (both restate grid.py)."""
+    from mlx_gptq_b200 import grid
+
+    rng = np.random.default_rng(99)
+    W = (rng.standard_normal((64, 1024)) * rng.uniform(0.001, 10, (64, 1))).astype(np.float32)
+    for mode in ("mxfp4", "mxfp8"):
+        q, s, _, dq = grid.rtn_quantize_mxfp(_cuda(W), mode)
+        oq, os_, _, odq = ogrid.rtn_quantize_mxfp(W, mode)
+        np.testing.assert_array_equal(q.cpu().numpy(), oq)
+        np.testing.assert_array_equal(s.cpu().numpy(), os_)
+    q, s, b, dq = grid.rtn_quantize(_cuda(W), 4, 64)
+    oq, os_, ob, odq = ogrid.rtn_quantize(W, 4, 64)
+    np.testing.assert_array_equal(q.cpu().numpy(), oq)
+    np.testing.assert_array_equal(dq.cpu().numpy(), odq)
