@@ -334,8 +334,8 @@ __global__ void escalate_kernel(int64_t B, FactorState st) {
 // ---------------------------------------------------------------------------
 template <int VPL, int VPB>
 __global__ void __launch_bounds__(256) affine_block_kernel(float* __restrict__ W, const float* __restrict__ U,
-                                                           int64_t R, int64_t C, int64_t i1, int bits, int nshrink,
-                                                           int storage, uint8_t* __restrict__ q,
+                                                           int64_t R, int64_t C, int64_t i1, int nslots, int bits,
+                                                           int nshrink, int storage, uint8_t* __restrict__ q,
                                                            void* __restrict__ scales, void* __restrict__ biases,
                                                            float* __restrict__ Err) {
   constexpr int G = 32 * VPL, BS = 32 * VPB;
@@ -349,13 +349,15 @@ __global__ void __launch_bounds__(256) affine_block_kernel(float* __restrict__ W
   const int64_t ng = C / G;
   float* wrow = W + (b * R + r) * C + i1;
   const float* Ub = U + b * C * C + i1 * C + i1;  // U1 = U[i1:i2, i1:i2], row stride C
+  // nslots = columns in this block / 32 (< VPB only for the last, partial block)
   float w[VPB], dqv[VPB], ev[VPB], qv[VPB];
 #pragma unroll
-  for (int k = 0; k < VPB; ++k) w[k] = wrow[lane + 32 * k];
+  for (int k = 0; k < VPB; ++k) w[k] = k < nslots ? wrow[lane + 32 * k] : 0.0f;
   const float maxq = float((1 << bits) - 1);
   float s = 0.0f, bb = 0.0f;
 #pragma unroll
   for (int k = 0; k < VPB; ++k) {  // slot k = columns 32k .. 32k+31 of the block
+    if (k >= nslots) break;
     if ((32 * k) % G == 0) {       // group start (gptq.py:250-256)
       float v[VPL];
 #pragma unroll
@@ -383,7 +385,7 @@ __global__ void __launch_bounds__(256) affine_block_kernel(float* __restrict__ W
 #pragma unroll
       for (int kk = k; kk < VPB; ++kk) {
         const int col = 32 * kk + lane;
-        if (col > j) w[kk] = w[kk] - e * __ldg(urow + col);
+        if (kk < nslots && col > j) w[kk] = w[kk] - e * __ldg(urow + col);
       }
     }
   }
@@ -391,6 +393,7 @@ __global__ void __launch_bounds__(256) affine_block_kernel(float* __restrict__ W
   float* erow = Err + (b * R + r) * BS;
 #pragma unroll
   for (int k = 0; k < VPB; ++k) {
+    if (k >= nslots) break;
     wrow[lane + 32 * k] = dqv[k];
     qrow[lane + 32 * k] = uint8_t(qv[k]);
     erow[lane + 32 * k] = ev[k];
@@ -582,14 +585,12 @@ extern "C" int gq_gptq_affine(float* W, const void* W_orig, int w_dtype, const f
   const int nshrink = clip == GQ_CLIP_MSE ? kMaxShrinks : 1;
   const dim3 cgrid(unsigned((R + 7) / 8), unsigned(B));
   for (int64_t i1 = 0; i1 < C; i1 += bs) {
+    // the last block may be partial (gptq.py:242); it is still a whole number of groups
     const int64_t n = std::min<int64_t>(bs, C - i1);
-    // C % G == 0 and bs % G == 0: a trailing partial block is a whole number of groups,
-    // and VPB must match it; only full blocks reach the templated kernel below.
-    GQ_REQUIRE(n == bs, "gq_gptq_affine: C=%lld must be a multiple of the block (%lld)", (long long)C,
-               (long long)bs);
-#define AB(VPL, VPB)                                                                                            \
-  affine_block_kernel<VPL, VPB><<<cgrid, 256, 0, s>>>(W, U, R, C, i1, bits, nshrink, storage_dtype, q, scales, \
-                                                      biases, Err)
+    const int nslots = int(n / 32);
+#define AB(VPL, VPB)                                                                                                \
+  affine_block_kernel<VPL, VPB><<<cgrid, 256, 0, s>>>(W, U, R, C, i1, nslots, bits, nshrink, storage_dtype, q,     \
+                                                      scales, biases, Err)
     if (bs == 128) {
       switch (group_size) {
         case 32: AB(1, 4); break;

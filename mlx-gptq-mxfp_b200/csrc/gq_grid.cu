@@ -138,7 +138,6 @@ using namespace gq;
 extern "C" int gq_rtn_affine(const void* W, int w_dtype, int64_t rows, int64_t C, int bits, int group_size, int clip,
                              int storage_dtype, uint8_t* q, void* scales, void* biases, void* w_dq, int wdq_dtype,
                              void* stream) {
-  GQ_REQUIRE(W && q && scales && biases, "gq_rtn_affine: null pointer");
   GQ_REQUIRE(valid_dtype(w_dtype) && valid_dtype(storage_dtype) && valid_dtype(wdq_dtype), "gq_rtn_affine: dtype");
   GQ_REQUIRE(bits == 2 || bits == 3 || bits == 4 || bits == 5 || bits == 6 || bits == 8,
              "gq_rtn_affine: bits %d unsupported", bits);
@@ -149,6 +148,7 @@ extern "C" int gq_rtn_affine(const void* W, int w_dtype, int64_t rows, int64_t C
   GQ_REQUIRE(clip == GQ_CLIP_MSE || clip == GQ_CLIP_MINMAX, "gq_rtn_affine: clip");
   const int64_t nw = rows * (C / group_size);
   if (nw == 0) return GQ_OK;
+  GQ_REQUIRE(W && q && scales && biases, "gq_rtn_affine: null pointer");
   const int nshrink = clip == GQ_CLIP_MSE ? kMaxShrinks : 1;
   cudaStream_t s = (cudaStream_t)stream;
   const unsigned grid = blocks_for(nw, 8);
@@ -167,12 +167,12 @@ extern "C" int gq_rtn_affine(const void* W, int w_dtype, int64_t rows, int64_t C
 
 extern "C" int gq_rtn_mxfp(const void* W, int w_dtype, int64_t rows, int64_t C, int mode, uint8_t* q,
                            uint8_t* q_packed, uint8_t* scales, void* w_dq, int wdq_dtype, void* stream) {
-  GQ_REQUIRE(W && q && scales, "gq_rtn_mxfp: null pointer");
   GQ_REQUIRE(mode == GQ_MXFP4 || mode == GQ_MXFP8, "gq_rtn_mxfp: not a microscaling mode: %d", mode);
   GQ_REQUIRE(valid_dtype(w_dtype) && valid_dtype(wdq_dtype), "gq_rtn_mxfp: dtype");
   GQ_REQUIRE(rows >= 0 && C >= 0 && C % 32 == 0, "gq_rtn_mxfp: columns %lld not divisible by 32", (long long)C);
   const int64_t ng = rows * (C / 32);
   if (ng == 0) return GQ_OK;
+  GQ_REQUIRE(W && q && scales, "gq_rtn_mxfp: null pointer");
   cudaStream_t s = (cudaStream_t)stream;
   if (mode == GQ_MXFP4)
     rtn_mxfp_kernel<GQ_MXFP4><<<blocks_for(ng, 8), 256, 0, s>>>(W, w_dtype, ng, q, q_packed, scales, w_dq, wdq_dtype);
@@ -183,13 +183,13 @@ extern "C" int gq_rtn_mxfp(const void* W, int w_dtype, int64_t rows, int64_t C, 
 
 extern "C" int gq_dequantize(const uint8_t* q, const void* scales, const void* biases, int scale_dtype, int64_t rows,
                              int64_t C, int mode, int group_size, float* out, void* stream) {
-  GQ_REQUIRE(q && scales && out, "gq_dequantize: null pointer");
   GQ_REQUIRE(mode == GQ_AFFINE || mode == GQ_MXFP4 || mode == GQ_MXFP8, "gq_dequantize: mode %d", mode);
   GQ_REQUIRE(mode == GQ_AFFINE || group_size == 32, "gq_dequantize: MXFP requires group size 32");
   GQ_REQUIRE(mode != GQ_AFFINE || (biases && valid_dtype(scale_dtype)), "gq_dequantize: affine needs biases");
   GQ_REQUIRE(group_size > 0 && C % group_size == 0, "gq_dequantize: C %% group");
   const int64_t n = rows * C;
   if (n == 0) return GQ_OK;
+  GQ_REQUIRE(q && scales && out, "gq_dequantize: null pointer");
   dequant_kernel<<<blocks_for(n, 256), 256, 0, (cudaStream_t)stream>>>(q, scales, biases, scale_dtype, n, C, mode,
                                                                         group_size, out);
   return check_launch("dequant_kernel");
@@ -197,10 +197,10 @@ extern "C" int gq_dequantize(const uint8_t* q, const void* scales, const void* b
 
 extern "C" int gq_pack_q(const uint8_t* q, int64_t rows, int64_t C, int bits, uint32_t* words, void* stream) {
   GQ_REQUIRE(bits == 2 || bits == 4 || bits == 8, "cannot pack %d-bit for MLX (supported: (2, 4, 8))", bits);
-  GQ_REQUIRE(q && words, "gq_pack_q: null pointer");
   GQ_REQUIRE(C % (32 / bits) == 0, "gq_pack_q: last dim %lld not divisible by %d", (long long)C, 32 / bits);
   const int64_t nw = rows * C / (32 / bits);
   if (nw == 0) return GQ_OK;
+  GQ_REQUIRE(q && words, "gq_pack_q: null pointer");
   pack_q_kernel<<<blocks_for(nw, 256), 256, 0, (cudaStream_t)stream>>>(q, nw, bits, words);
   return check_launch("pack_q_kernel");
 }
@@ -208,27 +208,27 @@ extern "C" int gq_pack_q(const uint8_t* q, int64_t rows, int64_t C, int bits, ui
 extern "C" int gq_unpack_q(const uint32_t* words, int64_t rows, int64_t n_words, int bits, int64_t out_cols,
                            uint8_t* q, void* stream) {
   GQ_REQUIRE(bits == 2 || bits == 4 || bits == 8, "gq_unpack_q: bits %d", bits);
-  GQ_REQUIRE(words && q, "gq_unpack_q: null pointer");
   GQ_REQUIRE(out_cols <= n_words * (32 / bits), "gq_unpack_q: out_cols too large");
   const int64_t n = rows * out_cols;
   if (n == 0) return GQ_OK;
+  GQ_REQUIRE(words && q, "gq_unpack_q: null pointer");
   unpack_q_kernel<<<blocks_for(n, 256), 256, 0, (cudaStream_t)stream>>>(words, rows, n_words, bits, out_cols, q);
   return check_launch("unpack_q_kernel");
 }
 
 extern "C" int gq_pack_nibbles(const uint8_t* q, int64_t rows, int64_t C, uint8_t* out, void* stream) {
-  GQ_REQUIRE(q && out, "gq_pack_nibbles: null pointer");
   GQ_REQUIRE(C % 2 == 0, "gq_pack_nibbles: odd last dim");
   const int64_t n = rows * C / 2;
   if (n == 0) return GQ_OK;
+  GQ_REQUIRE(q && out, "gq_pack_nibbles: null pointer");
   pack_nibbles_kernel<<<blocks_for(n, 256), 256, 0, (cudaStream_t)stream>>>(q, n, out);
   return check_launch("pack_nibbles_kernel");
 }
 
 extern "C" int gq_unpack_nibbles(const uint8_t* packed, int64_t rows, int64_t n_bytes, uint8_t* q, void* stream) {
-  GQ_REQUIRE(packed && q, "gq_unpack_nibbles: null pointer");
   const int64_t n = rows * n_bytes;
   if (n == 0) return GQ_OK;
+  GQ_REQUIRE(packed && q, "gq_unpack_nibbles: null pointer");
   unpack_nibbles_kernel<<<blocks_for(n, 256), 256, 0, (cudaStream_t)stream>>>(packed, n, q);
   return check_launch("unpack_nibbles_kernel");
 }

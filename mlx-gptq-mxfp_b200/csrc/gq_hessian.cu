@@ -8,9 +8,17 @@
 //
 // One CTA per 128 x 256 output tile on or above the diagonal (H is symmetric;
 // the epilogue mirrors). Warp roles: warp 0 = TMA producer, warp 1 = TMEM owner
-// and MMA issuer, warps 2-5 = epilogue (TMEM lanes 32*(warp%4) .. +31).
-// Pipeline: 4 stages x (A 128x64 + B 256x64 bf16) = 192 KB of shared memory,
-// fp32 accumulators in 256 TMEM columns.
+// and MMA issuer, warps 2-9 = accumulator warps (TMEM lanes 32*(warp%4) .. +31,
+// column half (warp-2)/4).
+//
+// Precision: the tensor core's fp32 accumulation is biased (it loses ~1e-7
+// relative per MMA step, always toward zero), so one accumulator over 131072
+// tokens drifts by ~7e-4. The token range is therefore cut into chunks of
+// kChunkTiles * 64 tokens; each chunk accumulates in one of two TMEM buffers
+// (2 x 256 columns) while the accumulator warps add the previous chunk into
+// fp32 registers with round-to-nearest adds. Error stays ~2e-6 relative, the
+// tensor pipe never waits, and no extra memory traffic is generated.
+// Pipeline: 4 stages x (A 128x64 + B 256x64 bf16) = 192 KB of shared memory.
 #include <mutex>
 
 #include "gq_common.cuh"
@@ -18,12 +26,14 @@
 namespace gq {
 namespace hess {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4, THREADS = 192;
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int EPI_WARPS = 8, THREADS = 64 + 32 * EPI_WARPS;
+constexpr int kChunkTiles = 16;                      // 1024 tokens per TMEM chunk
 constexpr uint32_t BOX_BYTES = 64 * 64 * 2;          // one 64-channel x 64-token TMA box
 constexpr uint32_t A_BYTES = BM * BK * 2;            // 16 KB
 constexpr uint32_t B_BYTES = BN * BK * 2;            // 32 KB
 constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;  // 48 KB
-constexpr uint32_t TMEM_COLS = 256;
+constexpr uint32_t TMEM_COLS = 512;                  // two 256-column accumulators
 constexpr size_t SMEM_BYTES = size_t(STAGES) * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
 
 // Tiles (tm, tn) with tm <= 2*tn + 1 touch the upper triangle; enumerate them
@@ -37,6 +47,10 @@ __host__ inline int64_t num_tiles(int64_t c) {
   return t;
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __global__ void __launch_bounds__(THREADS, 1)
     hessian_kernel(const __grid_constant__ CUtensorMap tmap, int64_t n, int64_t c, float* __restrict__ H,
                    int64_t ldh, float alpha, float beta, int32_t* status) {
@@ -44,8 +58,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
   uint64_t* empty = full + STAGES;
-  uint64_t* accum = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  uint64_t* tfull = empty + STAGES;  // [2] chunk accumulated in TMEM buffer b
+  uint64_t* tempty = tfull + 2;      // [2] TMEM buffer b drained
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -57,13 +72,17 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
   const int64_t tm = t;
   const int KT = int((n + BK - 1) / BK);
+  const int NCH = (KT + kChunkTiles - 1) / kChunkTiles;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], EPI_WARPS);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -101,42 +120,64 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_bf16(BM, BN, true, true);
       for (int kt = 0; kt < KT; ++kt) {
+        const int ch = kt / kChunkTiles, buf = ch & 1;
+        const bool chunk_start = kt % kChunkTiles == 0;
+        const bool chunk_end = kt % kChunkTiles == kChunkTiles - 1 || kt == KT - 1;
+        if (chunk_start && !mbar_wait(&tempty[buf], ((ch >> 1) & 1) ^ 1, abort_flag, status)) break;
         const int s = kt % STAGES;
         const uint32_t ph = (kt / STAGES) & 1;
         if (!mbar_wait(&full[s], ph, abort_flag, status)) break;
         tc_fence_after();
         const uint32_t a0 = smem_u32(smem + s * STAGE_BYTES), b0 = a0 + A_BYTES;
+        const uint32_t d = tmem + uint32_t(buf * BN);
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk) {
           // K advances 16 rows of 128 B inside the swizzled boxes; LBO = next
           // 64-channel box, SBO = next 8-row core-matrix group.
           const uint64_t ad = umma_desc_sw128(a0 + kk * 2048, BOX_BYTES, 1024);
           const uint64_t bd = umma_desc_sw128(b0 + kk * 2048, BOX_BYTES, 1024);
-          umma_f16(tmem, ad, bd, idesc, (kt | kk) != 0);
+          umma_f16(d, ad, bd, idesc, (!chunk_start || kk != 0) ? 1u : 0u);
         }
         umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+        if (chunk_end) umma_commit(&tfull[buf]);
       }
-      umma_commit(accum);
     }
   } else {
-    // epilogue: TMEM -> registers -> H (upper part) and its mirror
-    const bool ok = mbar_wait(accum, 0, abort_flag, status);
-    tc_fence_after();
-    if (ok && !*abort_flag && KT > 0) {
-      const int qw = warp & 3;
-      const int64_t gr = tm * BM + qw * 32 + lane;
-      const int64_t cb = tn * BN;
-      const bool all_upper = cb > tm * BM + BM - 1;
-#pragma unroll 1
-      for (int ch = 0; ch < BN / 32; ++ch) {
-        uint32_t acc[32];
-        tmem_ld32(tmem + (uint32_t(qw * 32) << 16) + uint32_t(ch * 32), acc);
-        tmem_ld_wait();
-        const int64_t c0 = cb + ch * 32;
-        if (c0 >= c) break;
-        float v[32];
+    // accumulator warps: drain each chunk into fp32 registers, then write H
+    const int qw = warp & 3, half = (warp - 2) >> 2;
+    const uint32_t lane_base = uint32_t(qw * 32) << 16;
+    float acc[128];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = alpha * __uint_as_float(acc[j]);
+    for (int j = 0; j < 128; ++j) acc[j] = 0.0f;
+    bool ok = true;
+    for (int ch = 0; ch < NCH; ++ch) {
+      const int buf = ch & 1;
+      ok = mbar_wait(&tfull[buf], (ch >> 1) & 1, abort_flag, status);
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_base + uint32_t(buf * BN + half * 128 + q4 * 32), r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[q4 * 32 + j] = acc[q4 * 32 + j] + __uint_as_float(r[j]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+    }
+    if (ok && !*abort_flag && KT > 0) {
+      const int64_t gr = tm * BM + qw * 32 + lane;
+      const int64_t cb = tn * BN + half * 128;
+      const bool all_upper = tn * BN > tm * BM + BM - 1;
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        const int64_t c0 = cb + q4 * 32;
+        if (c0 >= c) break;
+        float* v = acc + q4 * 32;  // scaled in place (each value is used once after this)
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = alpha * v[j];
         // direct (upper) part: row gr, columns c0..c0+31 with column >= row
         if (gr < c) {
           float* hp = H + gr * ldh + c0;
@@ -159,7 +200,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
         // mirror (strictly lower) part: H[gc][gr] for gc > gr; lanes hold consecutive gr
-#pragma unroll 4
+#pragma unroll
         for (int j = 0; j < 32; ++j) {
           const int64_t gc = c0 + j;
           if (gc > gr && gc < c && gr < c) {
