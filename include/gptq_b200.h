@@ -17,7 +17,8 @@
  *    message for the last failing call on the calling host thread.
  *  - Re-entrant: no mutable global state; the library allocates no device memory.
  *    Scratch is caller-provided ("workspace"), sized by the *_workspace_size
- *    queries.
+ *    queries. (gq_gptq_mxfp_noalloc is the one exception: it uses a fixed array
+ *    inside the library instead of a workspace; see its comment.)
  *  - Device-side waits are bounded (2 s); a kernel that gives up writes
  *    GQ_ERR_TIMEOUT to the optional device word `status` and returns.
  */
@@ -127,6 +128,27 @@ int gq_gptq_mxfp(const void* W, int w_dtype, const float* H, const float* U, con
                  const int32_t* info, int64_t B, int64_t R, int64_t C, int mode, int algorithm, uint8_t* q,
                  uint8_t* q_packed, uint8_t* scales, void* w_dq, int wdq_dtype, float* rel_err, void* workspace,
                  size_t workspace_bytes, void* stream);
+
+/* Same computation and arguments as gq_gptq_mxfp, but the library allocates
+ * nothing and the caller passes no workspace: the rel_err partial sums live in a
+ * fixed 4 MiB array inside the library (every GPU that loads the library holds
+ * it until the process exits). For hosts that cannot call cudaMalloc: callers
+ * that own all device memory through their own pool or arena, that must not
+ * allocate while running (an embedded runtime, a real-time serving loop), or
+ * whose binding layer has no CUDA allocator to reach (a JNI, cgo or ctypes shim
+ * given only the tensors it must read and write). Inputs and outputs are still
+ * the caller's.
+ * Limit: B * ceil(R/128) * (C/32) <= 524288 (row tile, group) pairs, else
+ * GQ_ERR_ARG; e.g. [1, 11008, 4096] uses 11008 and [128, 1536, 2048] uses 98304.
+ * The first call on a device looks up the array's device address (once per
+ * device, with that device current); make that first call before any stream
+ * capture. The array is shared by all calls and keeps the last call's contents;
+ * each call rewrites every entry it reads, so nothing needs clearing, but calls
+ * that overlap on the GPU (other streams, other host threads) race on it.
+ * This entry point has no counterpart in the reference. */
+int gq_gptq_mxfp_noalloc(const void* W, int w_dtype, const float* H, const float* U, const uint8_t* dead,
+                         const int32_t* info, int64_t B, int64_t R, int64_t C, int mode, int algorithm, uint8_t* q,
+                         uint8_t* q_packed, uint8_t* scales, void* w_dq, int wdq_dtype, float* rel_err, void* stream);
 
 /* Affine GPTQ (gptq.py:183-272): blocked column loop (block = max(block_size, G)
  * rounded down to a multiple of G) with the MSE/minmax clip search at each group

@@ -501,3 +501,54 @@ extern "C" int gq_gptq_mxfp(const void* W, int w_dtype, const float* H, const fl
   if (st != GQ_OK || !rel_err) return st;
   return launch_rel_err(partials, B, ((R + 127) / 128) * (C / 32), rel_err, s);
 }
+
+// ---------------------------------------------------------------------------
+// MXFP GPTQ without caller workspace (see gq_gptq_mxfp_noalloc in gptq_b200.h)
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace gq {
+
+// Scratch for the rel_err partial sums of gq_gptq_mxfp_noalloc: one (num, den)
+// float pair per (batch item, 128-row tile, 32-column group). Every GPU that
+// loads this library holds it (4 MiB) until the process exits.
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+// Device address of g_noalloc_scratch on the current device, looked up once per
+// device. In host code the symbol itself is only a host-side stand-in and must
+// never be handed to a kernel.
+static int noalloc_scratch(void** out) {
+  constexpr int kMaxDevices = 64;
+  static std::mutex mu;
+  static void* addr[kMaxDevices] = {};
+  int dev = 0;
+  GQ_CUDA_TRY(cudaGetDevice(&dev));
+  GQ_REQUIRE(dev >= 0 && dev < kMaxDevices, "gq_gptq_mxfp_noalloc: device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    GQ_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return GQ_OK;
+}
+
+}  // namespace gq
+
+extern "C" int gq_gptq_mxfp_noalloc(const void* W, int w_dtype, const float* H, const float* U, const uint8_t* dead,
+                                    const int32_t* info, int64_t B, int64_t R, int64_t C, int mode, int algorithm,
+                                    uint8_t* q, uint8_t* q_packed, uint8_t* scales, void* w_dq, int wdq_dtype,
+                                    float* rel_err, void* stream) {
+  const size_t need = gq_gptq_mxfp_workspace_size(B, R, C);
+  GQ_REQUIRE(need <= kNoAllocScratchBytes,
+             "gq_gptq_mxfp_noalloc: B*ceil(R/128)*(C/32) = %zu (row tile, group) pairs exceed the fixed scratch "
+             "limit of %zu; split the batch or use gq_gptq_mxfp with a workspace",
+             need / (2 * sizeof(float)), kNoAllocScratchBytes / (2 * sizeof(float)));
+  void* scratch = nullptr;
+  int st = noalloc_scratch(&scratch);
+  if (st != GQ_OK) return st;
+  return gq_gptq_mxfp(W, w_dtype, H, U, dead, info, B, R, C, mode, algorithm, q, q_packed, scales, w_dq, wdq_dtype,
+                      rel_err, scratch, kNoAllocScratchBytes, stream);
+}

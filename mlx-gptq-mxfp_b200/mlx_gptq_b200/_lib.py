@@ -39,6 +39,7 @@ SIGNATURES = {
     "gq_prepare_hinv": (I32, [P, I64, I64, F32, P, P, P, P, SZ, P]),
     "gq_gptq_mxfp_workspace_size": (SZ, [I64, I64, I64]),
     "gq_gptq_mxfp": (I32, [P, I32, P, P, P, P, I64, I64, I64, I32, I32, P, P, P, P, I32, P, P, SZ, P]),
+    "gq_gptq_mxfp_noalloc": (I32, [P, I32, P, P, P, P, I64, I64, I64, I32, I32, P, P, P, P, I32, P, P]),
     "gq_gptq_affine_workspace_size": (SZ, [I64, I64, I64, I32, I32]),
     "gq_gptq_affine": (I32, [P, P, I32, P, I64, I64, I64, I32, I32, I32, I32, I32, P, P, P, P, P, SZ, P]),
     "gq_prepare_weights": (I32, [P, I32, P, I64, I64, I64, P, P]),
