@@ -328,6 +328,29 @@ def run_reference_arm(args, ws, rank):
     print(json.dumps(line), flush=True)
 
 
+def profile_case(case, device):
+    """Small, self-contained launches for ncu captures (a few launches, inputs > L2)."""
+    from mlx_gptq_b200 import hessian_accumulate, layer
+
+    if case == "hessian":
+        X = student_t_bf16(16384, HIDDEN, 7, device)  # 128 MiB > L2
+        H = torch.empty(HIDDEN, HIDDEN, device=device)
+        for _ in range(4):
+            hessian_accumulate(X, H, 1.0, 0.0)
+    elif case == "solve":
+        X = student_t_bf16(8192, HIDDEN, 7, device)
+        H = torch.empty(HIDDEN, HIDDEN, device=device)
+        hessian_accumulate(X, H, 1.0, 0.0)
+        W = weights_bf16(INTER, HIDDEN, 8, device)  # 90 MB bf16 in, 90 MB bf16 out
+        f = layer.mxfp_factors(H.unsqueeze(0))
+        for _ in range(3):
+            layer.solve_mxfp_packed(W, f, "mxfp4", "safe-scale-search", torch.bfloat16, True, check_info=False)
+    else:
+        raise SystemExit(f"unknown profile case {case}")
+    torch.cuda.synchronize()
+    print(f"profile case {case} done")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -336,8 +359,13 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--profile-case", choices=["hessian", "solve"], default=None,
+                    help="run a small case of one kernel for an ncu capture and exit")
     args = ap.parse_args()
     ws, rank, local = dist_env()
+    if args.profile_case:
+        profile_case(args.profile_case, torch.device("cuda", 0))
+        return
     if args.impl == "reference":
         run_reference_arm(args, ws, rank)
         return
