@@ -335,16 +335,26 @@ def profile_case(case, device):
     if case == "hessian":
         X = student_t_bf16(16384, HIDDEN, 7, device)  # 128 MiB > L2
         H = torch.empty(HIDDEN, HIDDEN, device=device)
-        for _ in range(4):
+        for i in range(4):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
             hessian_accumulate(X, H, 1.0, 0.0)
+            b.record()
+            b.synchronize()
+            print(f"hessian launch {i}: {a.elapsed_time(b):.3f} ms")
     elif case == "solve":
         X = student_t_bf16(8192, HIDDEN, 7, device)
         H = torch.empty(HIDDEN, HIDDEN, device=device)
         hessian_accumulate(X, H, 1.0, 0.0)
         W = weights_bf16(INTER, HIDDEN, 8, device)  # 90 MB bf16 in, 90 MB bf16 out
         f = layer.mxfp_factors(H.unsqueeze(0))
-        for _ in range(3):
+        for i in range(4):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
             layer.solve_mxfp_packed(W, f, "mxfp4", "safe-scale-search", torch.bfloat16, True, check_info=False)
+            b.record()
+            b.synchronize()
+            print(f"solve launch {i}: {a.elapsed_time(b):.3f} ms ({W.numel() / a.elapsed_time(b) / 1e6:.2f} G elems/s)")
     else:
         raise SystemExit(f"unknown profile case {case}")
     torch.cuda.synchronize()

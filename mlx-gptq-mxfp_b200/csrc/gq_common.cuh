@@ -150,6 +150,72 @@ __device__ __forceinline__ float e4m3_decode(uint32_t c) {
   return (c & 0x80u) ? -v : v;
 }
 
+// ---------------------------------------------------------------------------
+// sm_100 hardware conversions, two values per instruction. E2M1 and E4M3 with
+// round-to-nearest-even and saturation are exactly the reference's grids: the
+// E2M1 thresholds of grid.py:82-105 are the RNE midpoints (ties at 0.25, 1.25,
+// 2.5, 5 go down to the even code, ties at 0.75, 1.75, 3.5 up), everything
+// above 5 maps to 6; E4M3 after the reference's +-448 clamp is the satfinite
+// RNE cast. The one difference is the sign of zero: the reference sets the E2M1
+// sign bit from (x < 0), so -0.0 and NaN give code 0 -- callers pass +0.0 for them.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cvt_e2m1x2(float lo, float hi) {  // byte: lo in bits 0-3
+  uint16_t r;
+  asm("{ .reg .b8 t; cvt.rn.satfinite.e2m1x2.f32 t, %1, %2; mov.b16 %0, {t, 0}; }" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ float2 e2m1x2_to_f32(uint32_t byte) {  // .x from bits 0-3
+  uint32_t h2;
+  const uint16_t t = uint16_t(byte);
+  asm("{ .reg .b8 a, z; mov.b16 {a, z}, %1; cvt.rn.f16x2.e2m1x2 %0, a; }" : "=r"(h2) : "h"(t));
+  return __half22float2(*reinterpret_cast<const __half2*>(&h2));
+}
+__device__ __forceinline__ uint32_t cvt_e4m3x2(float lo, float hi) {  // 16 bits: lo in bits 0-7
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ float2 e4m3x2_to_f32(uint32_t two) {  // .x from bits 0-7
+  uint32_t h2;
+  const uint16_t t = uint16_t(two);
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(t));
+  return __half22float2(*reinterpret_cast<const __half2*>(&h2));
+}
+__device__ __forceinline__ float e2m1_sanitize(float x) { return (x == 0.0f || x != x) ? 0.0f : x; }
+
+// E2M1 grid value (without the scale) of x, by arithmetic on the full-rate
+// pipes: round-to-nearest-even at spacing 0.5 below 2, 1 in [2, 4), 2 above,
+// saturating at 6 -- the reference's thresholds (grid.py:82-105) -- with the
+// reference's sign convention (negative only when x < 0; NaN -> 0).
+__device__ __forceinline__ float e2m1_round(float x) {
+  float a = fabsf(x);
+  a = a == a ? a : 0.0f;
+  const float k = a < 2.0f ? 2.0f : (a < 4.0f ? 1.0f : 0.5f);
+  const float ik = a < 2.0f ? 0.5f : (a < 4.0f ? 1.0f : 2.0f);
+  const float v = fminf(rintf(a * k) * ik, 6.0f);
+  return x < 0.0f ? -v : v;
+}
+
+// Two MXFP elements at once (scale 2^e, inv = 2^-e): codes packed as in the
+// artifact (mxfp4: one byte, element 0 in the low nibble; mxfp8: two bytes,
+// element 0 in the low byte) and the dequantized values.
+template <int MODE>
+__device__ __forceinline__ uint32_t mx_quant2(float w0, float w1, float inv, float sc, float& dq0, float& dq1) {
+  float x0 = w0 * inv, x1 = w1 * inv;
+  uint32_t codes;
+  float2 v;
+  if (MODE == GQ_MXFP4) {
+    codes = cvt_e2m1x2(e2m1_sanitize(x0), e2m1_sanitize(x1));
+    v = e2m1x2_to_f32(codes);
+  } else {
+    codes = cvt_e4m3x2(x0, x1);
+    v = e4m3x2_to_f32(codes);
+  }
+  dq0 = v.x * sc;
+  dq1 = v.y * sc;
+  return codes;
+}
+
 // Grid value of an MXFP code (without the scale).
 template <int MODE>
 __device__ __forceinline__ float mx_value(uint32_t code) {

@@ -58,8 +58,8 @@ __global__ void __launch_bounds__(256) rtn_mxfp_kernel(const void* __restrict__ 
   const float w = load_any(W, idx, w_dtype);
   const float amax = warp_max(fabsf(w));
   const int e = mx_scale_exponent(amax, MODE == GQ_MXFP4 ? 6.0f : 448.0f);
-  uint32_t code;
-  const float dq = mx_quant<MODE>(w, exp2i(-e), exp2i(e), code);
+  float dq, unused;
+  const uint32_t code = mx_quant2<MODE>(w, 0.0f, exp2i(-e), exp2i(e), dq, unused) & (MODE == GQ_MXFP4 ? 0xFu : 0xFFu);
   q[idx] = uint8_t(code);
   if (MODE == GQ_MXFP4 && q_packed) {
     uint32_t hi = __shfl_down_sync(0xFFFFFFFFu, code, 1);

@@ -137,9 +137,11 @@ __global__ void __launch_bounds__(128) mx_hinv_kernel(const float* __restrict__ 
 // --------------------------------------------------------------------------
 
 // e^T H e for a 32-vector held in registers (the einsum of gptq.py:123-125, 168).
-// The row index i runs as a rolled loop (bounded register pressure); e_i comes
-// from this thread's column of the staging buffer Es, the 32-wide row dot uses
-// the registers. Four partial accumulators give the FMA pipe independent chains.
+// The row index i runs as a rolled loop: the kernel's code stays small enough
+// for the instruction cache, which matters more here than halving the FMAs with
+// the symmetric form (fully unrolled it ran 2x slower). e_i comes from this
+// thread's column of the staging buffer Es, the 32-wide row dot from registers;
+// four partial sums give the FMA pipe independent chains.
 __device__ __forceinline__ float quad32(const float (&e)[32], const float (*Hs)[32], float (*Es)[129], int tid) {
 #pragma unroll
   for (int c = 0; c < 32; ++c) Es[c][tid] = e[c];
@@ -158,6 +160,15 @@ __device__ __forceinline__ float quad32(const float (&e)[32], const float (*Hs)[
     obj = fmaf(Es[i][tid], (a0 + a1) + (a2 + a3), obj);
   }
   return obj;
+}
+
+// Grid value (without the scale) of w * inv for the mode.
+template <int MODE>
+__device__ __forceinline__ float mx_round(float w, float inv) {
+  if (MODE == GQ_MXFP4) return e2m1_round(w * inv);
+  float d0, d1;
+  mx_quant2<MODE>(w, 0.0f, inv, 1.0f, d0, d1);
+  return d0;
 }
 
 template <typename T>
@@ -211,8 +222,26 @@ __device__ __forceinline__ void store_row32<__nv_bfloat16>(__nv_bfloat16* __rest
   }
 }
 
+// Code storage of one row group: mxfp4 = 16 bytes of nibble pairs (the artifact
+// layout: column c at bits 4*(c%8) of word c/8); mxfp8 = 32 E4M3 bytes.
+template <int MODE> struct Codes {
+  static constexpr int kWords = MODE == GQ_MXFP4 ? 4 : 8;
+  uint32_t w[kWords];
+  __device__ __forceinline__ void clear() {
+#pragma unroll
+    for (int i = 0; i < kWords; ++i) w[i] = 0;
+  }
+  // pair (c, c+1), c even, as returned by mx_quant2
+  __device__ __forceinline__ void put2(int c, uint32_t codes) {
+    if (MODE == GQ_MXFP4) w[c >> 3] |= codes << (4 * (c & 7));
+    else w[c >> 2] |= codes << (8 * (c & 3));
+  }
+};
+
+// 3 CTAs per SM (168 registers) measured fastest: occupancy hides the latency of
+// the sequential GPTQ chain better than the extra registers would.
 template <int MODE, bool SAFE, typename Tin, typename Tout>
-__global__ void __launch_bounds__(128) mx_gptq_kernel(const Tin* __restrict__ W, const float* __restrict__ H,
+__global__ void __launch_bounds__(128, 3) mx_gptq_kernel(const Tin* __restrict__ W, const float* __restrict__ H,
                                                       const float* __restrict__ U, const uint8_t* __restrict__ dead,
                                                       const int32_t* __restrict__ info, int64_t R, int64_t C,
                                                       uint8_t* __restrict__ q, uint8_t* __restrict__ qp,
@@ -271,10 +300,7 @@ __global__ void __launch_bounds__(128) mx_gptq_kernel(const Tin* __restrict__ W,
         const float sc = exp2i(e), inv = exp2i(-e);
         float err[32];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          uint32_t code;
-          err[c] = mx_quant<MODE>(o[c], inv, sc, code) - o[c];
-        }
+        for (int c = 0; c < 32; ++c) err[c] = mx_round<MODE>(o[c], inv) * sc - o[c];
         const float obj = quad32(err, Hs, Es, tid);
         if (t == 0 || obj < best_obj) {
           best_obj = obj;
@@ -284,18 +310,15 @@ __global__ void __launch_bounds__(128) mx_gptq_kernel(const Tin* __restrict__ W,
     }
     const float sc = exp2i(best_e), inv = exp2i(-best_e);
 
-    // sequential GPTQ over the 32 columns with the fixed scale. After column c
-    // is quantized, wv[c] is reused to hold its error gdq[c] - o[c]; dq itself
-    // is re-derived from the code (value(code) * scale is exact and repeatable).
-    float wv[32];
+    // sequential GPTQ over the 32 columns with the fixed scale. After column c is
+    // quantized, wv[c] is reused for its error dq[c] - o[c].
+    float wv[32], gv[32];  // gv: grid values (dq = gv * sc) of the GPTQ pass
 #pragma unroll
     for (int c = 0; c < 32; ++c) wv[c] = o[c];
-    uint32_t gcode[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // 4 codes per word (byte lanes)
 #pragma unroll
     for (int c = 0; c < 32; ++c) {
-      uint32_t code;
-      const float dq = mx_quant<MODE>(wv[c], inv, sc, code);
-      gcode[c >> 2] |= code << (8 * (c & 3));
+      gv[c] = mx_round<MODE>(wv[c], inv);
+      const float dq = gv[c] * sc;
       const float err = (wv[c] - dq) / Us[c][c];
 #pragma unroll
       for (int k = c + 1; k < 32; ++k) wv[k] = wv[k] - err * Us[c][k];
@@ -308,43 +331,43 @@ __global__ void __launch_bounds__(128) mx_gptq_kernel(const Tin* __restrict__ W,
     if (use_gptq) {
       bool valid = true;
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const uint32_t code = (gcode[c >> 2] >> (8 * (c & 3))) & 0xFFu;
-        valid = valid && (fabsf(mx_value<MODE>(code) * sc) <= limit);
-      }
+      for (int c = 0; c < 32; ++c) valid = valid && (fabsf(gv[c] * sc) <= limit);
       use_gptq = valid;
     }
     if (!use_gptq) {  // baseline: RTN with the chosen scale
 #pragma unroll
-      for (int c = 0; c < 8; ++c) gcode[c] = 0;
-#pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        uint32_t code;
-        mx_quant<MODE>(o[c], inv, sc, code);
-        gcode[c >> 2] |= code << (8 * (c & 3));
-      }
+      for (int c = 0; c < 32; ++c) gv[c] = mx_round<MODE>(o[c], inv);
     }
+    // codes of the grid values: the hardware cast of an on-grid value is exact and
+    // the sign of zero already follows the reference
+    Codes<MODE> code;
+    code.clear();
     float gdq[32];
 #pragma unroll
-    for (int c = 0; c < 32; ++c) gdq[c] = mx_value<MODE>((gcode[c >> 2] >> (8 * (c & 3))) & 0xFFu) * sc;
+    for (int c = 0; c < 32; c += 2) {
+      code.put2(c, MODE == GQ_MXFP4 ? cvt_e2m1x2(gv[c], gv[c + 1]) : cvt_e4m3x2(gv[c], gv[c + 1]));
+      gdq[c] = gv[c] * sc;
+      gdq[c + 1] = gv[c + 1] * sc;
+    }
     // outputs
     if (q) {
-      uint4* qd = reinterpret_cast<uint4*>(q + off);
-      qd[0] = make_uint4(gcode[0], gcode[1], gcode[2], gcode[3]);
-      qd[1] = make_uint4(gcode[4], gcode[5], gcode[6], gcode[7]);
-    }
-    if (MODE == GQ_MXFP4 && qp) {
-      uint32_t pk[4];
+      uint32_t qw[8];
+      if (MODE == GQ_MXFP4) {
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        // bytes (c0 | c1<<4), (c2 | c3<<4) from words 2t, 2t+1
-        const uint32_t a = gcode[2 * t], bb = gcode[2 * t + 1];
-        pk[t] = ((a & 0xFu) | ((a >> 4) & 0xF0u)) | (((a >> 16) & 0xFu) << 8) | (((a >> 20) & 0xF0u) << 8) |
-                (((bb & 0xFu) | ((bb >> 4) & 0xF0u)) << 16) | (((bb >> 16) & 0xFu) << 24) |
-                (((bb >> 20) & 0xF0u) << 24);
+        for (int w = 0; w < 8; ++w) {
+          const uint32_t n = (code.w[w >> 1] >> (16 * (w & 1))) & 0xFFFFu;
+          qw[w] = (n & 0xFu) | ((n & 0xF0u) << 4) | ((n & 0xF00u) << 8) | ((n & 0xF000u) << 12);
+        }
+      } else {
+#pragma unroll
+        for (int w = 0; w < 8; ++w) qw[w] = code.w[w];
       }
-      *reinterpret_cast<uint4*>(qp + off / 2) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      uint4* qd = reinterpret_cast<uint4*>(q + off);
+      qd[0] = make_uint4(qw[0], qw[1], qw[2], qw[3]);
+      qd[1] = make_uint4(qw[4], qw[5], qw[6], qw[7]);
     }
+    if (MODE == GQ_MXFP4 && qp)
+      *reinterpret_cast<uint4*>(qp + off / 2) = make_uint4(code.w[0], code.w[1], code.w[2], code.w[3]);
     scales[(b * R + r) * G + g] = uint8_t(best_e + 127);
     if (wdq) store_row32<Tout>(wdq + off, gdq);
     if (partials) {

@@ -111,3 +111,28 @@ def test_pack_edge_cases():
     assert empty.shape == (0, 4)
     full = np.full((3, 64), 15, np.uint8)
     assert (packing.pack_q(full, 4) == 0xFFFFFFFF).all()
+
+
+@pytest.mark.parametrize("mode,fmax", [("mxfp4", 6.0), ("mxfp8", 448.0)])
+def test_mxfp_element_codes_dense_sweep(mode, fmax):
+    """Every element code of the MXFP grids vs the oracle on ~1M values: a group max of
+    fmax pins the scale to 2^0, so the other 31 entries are quantized as they are.
+    Covers every threshold +-1 ulp, zeros of both signs, subnormals and saturation."""
+    from mlx_gptq_b200 import grid
+    from oracle import grid as ogrid
+
+    rng = np.random.default_rng(2024)
+    edges = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 6.0, 448.0, 464.0, 2.0**-9, 2.0**-6, 2.0**-10],
+                     np.float32)
+    near = np.concatenate([np.nextafter(edges, np.float32(0)), edges, np.nextafter(edges, np.float32(1e9))])
+    vals = np.concatenate([near, -near, [0.0, -0.0, 1e-40, -1e-40, 7.0, -7.0, 500.0, -500.0]]).astype(np.float32)
+    rnd = (rng.standard_normal(1 << 20) * rng.choice([0.01, 0.3, 1.0, 3.0, 100.0], 1 << 20)).astype(np.float32)
+    x = np.concatenate([vals, rnd])
+    x = np.clip(x, -fmax, fmax) if mode == "mxfp4" else x
+    n = (len(x) // 31) * 31
+    W = np.concatenate([x[:n].reshape(-1, 31), np.full((n // 31, 1), fmax, np.float32)], axis=1)
+    q, s, _, dq = grid.rtn_quantize_mxfp(_cuda(W), mode)
+    oq, os_, _, odq = ogrid.rtn_quantize_mxfp(W, mode)
+    np.testing.assert_array_equal(s.cpu().numpy(), os_)
+    np.testing.assert_array_equal(q.cpu().numpy(), oq)
+    np.testing.assert_array_equal(dq.cpu().numpy().view(np.uint32), odq.view(np.uint32))
