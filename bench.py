@@ -328,6 +328,21 @@ def run_reference_arm(args, ws, rank):
     print(json.dumps(line), flush=True)
 
 
+def moe_routing(tokens, experts, topk, seed, device):
+    """C3 router: softmax logits N(0,1) + per-expert Zipf(1.1) bias -1.1*ln(rank), top-k.
+    Returns (token_idx int32 [tokens*topk] grouped by expert, offsets int64 [E+1] on CPU)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    rank = torch.randperm(experts, generator=g, device=device).float() + 1.0
+    logits = torch.randn(tokens, experts, generator=g, device=device) - 1.1 * torch.log(rank)
+    top = logits.topk(topk, dim=1).indices.reshape(-1)
+    order = torch.sort(top, stable=True).indices
+    token_idx = (order // topk).to(torch.int32)
+    counts = torch.bincount(top, minlength=experts).cpu()
+    offsets = torch.zeros(experts + 1, dtype=torch.int64)
+    offsets[1:] = torch.cumsum(counts, 0)
+    return token_idx, offsets
+
+
 def profile_case(case, device):
     """Small, self-contained launches for ncu captures (a few launches, inputs > L2)."""
     from mlx_gptq_b200 import hessian_accumulate, layer
@@ -355,6 +370,37 @@ def profile_case(case, device):
             b.record()
             b.synchronize()
             print(f"solve launch {i}: {a.elapsed_time(b):.3f} ms ({W.numel() / a.elapsed_time(b) / 1e6:.2f} G elems/s)")
+    elif case == "moe":
+        from mlx_gptq_b200 import hessian_grouped
+
+        T, E, K, I = 524288, 128, 2048, 768
+        X = (torch.randn(T, K, generator=torch.Generator(device=device).manual_seed(1), device=device)
+             .to(torch.bfloat16))
+        token_idx, offsets = moe_routing(T, E, 8, 2, device)
+        cnt = (offsets[1:] - offsets[:-1])
+        print(f"routed slots {int(offsets[-1])}, tokens/expert min {int(cnt.min())} median "
+              f"{int(cnt.median())} max {int(cnt.max())} zero {int((cnt == 0).sum())}")
+        H = torch.empty(E, K, K, device=device)
+        flop = 2.0 * float((cnt.double() * K * K).sum())
+        for i in range(3):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            hessian_grouped(X, token_idx, offsets, E, H=H)
+            b.record()
+            b.synchronize()
+            print(f"grouped hessian launch {i}: {a.elapsed_time(b):.3f} ms, {flop / a.elapsed_time(b) / 1e9:.1f} "
+                  f"TFLOP/s (2*N_e*C^2 summed over experts)")
+        W = (torch.randn(E, 2 * I, K, generator=torch.Generator(device=device).manual_seed(0), device=device)
+             * 0.02).to(torch.bfloat16)
+        for i in range(3):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            f = layer.mxfp_factors(H)
+            layer.solve_mxfp_packed(W, f, "mxfp4", "groupwise", torch.bfloat16, True, check_info=False)
+            b.record()
+            b.synchronize()
+            print(f"batched solve (128 experts gate_up, groupwise) {i}: {a.elapsed_time(b):.3f} ms, "
+                  f"{W.numel() / a.elapsed_time(b) / 1e6:.1f} G elems/s")
     else:
         raise SystemExit(f"unknown profile case {case}")
     torch.cuda.synchronize()
@@ -369,7 +415,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--profile-case", choices=["hessian", "solve"], default=None,
+    ap.add_argument("--profile-case", choices=["hessian", "solve", "moe"], default=None,
                     help="run a small case of one kernel for an ncu capture and exit")
     args = ap.parse_args()
     ws, rank, local = dist_env()

@@ -78,6 +78,21 @@ const char* gq_last_error(void);
 int gq_hessian_bf16(const void* X, int64_t n, int64_t c, int64_t ldx, float* H, int64_t ldh, float alpha,
                     float beta, int32_t* status, void* stream);
 
+/* Per-expert Hessians in one launch:
+ * H[e] = beta * H[e] + alpha * sum over t in token_idx[offsets[e] .. offsets[e+1]) of X[t]^T X[t],
+ * for e < E. X: bf16 [n, c] (ldx % 8 == 0, c % 8 == 0); token_idx: int32 row indices into X;
+ * offsets: int64 [E + 1] (device) and host_offsets (the same values in host memory, used
+ * to plan the launch); H: fp32 [E, c, c]. Experts without tokens get H[e] = beta * H[e].
+ * The routed rows are first copied into zero-padded per-expert segments of the
+ * workspace (gq_hessian_grouped_workspace_size bytes), then one tcgen05 launch covers
+ * every (expert, tile) pair, heaviest experts first.
+ * Replaces the per-expert Stash.hessian calls of mlx_gptq/sequential.py:546-555
+ * (stashes filled by the expert routing of mlx_gptq/capture.py:192-207). */
+size_t gq_hessian_grouped_workspace_size(const int64_t* host_offsets, int64_t E, int64_t c);
+int gq_hessian_grouped_bf16(const void* X, int64_t n, int64_t c, int64_t ldx, const int32_t* token_idx,
+                            const int64_t* offsets, const int64_t* host_offsets, int64_t E, float* H, float alpha,
+                            float beta, void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
+
 /* ------------------------------------------------------------------------
  * Solver pieces (mlx_gptq/gptq.py)
  * ------------------------------------------------------------------------ */
@@ -92,8 +107,9 @@ int gq_dead_columns(float* H, int64_t B, int64_t C, uint8_t* dead, void* stream)
  * escalated x10 per block on failure, at most 6 attempts (gptq.py:27-66 as
  * called per group by gptq.py:99-100).
  * H: fp32 [B, C, C] (C % 32 == 0); U: fp32 [B, C/32, 32, 32];
- * info: int32 [B, C/32], 0 = factored, else 1 + number of failed attempts (7 =
- * gave up); damp_used: fp32 [B, C/32] (nullable). */
+ * info: int32 [B, C/32], 0 = factored (possibly after escalation), 1 = not
+ * positive definite after 6 attempts, 2 = the inverse could not be factored;
+ * damp_used: fp32 [B, C/32] damping factor that succeeded (nullable). */
 int gq_mx_prepare_hinv(const float* H, int64_t B, int64_t C, float damp, float* U, int32_t* info,
                        float* damp_used, void* stream);
 

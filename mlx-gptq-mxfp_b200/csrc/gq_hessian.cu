@@ -19,7 +19,9 @@
 // fp32 registers with round-to-nearest adds. Error stays ~2e-6 relative, the
 // tensor pipe never waits, and no extra memory traffic is generated.
 // Pipeline: 4 stages x (A 128x64 + B 256x64 bf16) = 192 KB of shared memory.
+#include <algorithm>
 #include <mutex>
+#include <vector>
 
 #include "gq_common.cuh"
 
@@ -51,9 +53,14 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Grouped form: `sched` (nullable) lists one entry per CTA, expert * tiles_per_expert +
+// tile (heaviest experts first); expert e's rows are X rows seg[e] .. seg[e+1] (a
+// multiple of 64, zero-padded by the gather pass) and its output is H + e*c*ldh.
+// Dense form (sched == nullptr): one expert, rows 0 .. n.
 __global__ void __launch_bounds__(THREADS, 1)
     hessian_kernel(const __grid_constant__ CUtensorMap tmap, int64_t n, int64_t c, float* __restrict__ H,
-                   int64_t ldh, float alpha, float beta, int32_t* status) {
+                   int64_t ldh, float alpha, float beta, int32_t* status, const int32_t* __restrict__ sched,
+                   const int64_t* __restrict__ seg, int64_t tiles_per_expert) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
@@ -65,7 +72,14 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t mt = (c + BM - 1) / BM;
-  int64_t t = blockIdx.x, tn = 0;
+  int64_t t = blockIdx.x, tn = 0, y0 = 0;
+  if (sched) {
+    const int64_t v = sched[blockIdx.x], e = v / tiles_per_expert;
+    t = v % tiles_per_expert;
+    y0 = seg[e];
+    n = seg[e + 1] - y0;
+    H += e * c * ldh;
+  }
   while (t >= tiles_in_panel(tn, mt)) {
     t -= tiles_in_panel(tn, mt);
     ++tn;
@@ -102,7 +116,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, status)) break;
         mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
         uint8_t* st = smem + s * STAGE_BYTES;
-        const int y = kt * BK;
+        const int y = int(y0) + kt * BK;
         const int xa = int(tm * BM), xb = int(tn * BN);
         tma_load_2d(st, &tmap, xa, y, &full[s]);
         tma_load_2d(st + BOX_BYTES, &tmap, xa + 64, y, &full[s]);
@@ -167,7 +181,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
     }
-    if (ok && !*abort_flag && KT > 0) {
+    if (ok && !*abort_flag) {  // KT == 0 (an expert without tokens): writes beta * H
       const int64_t gr = tm * BM + qw * 32 + lane;
       const int64_t cb = tn * BN + half * 128;
       const bool all_upper = tn * BN > tm * BM + BM - 1;
@@ -270,6 +284,116 @@ int make_x_map(CUtensorMap* map, const void* X, int64_t rows, int64_t cols, int6
 
 using namespace gq;
 
+namespace gq {
+namespace hess {
+// Copy each expert's routed rows into a contiguous, 64-row-padded segment:
+// dst rows seg[e] .. seg[e+1] = X[token_idx[offsets[e] ..]] then zeros.
+__global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ X, int64_t c, int64_t ldx,
+                                   const int32_t* __restrict__ token_idx, const int64_t* __restrict__ offsets,
+                                   const int64_t* __restrict__ seg, int64_t E, int64_t total,
+                                   __nv_bfloat16* __restrict__ dst) {
+  const int64_t row = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= total) return;
+  int64_t lo = 0, hi = E;  // find e with seg[e] <= row < seg[e+1]
+  while (hi - lo > 1) {
+    const int64_t mid = (lo + hi) >> 1;
+    if (seg[mid] <= row) lo = mid; else hi = mid;
+  }
+  const int64_t local = row - seg[lo];
+  const int64_t cnt = offsets[lo + 1] - offsets[lo];
+  uint4* d = reinterpret_cast<uint4*>(dst + row * c);
+  const int64_t nvec = c / 8;
+  if (local < cnt) {
+    const uint4* src = reinterpret_cast<const uint4*>(X + int64_t(token_idx[offsets[lo] + local]) * ldx);
+    for (int64_t i = lane; i < nvec; i += 32) d[i] = src[i];
+  } else {
+    for (int64_t i = lane; i < nvec; i += 32) d[i] = make_uint4(0, 0, 0, 0);
+  }
+}
+
+struct GroupedPlan {
+  std::vector<int64_t> seg;     // E + 1 padded row starts
+  std::vector<int32_t> sched;   // one entry per CTA
+  int64_t total = 0;            // padded rows
+};
+
+static GroupedPlan plan_grouped(const int64_t* host_offsets, int64_t E, int64_t c) {
+  GroupedPlan p;
+  p.seg.resize(E + 1);
+  p.seg[0] = 0;
+  for (int64_t e = 0; e < E; ++e) {
+    const int64_t cnt = host_offsets[e + 1] - host_offsets[e];
+    p.seg[e + 1] = p.seg[e] + (cnt + BK - 1) / BK * BK;
+  }
+  p.total = p.seg[E];
+  const int64_t tpe = num_tiles(c);
+  std::vector<int64_t> order(E);
+  for (int64_t e = 0; e < E; ++e) order[e] = e;
+  std::stable_sort(order.begin(), order.end(), [&](int64_t a, int64_t b) {
+    return (p.seg[a + 1] - p.seg[a]) > (p.seg[b + 1] - p.seg[b]);
+  });
+  p.sched.reserve(E * tpe);
+  for (int64_t e : order)
+    for (int64_t t = 0; t < tpe; ++t) p.sched.push_back(int32_t(e * tpe + t));
+  return p;
+}
+}  // namespace hess
+}  // namespace gq
+
+static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+extern "C" size_t gq_hessian_grouped_workspace_size(const int64_t* host_offsets, int64_t E, int64_t c) {
+  if (!host_offsets || E <= 0 || c <= 0) return 0;
+  int64_t total = 0;
+  for (int64_t e = 0; e < E; ++e) total += (host_offsets[e + 1] - host_offsets[e] + 63) / 64 * 64;
+  return align256(size_t(total) * size_t(c) * 2) + align256(size_t(E + 1) * 8) +
+         align256(size_t(E) * size_t(gq::hess::num_tiles(c)) * 4);
+}
+
+extern "C" int gq_hessian_grouped_bf16(const void* X, int64_t n, int64_t c, int64_t ldx, const int32_t* token_idx,
+                                       const int64_t* offsets, const int64_t* host_offsets, int64_t E, float* H,
+                                       float alpha, float beta, void* workspace, size_t workspace_bytes,
+                                       int32_t* status, void* stream) {
+  GQ_REQUIRE(H && offsets && host_offsets && E > 0, "gq_hessian_grouped_bf16: null pointer or E <= 0");
+  GQ_REQUIRE(c > 0 && c % 8 == 0 && ldx >= c && ldx % 8 == 0, "gq_hessian_grouped_bf16: c, ldx must be multiples of 8");
+  GQ_REQUIRE(aligned16(H), "gq_hessian_grouped_bf16: H must be 16-byte aligned");
+  for (int64_t e = 0; e < E; ++e)
+    GQ_REQUIRE(host_offsets[e + 1] >= host_offsets[e], "gq_hessian_grouped_bf16: offsets must be non-decreasing");
+  GQ_REQUIRE(host_offsets[0] == 0, "gq_hessian_grouped_bf16: offsets[0] must be 0");
+  const size_t need = gq_hessian_grouped_workspace_size(host_offsets, E, c);
+  GQ_REQUIRE(workspace && workspace_bytes >= need && aligned16(workspace),
+             "gq_hessian_grouped_bf16: workspace too small (%zu < %zu)", workspace_bytes, need);
+  GQ_REQUIRE(host_offsets[E] == 0 || (X && token_idx && aligned16(X)), "gq_hessian_grouped_bf16: X / token_idx");
+  hess::GroupedPlan plan = hess::plan_grouped(host_offsets, E, c);
+  GQ_REQUIRE(plan.total < (int64_t(1) << 31) && int64_t(plan.sched.size()) < (int64_t(1) << 31),
+             "gq_hessian_grouped_bf16: too many rows");
+  cudaStream_t s = (cudaStream_t)stream;
+  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  __nv_bfloat16* Xg = reinterpret_cast<__nv_bfloat16*>(ws);
+  ws += align256(size_t(plan.total) * size_t(c) * 2);
+  int64_t* seg = reinterpret_cast<int64_t*>(ws);
+  ws += align256(size_t(E + 1) * 8);
+  int32_t* sched = reinterpret_cast<int32_t*>(ws);
+  GQ_CUDA_TRY(cudaMemcpyAsync(seg, plan.seg.data(), size_t(E + 1) * 8, cudaMemcpyHostToDevice, s));
+  GQ_CUDA_TRY(cudaMemcpyAsync(sched, plan.sched.data(), plan.sched.size() * 4, cudaMemcpyHostToDevice, s));
+  if (plan.total > 0) {
+    hess::gather_rows_kernel<<<unsigned((plan.total + 7) / 8), 256, 0, s>>>(
+        reinterpret_cast<const __nv_bfloat16*>(X), c, ldx, token_idx, offsets, seg, E, plan.total, Xg);
+    int st = check_launch("gather_rows_kernel");
+    if (st != GQ_OK) return st;
+  }
+  CUtensorMap map;
+  // a map needs at least one row; with no routed rows at all every CTA has KT == 0
+  int st = hess::make_x_map(&map, plan.total > 0 ? (const void*)Xg : workspace, plan.total > 0 ? plan.total : 1, c, c);
+  if (st != GQ_OK) return st;
+  GQ_CUDA_TRY(cudaFuncSetAttribute(hess::hessian_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   int(hess::SMEM_BYTES)));
+  hess::hessian_kernel<<<unsigned(plan.sched.size()), hess::THREADS, hess::SMEM_BYTES, s>>>(
+      map, 0, c, H, c, alpha, beta, status, sched, seg, hess::num_tiles(c));
+  return check_launch("hessian_kernel (grouped)");
+}
+
 extern "C" int gq_hessian_bf16(const void* X, int64_t n, int64_t c, int64_t ldx, float* H, int64_t ldh, float alpha,
                                float beta, int32_t* status, void* stream) {
   GQ_REQUIRE(H && (X || n == 0), "gq_hessian_bf16: null pointer");
@@ -289,6 +413,6 @@ extern "C" int gq_hessian_bf16(const void* X, int64_t n, int64_t c, int64_t ldx,
                                    int(hess::SMEM_BYTES)));
   const int64_t tiles = hess::num_tiles(c);
   hess::hessian_kernel<<<unsigned(tiles), hess::THREADS, hess::SMEM_BYTES, s>>>(map, n, c, H, ldh, alpha, beta,
-                                                                                status);
+                                                                                status, nullptr, nullptr, tiles);
   return check_launch("hessian_kernel");
 }

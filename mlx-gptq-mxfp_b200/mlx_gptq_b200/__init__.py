@@ -6,7 +6,7 @@ the artifact store) backed by hand-written CUDA kernels in libgptq_b200.so.
 """
 
 from . import _lib  # noqa: F401
-from .capture import Stash, hessian_accumulate, hessian_from_rows  # noqa: F401
+from .capture import Stash, hessian_accumulate, hessian_from_rows, hessian_grouped  # noqa: F401
 from .gptq import gptq_quantize, solve_gptq  # noqa: F401
 
 __all__ = ["solve_gptq", "gptq_quantize", "Stash", "hessian_accumulate", "hessian_from_rows"]

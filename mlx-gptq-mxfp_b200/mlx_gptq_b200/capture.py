@@ -44,6 +44,35 @@ def hessian_from_rows(X: torch.Tensor) -> torch.Tensor:
     return hessian_accumulate(X, H, 1.0, 0.0)
 
 
+@torch.no_grad()
+def hessian_grouped(X: torch.Tensor, token_idx: torch.Tensor, offsets: torch.Tensor, num_experts: int,
+                    H: torch.Tensor | None = None, alpha: float = 1.0, beta: float = 0.0) -> torch.Tensor:
+    """Per-expert H[e] = beta*H[e] + alpha * X[rows_e]^T X[rows_e] in one launch, with
+    rows_e = token_idx[offsets[e]:offsets[e+1]] (the per-expert stashes of the reference's
+    capture, as token indices into the layer input X bf16 [n, c] instead of row copies).
+    offsets: int64 [E+1] (any device). Returns H float32 [E, c, c]."""
+    L.require_cuda(X)
+    if X.dtype != torch.bfloat16 or X.dim() != 2:
+        raise ValueError("X must be bfloat16 [n, c]")
+    n, c = X.shape
+    if X.stride(1) != 1 or X.stride(0) % 8 or X.data_ptr() % 16:
+        X = X.contiguous()
+    off_host = offsets.detach().to("cpu", torch.int64).contiguous()
+    if off_host.numel() != num_experts + 1:
+        raise ValueError("offsets must have num_experts + 1 entries")
+    off_dev = off_host.to(X.device)
+    idx = token_idx.to(X.device, torch.int32).contiguous()
+    if H is None:
+        H = torch.empty(num_experts, c, c, dtype=torch.float32, device=X.device)
+    lib = L.lib()
+    ws_bytes = lib.gq_hessian_grouped_workspace_size(off_host.data_ptr(), num_experts, c)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=X.device)
+    L.check(lib.gq_hessian_grouped_bf16(L.ptr(X), n, c, X.stride(0), L.ptr(idx), L.ptr(off_dev),
+                                        off_host.data_ptr(), num_experts, L.ptr(H), float(alpha), float(beta),
+                                        L.ptr(ws), ws.numel(), None, L.stream_ptr(X.device)), "hessian_grouped")
+    return H
+
+
 class Stash:
     """Captured input rows for one logical weight matrix (capture.py:33-79)."""
 
