@@ -314,7 +314,7 @@ def run_reference_arm(args, ws, rank):
     small = {k: v for k, v in wl.items()}
     vals = []
     for i in range(args.warmup + args.steps):
-        r = cpu_baseline(small, n_tokens=2048, n_groups=2)
+        r = cpu_baseline(small, n_tokens=4096, n_groups=4)
         if i >= args.warmup:
             vals.append(r["value"])
     v = statistics.mean(vals)

@@ -1,17 +1,36 @@
-"""Calibration input stashes and the Hessian accumulation (tensor cores).
+"""Calibration input capture and the Hessian accumulation (tensor cores).
 
-Mirrors ``Stash`` of mlx_gptq/capture.py (add / add_sampled / nbytes / hessian
-/ clear). ``Stash.hessian`` forms H = X^T X in float32 with the tcgen05 kernel
-of libgptq_b200.so instead of float32 ``addmm`` per 65,536-row chunk
-(capture.py:68-76); ``hessian_from_rows`` is the same kernel on rows that are
-already in device memory.
+Mirrors mlx_gptq/capture.py of the reference: ``Stash`` (add / add_sampled /
+nbytes / hessian / clear) and ``CaptureManager`` (nn.Linear pre-hooks with
+same-input dedup, fused-expert interception of ``F.linear`` by weight-slice
+data pointer, unrouted-expert backfill, token statistics). Differences, all on
+the B200 side of the boundary:
+
+* stashes keep their rows on the device they were produced on by default
+  (``stash_device=None``) instead of copying every batch to host memory; pass
+  ``stash_device="cpu"`` for the reference's memory profile;
+* ``Stash.hessian`` forms H = X^T X in float32 with the tcgen05 kernel instead of
+  float32 ``addmm`` per 65,536-row chunk (capture.py:68-76);
+* ``CaptureManager.expert_hessians`` builds every expert's Hessian of a fused
+  parameter in one grouped launch.
 """
 
 from __future__ import annotations
 
+import logging
+import re
+from dataclasses import dataclass, field
+
 import torch
+import torch.nn.functional as F
+from torch.overrides import TorchFunctionMode
 
 from . import _lib as L
+
+log = logging.getLogger(__name__)
+
+# 3D expert parameter names understood, per the transformers fused layout (capture.py:30)
+FUSED_EXPERT_PARAMS = ("gate_up_proj", "gate_proj", "up_proj", "down_proj")
 
 
 @torch.no_grad()
@@ -76,9 +95,10 @@ def hessian_grouped(X: torch.Tensor, token_idx: torch.Tensor, offsets: torch.Ten
 class Stash:
     """Captured input rows for one logical weight matrix (capture.py:33-79)."""
 
-    def __init__(self, name: str, in_features: int):
+    def __init__(self, name: str, in_features: int, device=None):
         self.name = name
         self.in_features = in_features
+        self.device = device  # None: keep rows where they were produced
         self.chunks: list[torch.Tensor] = []
         self.tokens = 0
 
@@ -87,8 +107,16 @@ class Stash:
         if rows.shape[-1] != self.in_features:
             raise RuntimeError(
                 f"stash {self.name}: got rows of dim {rows.shape[-1]}, expected {self.in_features}")
-        self.chunks.append(rows.to("cpu", torch.bfloat16))
+        dev = rows.device if self.device is None else torch.device(self.device)
+        same = dev == rows.device and rows.dtype == torch.bfloat16
+        self.chunks.append(rows.clone() if same else rows.to(dev, torch.bfloat16))
         self.tokens += rows.shape[0]
+
+    def rows(self, device) -> torch.Tensor:
+        """All stashed rows as one bf16 [tokens, in_features] tensor on `device`."""
+        if not self.chunks:
+            return torch.empty(0, self.in_features, dtype=torch.bfloat16, device=device)
+        return torch.cat([c.to(device) for c in self.chunks], dim=0)
 
     def add_sampled(self, x: torch.Tensor, max_rows: int):
         """Deterministic, evenly spaced sample of input rows (capture.py:52-63)."""
@@ -123,3 +151,228 @@ class Stash:
 
     def clear(self):
         self.chunks.clear()
+
+
+@dataclass
+class LinearTask:
+    """A plain nn.Linear to quantize; `name` is layer-relative (capture.py:82-87)."""
+    name: str
+    module: torch.nn.Module
+    stash_key: str  # owner stash (may belong to a sibling with the same input)
+
+
+@dataclass
+class FusedExpertTask:
+    """One fused 3D expert parameter [E, out, in] to quantize per expert (capture.py:90-97)."""
+    module_name: str
+    param_name: str
+    param: torch.nn.Parameter
+    num_experts: int
+    stash_keys: list = field(default_factory=list)  # one per expert
+
+
+class CaptureManager:
+    """Owns all stashes and hooks for one decoder layer (capture.py:100-343).
+
+    Same discovery, routing and dedup rules as the reference: nn.Linear modules
+    not matching `exclude_regex` with in_features % group_size == 0 become
+    LinearTasks; 3D parameters named in FUSED_EXPERT_PARAMS become
+    FusedExpertTasks with one stash per expert; q/k/v (gate/up) fed the same
+    tensor in one batch share one stash; fused experts are captured from the
+    ``F.linear`` calls whose weight is one expert's slice."""
+
+    def __init__(self, layer: torch.nn.Module, exclude_regex, group_size: int, stash_device=None):
+        self.layer = layer
+        self.stash_device = stash_device
+        self.stashes: dict[str, Stash] = {}
+        self.linear_tasks: list[LinearTask] = []
+        self.fused_tasks: list[FusedExpertTask] = []
+        self._hooks = []
+        self._ptr_registry: dict[int, str] = {}
+        self._batch_seen: dict[int, tuple] = {}
+        self._fused_modules: dict[str, torch.nn.Module] = {}
+        self._fused_input_stashes: dict[str, Stash] = {}
+        self.fallback_experts: dict[str, str] = {}
+        self._mode = None
+        excl = re.compile(exclude_regex) if exclude_regex else None
+        seen = set()
+        for name, mod in layer.named_modules():
+            if isinstance(mod, torch.nn.Linear):
+                if excl and excl.search(name):
+                    continue
+                if mod.in_features % group_size:
+                    log.warning("skipping %s: in_features %d not divisible by group %d (stays unquantized)",
+                                name, mod.in_features, group_size)
+                    continue
+                self.linear_tasks.append(LinearTask(name, mod, stash_key=name))
+                continue
+            for pname, p in mod.named_parameters(recurse=False):
+                if p.dim() != 3 or pname not in FUSED_EXPERT_PARAMS or (name, pname) in seen:
+                    continue
+                seen.add((name, pname))
+                if p.shape[-1] % group_size:
+                    log.warning("skipping fused %s.%s: in dim %d not divisible by group %d",
+                                name, pname, p.shape[-1], group_size)
+                    continue
+                task = FusedExpertTask(name, pname, p, p.shape[0])
+                for e in range(p.shape[0]):
+                    key = f"{name}.{pname}::e{e}"
+                    task.stash_keys.append(key)
+                    self.stashes[key] = Stash(key, p.shape[-1], stash_device)
+                    self._ptr_registry[p.data_ptr() + e * p.stride(0) * p.element_size()] = key
+                self.fused_tasks.append(task)
+                self._fused_modules[name] = mod
+                if pname in ("gate_up_proj", "gate_proj", "up_proj"):
+                    self._fused_input_stashes.setdefault(name, Stash(f"{name}::all_inputs", p.shape[-1],
+                                                                     stash_device))
+        for t in self.linear_tasks:
+            self.stashes.setdefault(t.name, Stash(t.name, t.module.in_features, stash_device))
+
+    # ---- nn.Linear pre-hooks with same-input dedup (capture.py:167-178) ----
+    def _make_hook(self, task: LinearTask):
+        def hook(mod, args, kwargs=None):
+            x = args[0] if args else kwargs["input"]
+            seen = self._batch_seen.get(id(x))
+            if seen is not None and seen[0] is x:
+                task.stash_key = seen[1]
+                return
+            self._batch_seen[id(x)] = (x, task.stash_key)
+            self.stashes[task.stash_key].add(x)
+        return hook
+
+    def _make_fused_input_hook(self, module_name: str):
+        def hook(mod, args, kwargs=None):
+            x = args[0] if args else kwargs["hidden_states"]
+            self._fused_input_stashes[module_name].add_sampled(x, 64)
+        return hook
+
+    class _ExpertMode(TorchFunctionMode):
+        """Routes F.linear inputs to the stash of the expert slice used as weight (capture.py:192-207)."""
+
+        def __init__(self, mgr):
+            super().__init__()
+            self.mgr = mgr
+
+        def __torch_function__(self, func, types, args=(), kwargs=None):
+            kwargs = kwargs or {}
+            if func is F.linear and len(args) >= 2:
+                w = args[1]
+                if isinstance(w, torch.Tensor) and w.dim() == 2:
+                    key = self.mgr._ptr_registry.get(w.data_ptr())
+                    if key is not None:
+                        st = self.mgr.stashes[key]
+                        if w.shape[-1] == st.in_features:
+                            st.add(args[0])
+            return func(*args, **kwargs)
+
+    def __enter__(self):
+        for t in self.linear_tasks:
+            self._hooks.append(t.module.register_forward_pre_hook(self._make_hook(t)))
+        for name, module in self._fused_modules.items():
+            if name in self._fused_input_stashes:
+                self._hooks.append(module.register_forward_pre_hook(self._make_fused_input_hook(name)))
+        if self._ptr_registry:
+            self._mode = self._ExpertMode(self)
+            self._mode.__enter__()
+        return self
+
+    def __exit__(self, *exc):
+        if self._mode is not None:
+            self._mode.__exit__(*exc)
+            self._mode = None
+        for h in self._hooks:
+            h.remove()
+        self._hooks.clear()
+        self._batch_seen.clear()
+        return False
+
+    def begin_batch(self):
+        self._batch_seen.clear()
+
+    # ---- diagnostics ----
+    def total_stash_bytes(self) -> int:
+        return sum(s.nbytes() for s in self.stashes.values())
+
+    def expert_token_stats(self):
+        """param -> (min, median, max, zero_count) of tokens per expert (capture.py:242-251)."""
+        out = {}
+        for t in self.fused_tasks:
+            counts = sorted(self.stashes[k].tokens for k in t.stash_keys)
+            out[f"{t.module_name}.{t.param_name}"] = (counts[0], counts[len(counts) // 2], counts[-1],
+                                                      sum(1 for c in counts if c == 0))
+        return out
+
+    @torch.no_grad()
+    def backfill_unrouted_experts(self):
+        """Give never-routed experts a bounded sample of the block's real inputs
+        (capture.py:253-326); down-proj inputs come from that expert's own gate/up."""
+        by_module: dict[str, dict[str, FusedExpertTask]] = {}
+        for task in self.fused_tasks:
+            by_module.setdefault(task.module_name, {})[task.param_name] = task
+        backfilled = {}
+        for module_name, tasks in by_module.items():
+            source = self._fused_input_stashes.get(module_name)
+            if source is None or source.tokens == 0:
+                continue
+            input_task = next((tasks[n] for n in ("gate_up_proj", "gate_proj", "up_proj") if n in tasks), None)
+            if input_task is None:
+                continue
+            missing = [e for e, key in enumerate(input_task.stash_keys) if self.stashes[key].tokens == 0]
+            for expert in missing:
+                for task in tasks.values():
+                    if task.param_name == "down_proj":
+                        continue
+                    stash = self.stashes[task.stash_keys[expert]]
+                    for chunk in source.chunks:
+                        stash.add(chunk)
+                    self.fallback_experts[task.stash_keys[expert]] = "all_expert_inputs"
+                down_task = tasks.get("down_proj")
+                if down_task is not None:
+                    down_stash = self.stashes[down_task.stash_keys[expert]]
+                    if "gate_up_proj" in tasks:
+                        gate_up = tasks["gate_up_proj"].param[expert]
+                        for chunk in source.chunks:
+                            gate, up = F.linear(chunk.to(gate_up.device, gate_up.dtype), gate_up).chunk(2, dim=-1)
+                            down_stash.add(F.silu(gate) * up)
+                    elif "gate_proj" in tasks and "up_proj" in tasks:
+                        gw, uw = tasks["gate_proj"].param[expert], tasks["up_proj"].param[expert]
+                        for chunk in source.chunks:
+                            x = chunk.to(gw.device, gw.dtype)
+                            down_stash.add(F.silu(F.linear(x, gw)) * F.linear(x, uw))
+                    if down_stash.tokens:
+                        self.fallback_experts[down_task.stash_keys[expert]] = "all_expert_inputs"
+                backfilled.setdefault(module_name, []).append(expert)
+        return backfilled
+
+    def check_capture_happened(self):
+        """capture.py:328-337: fused experts must have gone through F.linear."""
+        for t in self.fused_tasks:
+            if all(self.stashes[k].tokens == 0 for k in t.stash_keys):
+                raise RuntimeError(
+                    f"No tokens captured for fused experts {t.module_name}.{t.param_name}. "
+                    "The model is probably not using the eager experts implementation; "
+                    "load it with experts_implementation='eager'.")
+
+    def drop_all(self):
+        for s in self.stashes.values():
+            s.clear()
+        for s in self._fused_input_stashes.values():
+            s.clear()
+
+    # ---- Hessians on the tensor cores ----
+    @torch.no_grad()
+    def expert_hessians(self, task: FusedExpertTask, device, experts=None) -> torch.Tensor:
+        """H [len(experts), C, C] float32 for the given experts of a fused task, one
+        grouped launch over their concatenated stash rows."""
+        experts = list(range(task.num_experts)) if experts is None else list(experts)
+        C = task.param.shape[-1]
+        rows, counts = [], []
+        for e in experts:
+            st = self.stashes[task.stash_keys[e]]
+            rows.extend(c.to(device) for c in st.chunks)
+            counts.append(st.tokens)
+        X = torch.cat(rows, 0) if rows else torch.zeros(1, C, dtype=torch.bfloat16, device=device)
+        offsets = torch.zeros(len(experts) + 1, dtype=torch.int64)
+        offsets[1:] = torch.cumsum(torch.tensor(counts, dtype=torch.int64), 0)
+        idx = torch.arange(max(int(offsets[-1]), 1), dtype=torch.int32, device=device)
+        return hessian_grouped(X, idx, offsets, len(experts))

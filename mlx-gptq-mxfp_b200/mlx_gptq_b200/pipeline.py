@@ -1,0 +1,192 @@
+"""Per-layer solve scheduling (mlx_gptq/sequential.py:467-635, Pipeline.solve_layer).
+
+After a CaptureManager forward, ``solve_layer`` quantizes every task of one decoder
+layer and writes the dequantized weights back into it:
+
+* fused experts first: all experts' Hessians of a fused parameter in one grouped
+  tcgen05 launch, then one batched solve over the experts; gate_up rows split
+  into the gate ([0, R/2)) and up ([R/2, R)) artifacts (sequential.py:299-311);
+* then the plain linears, one Hessian per stash shared by its siblings
+  (q/k/v, gate/up: sequential.py:479-487), one solve per linear.
+
+Artifact names and per-tensor metadata follow the reference
+(sequential.py:522-531, 592-604), so the result feeds ArtifactWriter unchanged.
+
+With a torch.distributed process group, experts (and linears) are partitioned
+across ranks by longest-processing-time on their routed token counts; each
+rank solves its share and one all-gather per task hands every rank the codes,
+scales and dequantized weights of all experts (every rank re-forwards the layer,
+rank 0 writes artifacts). Nothing else crosses ranks.
+"""
+
+from __future__ import annotations
+
+import heapq
+import re
+import threading
+from dataclasses import dataclass, field
+
+import torch
+
+from . import _lib as L
+from .capture import CaptureManager, FusedExpertTask
+from .gptq import solve_gptq
+from .grid import MX_GROUP_SIZE
+
+
+@dataclass
+class LayerSolveArgs:
+    bits: int = 4
+    group_size: int = 64
+    mode: str = "affine"
+    mxfp_algorithm: str = "auto"
+    damp: float = 0.01
+    clip: str = "mse"
+    storage_dtype: torch.dtype = torch.bfloat16
+    overrides: list = field(default_factory=list)  # [(compiled regex, bits)]
+
+    def bits_for(self, artifact_name: str) -> int:
+        for pattern, bits in self.overrides:
+            if pattern.search(artifact_name):
+                return bits
+        return self.bits
+
+
+class SolveResult:
+    """artifact name -> (q, scales, biases) on the CPU, plus per-tensor meta (sequential.py:321-330)."""
+
+    def __init__(self):
+        self.tensors = {}
+        self.meta = {}
+        self.lock = threading.Lock()
+
+    def add(self, name, q, s, b, info):
+        with self.lock:
+            self.tensors[name] = (q.cpu(), s.cpu(), None if b is None else b.cpu())
+            self.meta[name] = info
+
+
+def artifact_names_for_fused(layer_prefix: str, task: FusedExpertTask, expert: int):
+    """Raw-checkpoint names of one expert's artifacts (sequential.py:299-311)."""
+    base = f"{layer_prefix}.{task.module_name}"
+    if task.param_name == "gate_up_proj":
+        return [f"{base}.{expert}.gate_proj.weight", f"{base}.{expert}.up_proj.weight"]
+    return [f"{base}.{expert}.{task.param_name}.weight"]
+
+
+def lpt_partition(costs, parts: int):
+    """Longest-processing-time assignment of items to `parts` bins; returns one sorted
+    index list per bin (deterministic: ties broken by item index)."""
+    bins = [[] for _ in range(parts)]
+    heap = [(0.0, p) for p in range(parts)]
+    heapq.heapify(heap)
+    for i in sorted(range(len(costs)), key=lambda i: (-costs[i], i)):
+        load, p = heapq.heappop(heap)
+        bins[p].append(i)
+        heapq.heappush(heap, (load + costs[i], p))
+    return [sorted(b) for b in bins]
+
+
+def _solve_batch(W, H, bits, args: LayerSolveArgs):
+    return solve_gptq(W, H, bits, args.group_size, damp=args.damp, clip=args.clip,
+                      storage_dtype=args.storage_dtype, mode=args.mode, mxfp_algorithm=args.mxfp_algorithm)
+
+
+def _all_gather_rows(t: torch.Tensor, counts, group):
+    """Concatenate per-rank [n_r, ...] tensors (n_r = counts[r]) on every rank."""
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    n_max = max(counts)
+    pad = torch.zeros((n_max,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+    pad[: t.shape[0]] = t
+    out = torch.empty((world * n_max,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+    dist.all_gather_into_tensor(out, pad, group=group)
+    return torch.cat([out[r * n_max: r * n_max + counts[r]] for r in range(world)], 0)
+
+
+@torch.no_grad()
+def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, device, group=None) -> SolveResult:
+    """Quantize every task of a captured layer; returns the artifacts (sequential.py:467-635)."""
+    import torch.distributed as dist
+
+    device = torch.device(device)
+    result = SolveResult()
+    world = dist.get_world_size(group) if group is not None else 1
+    rank = dist.get_rank(group) if group is not None else 0
+
+    for task in mgr.fused_tasks:
+        p = task.param
+        E, R, C = p.shape
+        bits = args.bits_for(artifact_names_for_fused(layer_prefix, task, 0)[0])
+        tokens = [mgr.stashes[k].tokens for k in task.stash_keys]
+        costs = [float(t) * C * C + 3.0 * R * C for t in tokens]  # Hessian + solve work
+        shares = lpt_partition(costs, world)
+        mine = shares[rank]
+        if mine:
+            H = mgr.expert_hessians(task, device, mine)
+            W = p.detach()[mine].to(device)
+            q, s, b, W_dq, rel = _solve_batch(W, H, bits, args)
+            del H
+        else:  # this rank owns no expert of the task: empty shares
+            q = torch.empty(0, R, C, dtype=torch.uint8, device=device)
+            s = torch.empty(0, R, C // args.group_size, dtype=torch.uint8 if args.mode != "affine" else
+                            args.storage_dtype, device=device)
+            b = None if args.mode != "affine" else torch.empty_like(s)
+            W_dq = torch.empty(0, R, C, dtype=torch.float32, device=device)
+            rel = torch.empty(0, dtype=torch.float32, device=device)
+        order = list(mine)
+        if world > 1:
+            counts = [len(x) for x in shares]
+            q = _all_gather_rows(q, counts, group)
+            s = _all_gather_rows(s, counts, group)
+            if b is not None:
+                b = _all_gather_rows(b, counts, group)
+            W_dq = _all_gather_rows(W_dq.to(p.dtype), counts, group)
+            rel = _all_gather_rows(rel, counts, group)
+            order = [e for share in shares for e in share]
+        idx = torch.tensor(order, dtype=torch.long)
+        p.data[idx.to(p.device)] = W_dq.to(p.dtype).to(p.device)
+        for i, e in enumerate(order):
+            names = artifact_names_for_fused(layer_prefix, task, e)
+            if len(names) == 1:
+                halves = [(q[i], s[i], None if b is None else b[i])]
+            else:
+                halves = [(q[i, : R // 2], s[i, : R // 2], None if b is None else b[i, : R // 2]),
+                          (q[i, R // 2:], s[i, R // 2:], None if b is None else b[i, R // 2:])]
+            for nm, (qq, ss, bb) in zip(names, halves):
+                result.add(nm, qq, ss, bb, {
+                    "bits": bits, "group_size": args.group_size, "mode": args.mode, "kind": "expert",
+                    "out_features": qq.shape[0], "in_features": C,
+                    "tokens": mgr.stashes[task.stash_keys[e]].tokens, "rel_err": round(float(rel[i]), 6),
+                    "fallback": mgr.fallback_experts.get(task.stash_keys[e])})
+
+    # plain linears: one Hessian per stash, shared by the siblings that read the same input
+    by_stash: dict[str, list] = {}
+    for t in mgr.linear_tasks:
+        by_stash.setdefault(t.stash_key, []).append(t)
+    keys = sorted(by_stash)
+    costs = [float(mgr.stashes[k].tokens) * mgr.stashes[k].in_features ** 2 for k in keys]
+    my_keys = [keys[i] for i in lpt_partition(costs, world)[rank]]
+    local = {}
+    for key in my_keys:
+        H0 = mgr.stashes[key].hessian(device)
+        for t in by_stash[key]:
+            name = f"{layer_prefix}.{t.name}.weight"
+            bits = args.bits_for(name)
+            W = t.module.weight.detach().to(device, torch.float32).unsqueeze(0)
+            q, s, b, W_dq, rel = _solve_batch(W, H0.clone().unsqueeze(0), bits, args)
+            local[t.name] = (q[0], s[0], None if b is None else b[0], W_dq[0], float(rel[0]), bits)
+    if world > 1:
+        gathered = [None] * world
+        dist.all_gather_object(gathered, {k: tuple(x.cpu() if torch.is_tensor(x) else x for x in v)
+                                          for k, v in local.items()}, group=group)
+        local = {k: v for part in gathered for k, v in part.items()}
+    for t in mgr.linear_tasks:
+        q, s, b, W_dq, rel, bits = local[t.name]
+        t.module.weight.data.copy_(W_dq.to(t.module.weight.dtype).to(t.module.weight.device))
+        result.add(f"{layer_prefix}.{t.name}.weight", q, s, b, {
+            "bits": bits, "group_size": args.group_size, "mode": args.mode, "kind": "linear",
+            "out_features": W_dq.shape[0], "in_features": W_dq.shape[1],
+            "tokens": mgr.stashes[t.stash_key].tokens, "rel_err": round(rel, 6)})
+    return result
