@@ -127,10 +127,14 @@ class Step:
         return outs
 
 
-def hessian_tiles(c, bm=128, bn=256):
-    """128x256 output tiles the Hessian kernel computes (those on/above the diagonal)."""
-    mt, nt = -(-c // bm), -(-c // bn)
-    return sum(min(2 * tn + 2, mt) for tn in range(nt))
+def hessian_executed_elems(c):
+    """Output elements the Hessian kernel computes per launch: 256x256 tiles on or above
+    the diagonal (2-SM kernel, the default), 128x256 ones with GQ_HESSIAN_KERNEL=1sm."""
+    if os.environ.get("GQ_HESSIAN_KERNEL", "2sm").startswith("1"):
+        mt, nt = -(-c // 128), -(-c // 256)
+        return 128 * 256 * sum(min(2 * tn + 2, mt) for tn in range(nt))
+    t = -(-c // 256)
+    return 256 * 256 * t * (t + 1) // 2
 
 
 def launches_per_step():
@@ -347,16 +351,19 @@ def profile_case(case, device):
     """Small, self-contained launches for ncu captures (a few launches, inputs > L2)."""
     from mlx_gptq_b200 import hessian_accumulate, layer
 
-    if case == "hessian":
-        X = student_t_bf16(16384, HIDDEN, 7, device)  # 128 MiB > L2
-        H = torch.empty(HIDDEN, HIDDEN, device=device)
+    if case in ("hessian", "hessian-full"):
+        n, k = (16384, HIDDEN) if case == "hessian" else (TOKENS, INTER)
+        X = student_t_bf16(n, k, 7, device)  # small case: 128 MiB > L2
+        H = torch.empty(k, k, device=device)
         for i in range(4):
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
             hessian_accumulate(X, H, 1.0, 0.0)
             b.record()
             b.synchronize()
-            print(f"hessian launch {i}: {a.elapsed_time(b):.3f} ms")
+            flop = 2.0 * n * k * k
+            print(f"hessian launch {i} [{os.environ.get('GQ_HESSIAN_KERNEL', '1sm')}] N={n} C={k}: "
+                  f"{a.elapsed_time(b):.3f} ms, {flop / a.elapsed_time(b) / 1e9:.1f} TFLOP/s (2*N*C^2)")
     elif case == "solve":
         X = student_t_bf16(8192, HIDDEN, 7, device)
         H = torch.empty(HIDDEN, HIDDEN, device=device)
@@ -415,7 +422,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--profile-case", choices=["hessian", "solve", "moe"], default=None,
+    ap.add_argument("--profile-case", choices=["hessian", "hessian-full", "solve", "moe"], default=None,
                     help="run a small case of one kernel for an ncu capture and exit")
     args = ap.parse_args()
     ws, rank, local = dist_env()
@@ -511,9 +518,9 @@ def main():
     peak_tf, peak_hbm, src = peaks()
     big_ms = statistics.mean(hess_big_ms)
     flop_big = 2.0 * TOKENS * INTER ** 2
-    executed_flop = 2.0 * TOKENS * 128 * 256 * hessian_tiles(INTER)
+    executed_flop = 2.0 * TOKENS * hessian_executed_elems(INTER)
     achieved = flop_big / (big_ms / 1e3) / 1e12
-    roofline = {"kernel": "hessian_kernel (K=11008 launch)", "bound": "tensor", "achieved": achieved,
+    roofline = {"kernel": "hessian2_kernel (2-SM tcgen05, K=11008 launch)", "bound": "tensor", "achieved": achieved,
                 "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved / peak_tf,
                 "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside a long step)",
                 "flop_per_launch": flop_big,

@@ -20,6 +20,7 @@
 // tensor pipe never waits, and no extra memory traffic is generated.
 // Pipeline: 4 stages x (A 128x64 + B 256x64 bf16) = 192 KB of shared memory.
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 #include <vector>
 
@@ -51,6 +52,52 @@ __host__ inline int64_t num_tiles(int64_t c) {
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Write one accumulator row slab: row gr, columns cb .. cb+127 of the tile
+// (acc scaled in place by alpha). Elements on or above the diagonal go to
+// H[gr][col] (= beta*H + value), strictly-above ones also to the mirror H[col][gr];
+// all_upper: every column of the tile is above every row (no masking).
+__device__ __forceinline__ void store_row_slab(float* __restrict__ H, int64_t ldh, int64_t c, int64_t gr,
+                                               int64_t cb, float (&acc)[128], float alpha, float beta,
+                                               bool all_upper) {
+#pragma unroll
+  for (int q4 = 0; q4 < 4; ++q4) {
+    const int64_t c0 = cb + q4 * 32;
+    if (c0 >= c) break;
+    float* v = acc + q4 * 32;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = alpha * v[j];
+    if (gr < c) {
+      float* hp = H + gr * ldh + c0;
+      if (all_upper && c0 + 32 <= c) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+          if (beta != 0.0f) {
+            const float4 h = *reinterpret_cast<const float4*>(hp + j);
+            o.x = beta * h.x + o.x, o.y = beta * h.y + o.y, o.z = beta * h.z + o.z, o.w = beta * h.w + o.w;
+          }
+          *reinterpret_cast<float4*>(hp + j) = o;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int64_t gc = c0 + j;
+          if (gc >= gr && gc < c) hp[j] = beta != 0.0f ? beta * hp[j] + v[j] : v[j];
+        }
+      }
+    }
+    // mirror (strictly lower) part: H[gc][gr] for gc > gr; lanes hold consecutive gr
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int64_t gc = c0 + j;
+      if (gc > gr && gc < c && gr < c) {
+        float* hp = H + gc * ldh + gr;
+        *hp = beta != 0.0f ? beta * *hp + v[j] : v[j];
+      }
+    }
+  }
 }
 
 // Grouped form: `sched` (nullable) lists one entry per CTA, expert * tiles_per_expert +
@@ -183,46 +230,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     if (ok && !*abort_flag) {  // KT == 0 (an expert without tokens): writes beta * H
       const int64_t gr = tm * BM + qw * 32 + lane;
-      const int64_t cb = tn * BN + half * 128;
-      const bool all_upper = tn * BN > tm * BM + BM - 1;
-#pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
-        const int64_t c0 = cb + q4 * 32;
-        if (c0 >= c) break;
-        float* v = acc + q4 * 32;  // scaled in place (each value is used once after this)
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = alpha * v[j];
-        // direct (upper) part: row gr, columns c0..c0+31 with column >= row
-        if (gr < c) {
-          float* hp = H + gr * ldh + c0;
-          if (all_upper && c0 + 32 <= c) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-              if (beta != 0.0f) {
-                const float4 h = *reinterpret_cast<const float4*>(hp + j);
-                o.x = beta * h.x + o.x, o.y = beta * h.y + o.y, o.z = beta * h.z + o.z, o.w = beta * h.w + o.w;
-              }
-              *reinterpret_cast<float4*>(hp + j) = o;
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int64_t gc = c0 + j;
-              if (gc >= gr && gc < c) hp[j] = beta != 0.0f ? beta * hp[j] + v[j] : v[j];
-            }
-          }
-        }
-        // mirror (strictly lower) part: H[gc][gr] for gc > gr; lanes hold consecutive gr
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int64_t gc = c0 + j;
-          if (gc > gr && gc < c && gr < c) {
-            float* hp = H + gc * ldh + gr;
-            *hp = beta != 0.0f ? beta * *hp + v[j] : v[j];
-          }
-        }
-      }
+      store_row_slab(H, ldh, c, gr, tn * BN + half * 128, acc, alpha, beta, tn * BN > tm * BM + BM - 1);
     }
   }
   tc_fence_before();
@@ -230,6 +238,217 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// 2-SM variant: a cluster of two CTAs computes one 256 x 256 tile with
+// tcgen05.mma.cta_group::2 (M = 256). Each CTA loads only its own 128 rows of A
+// and its half (128 columns) of B -- 32 KB per 64-token step instead of 48 KB --
+// so six stages fit in shared memory and hold 50% more MMA work in flight, and
+// L2 reads drop by a third. The even CTA of the pair issues the MMAs; both CTAs'
+// TMA bytes land on its stage barriers; its commits reach both CTAs' barriers.
+// Each CTA drains its own TMEM rows as in the 1-SM kernel.
+// ---------------------------------------------------------------------------
+namespace two {
+constexpr int STAGES = 6;
+constexpr uint32_t HALF_BYTES = 128 * BK * 2;            // 16 KB: 128 channels x 64 tokens
+constexpr uint32_t STAGE_BYTES = 2 * HALF_BYTES;         // A half + B half per CTA
+constexpr size_t SMEM_BYTES = size_t(STAGES) * STAGE_BYTES + 1024 + 512;
+constexpr uint32_t kPeerBitMask = 0xFEFFFFFFu;          // shared::cluster address -> even CTA of the pair
+
+__host__ __device__ inline int64_t tiles(int64_t c) {
+  const int64_t t = (c + 255) / 256;
+  return t * (t + 1) / 2;
+}
+
+__device__ __forceinline__ uint32_t cta_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void tma_load_2sm(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar) & kPeerBitMask)
+      : "memory");
+}
+__device__ __forceinline__ void umma_f16_2sm(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrives on the barrier at this smem offset in both CTAs once the issued MMAs complete.
+__device__ __forceinline__ void umma_commit_2sm(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(uint16_t(3))
+      : "memory");
+}
+}  // namespace two
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    hessian2_kernel(const __grid_constant__ CUtensorMap tmap, int64_t n, int64_t c, float* __restrict__ H,
+                    int64_t ldh, float alpha, float beta, int32_t* status, const int32_t* __restrict__ sched,
+                    const int64_t* __restrict__ seg, int64_t tiles_per_expert) {
+  constexpr int STAGES = two::STAGES;
+  constexpr uint32_t STAGE_BYTES = two::STAGE_BYTES, HALF_BYTES = two::HALF_BYTES;
+  using two::arrive_remote;
+  using two::cluster_sync;
+  using two::cta_rank;
+  using two::mapa;
+  using two::tma_load_2sm;
+  using two::umma_commit_2sm;
+  using two::umma_f16_2sm;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;  // [2] chunk accumulated in TMEM buffer b (both CTAs)
+  uint64_t* tempty = tfull + 2;      // [2] buffer b drained by both CTAs (used in the even CTA)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cta_rank();
+  int64_t q = blockIdx.x >> 1, y0 = 0;
+  if (sched) {
+    const int64_t v = sched[q], e = v / tiles_per_expert;
+    q = v % tiles_per_expert;
+    y0 = seg[e];
+    n = seg[e + 1] - y0;
+    H += e * c * ldh;
+  }
+  // cluster tile q -> (tm, tn), tm <= tn, panel by panel
+  int64_t tn = int64_t((sqrtf(8.0f * float(q) + 1.0f) - 1.0f) * 0.5f);
+  while ((tn + 1) * (tn + 2) / 2 <= q) ++tn;
+  while (tn * (tn + 1) / 2 > q) --tn;
+  const int64_t tm = q - tn * (tn + 1) / 2;
+  const int KT = int((n + BK - 1) / BK);
+  const int NCH = (KT + kChunkTiles - 1) / kChunkTiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 2 * EPI_WARPS);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap)) : "memory");
+      int issued = 0;
+      for (int kt = 0; kt < KT; ++kt) {
+        const int s = kt % STAGES;
+        const uint32_t ph = (kt / STAGES) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, status)) break;
+        if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * STAGE_BYTES);  // both CTAs' bytes
+        uint8_t* st = smem + s * STAGE_BYTES;
+        const int y = int(y0) + kt * BK;
+        const int xa = int(tm * 256 + rank * 128), xb = int(tn * 256 + rank * 128);
+        tma_load_2sm(st, &tmap, xa, y, &full[s]);
+        tma_load_2sm(st + BOX_BYTES, &tmap, xa + 64, y, &full[s]);
+        tma_load_2sm(st + HALF_BYTES, &tmap, xb, y, &full[s]);
+        tma_load_2sm(st + HALF_BYTES + BOX_BYTES, &tmap, xb + 64, y, &full[s]);
+        issued = kt + 1;
+      }
+      if (*abort_flag && rank == 0) {  // let copies already in flight land before the CTA exits
+        volatile int never = 0;
+        for (int kt = issued > STAGES ? issued - STAGES : 0; kt < issued; ++kt)
+          mbar_wait(&full[kt % STAGES], (kt / STAGES) & 1, &never, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(256, BN, true, true);
+      for (int kt = 0; kt < KT; ++kt) {
+        const int ch = kt / kChunkTiles, buf = ch & 1;
+        const bool chunk_start = kt % kChunkTiles == 0;
+        const bool chunk_end = kt % kChunkTiles == kChunkTiles - 1 || kt == KT - 1;
+        if (chunk_start && !mbar_wait(&tempty[buf], ((ch >> 1) & 1) ^ 1, abort_flag, status)) break;
+        const int s = kt % STAGES;
+        const uint32_t ph = (kt / STAGES) & 1;
+        if (!mbar_wait(&full[s], ph, abort_flag, status)) break;
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(smem + s * STAGE_BYTES), b0 = a0 + HALF_BYTES;
+        const uint32_t d = tmem + uint32_t(buf * BN);
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          const uint64_t ad = umma_desc_sw128(a0 + kk * 2048, BOX_BYTES, 1024);
+          const uint64_t bd = umma_desc_sw128(b0 + kk * 2048, BOX_BYTES, 1024);
+          umma_f16_2sm(d, ad, bd, idesc, (!chunk_start || kk != 0) ? 1u : 0u);
+        }
+        umma_commit_2sm(&empty[s]);
+        if (chunk_end) umma_commit_2sm(&tfull[buf]);
+      }
+    }
+  } else {
+    const int qw = warp & 3, half = (warp - 2) >> 2;
+    const uint32_t lane_base = uint32_t(qw * 32) << 16;
+    const uint32_t tempty_even0 = mapa(smem_u32(&tempty[0]), 0), tempty_even1 = mapa(smem_u32(&tempty[1]), 0);
+    float acc[128];
+#pragma unroll
+    for (int j = 0; j < 128; ++j) acc[j] = 0.0f;
+    bool ok = true;
+    for (int ch = 0; ch < NCH; ++ch) {
+      const int buf = ch & 1;
+      ok = mbar_wait(&tfull[buf], (ch >> 1) & 1, abort_flag, status);
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_base + uint32_t(buf * BN + half * 128 + q4 * 32), r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[q4 * 32 + j] = acc[q4 * 32 + j] + __uint_as_float(r[j]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) arrive_remote(buf ? tempty_even1 : tempty_even0);
+    }
+    if (ok && !*abort_flag) {
+      const int64_t gr = tm * 256 + rank * 128 + qw * 32 + lane;
+      store_row_slab(H, ldh, c, gr, tn * 256 + half * 128, acc, alpha, beta, tn > tm);
+    }
+  }
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
   }
 }
 
@@ -318,7 +537,7 @@ struct GroupedPlan {
   int64_t total = 0;            // padded rows
 };
 
-static GroupedPlan plan_grouped(const int64_t* host_offsets, int64_t E, int64_t c) {
+static GroupedPlan plan_grouped(const int64_t* host_offsets, int64_t E, int64_t tpe) {
   GroupedPlan p;
   p.seg.resize(E + 1);
   p.seg[0] = 0;
@@ -327,7 +546,6 @@ static GroupedPlan plan_grouped(const int64_t* host_offsets, int64_t E, int64_t 
     p.seg[e + 1] = p.seg[e] + (cnt + BK - 1) / BK * BK;
   }
   p.total = p.seg[E];
-  const int64_t tpe = num_tiles(c);
   std::vector<int64_t> order(E);
   for (int64_t e = 0; e < E; ++e) order[e] = e;
   std::stable_sort(order.begin(), order.end(), [&](int64_t a, int64_t b) {
@@ -337,6 +555,29 @@ static GroupedPlan plan_grouped(const int64_t* host_offsets, int64_t E, int64_t 
   for (int64_t e : order)
     for (int64_t t = 0; t < tpe; ++t) p.sched.push_back(int32_t(e * tpe + t));
   return p;
+}
+// Kernel choice: 256x256 tiles on CTA pairs (default; ~9% faster at C = 11008), or
+// GQ_HESSIAN_KERNEL=1sm for 128x256 tiles on one CTA each.
+static bool use_2sm() {
+  const char* v = getenv("GQ_HESSIAN_KERNEL");
+  return !(v && v[0] == '1');
+}
+static int64_t tiles_for(int64_t c, bool two_sm) { return two_sm ? two::tiles(c) : num_tiles(c); }
+
+static int launch(const CUtensorMap& map, int64_t n, int64_t c, float* H, int64_t ldh, float alpha, float beta,
+                  int32_t* status, const int32_t* sched, const int64_t* seg, int64_t tpe, int64_t units,
+                  bool two_sm, cudaStream_t s) {
+  if (two_sm) {
+    GQ_CUDA_TRY(cudaFuncSetAttribute(hessian2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     int(two::SMEM_BYTES)));
+    hessian2_kernel<<<unsigned(2 * units), THREADS, two::SMEM_BYTES, s>>>(map, n, c, H, ldh, alpha, beta, status,
+                                                                         sched, seg, tpe);
+    return check_launch("hessian2_kernel");
+  }
+  GQ_CUDA_TRY(cudaFuncSetAttribute(hessian_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(SMEM_BYTES)));
+  hessian_kernel<<<unsigned(units), THREADS, SMEM_BYTES, s>>>(map, n, c, H, ldh, alpha, beta, status, sched, seg,
+                                                              tpe);
+  return check_launch("hessian_kernel");
 }
 }  // namespace hess
 }  // namespace gq
@@ -348,7 +589,7 @@ extern "C" size_t gq_hessian_grouped_workspace_size(const int64_t* host_offsets,
   int64_t total = 0;
   for (int64_t e = 0; e < E; ++e) total += (host_offsets[e + 1] - host_offsets[e] + 63) / 64 * 64;
   return align256(size_t(total) * size_t(c) * 2) + align256(size_t(E + 1) * 8) +
-         align256(size_t(E) * size_t(gq::hess::num_tiles(c)) * 4);
+         align256(size_t(E) * size_t(std::max(gq::hess::num_tiles(c), gq::hess::two::tiles(c))) * 4);
 }
 
 extern "C" int gq_hessian_grouped_bf16(const void* X, int64_t n, int64_t c, int64_t ldx, const int32_t* token_idx,
@@ -365,7 +606,9 @@ extern "C" int gq_hessian_grouped_bf16(const void* X, int64_t n, int64_t c, int6
   GQ_REQUIRE(workspace && workspace_bytes >= need && aligned16(workspace),
              "gq_hessian_grouped_bf16: workspace too small (%zu < %zu)", workspace_bytes, need);
   GQ_REQUIRE(host_offsets[E] == 0 || (X && token_idx && aligned16(X)), "gq_hessian_grouped_bf16: X / token_idx");
-  hess::GroupedPlan plan = hess::plan_grouped(host_offsets, E, c);
+  const bool two_sm = hess::use_2sm();
+  const int64_t tpe = hess::tiles_for(c, two_sm);
+  hess::GroupedPlan plan = hess::plan_grouped(host_offsets, E, tpe);
   GQ_REQUIRE(plan.total < (int64_t(1) << 31) && int64_t(plan.sched.size()) < (int64_t(1) << 31),
              "gq_hessian_grouped_bf16: too many rows");
   cudaStream_t s = (cudaStream_t)stream;
@@ -387,11 +630,7 @@ extern "C" int gq_hessian_grouped_bf16(const void* X, int64_t n, int64_t c, int6
   // a map needs at least one row; with no routed rows at all every CTA has KT == 0
   int st = hess::make_x_map(&map, plan.total > 0 ? (const void*)Xg : workspace, plan.total > 0 ? plan.total : 1, c, c);
   if (st != GQ_OK) return st;
-  GQ_CUDA_TRY(cudaFuncSetAttribute(hess::hessian_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   int(hess::SMEM_BYTES)));
-  hess::hessian_kernel<<<unsigned(plan.sched.size()), hess::THREADS, hess::SMEM_BYTES, s>>>(
-      map, 0, c, H, c, alpha, beta, status, sched, seg, hess::num_tiles(c));
-  return check_launch("hessian_kernel (grouped)");
+  return hess::launch(map, 0, c, H, c, alpha, beta, status, sched, seg, tpe, int64_t(plan.sched.size()), two_sm, s);
 }
 
 extern "C" int gq_hessian_bf16(const void* X, int64_t n, int64_t c, int64_t ldx, float* H, int64_t ldh, float alpha,
@@ -409,10 +648,7 @@ extern "C" int gq_hessian_bf16(const void* X, int64_t n, int64_t c, int64_t ldx,
   CUtensorMap map;
   int st = hess::make_x_map(&map, X, n, c, ldx);
   if (st != GQ_OK) return st;
-  GQ_CUDA_TRY(cudaFuncSetAttribute(hess::hessian_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   int(hess::SMEM_BYTES)));
-  const int64_t tiles = hess::num_tiles(c);
-  hess::hessian_kernel<<<unsigned(tiles), hess::THREADS, hess::SMEM_BYTES, s>>>(map, n, c, H, ldh, alpha, beta,
-                                                                                status, nullptr, nullptr, tiles);
-  return check_launch("hessian_kernel");
+  const bool two_sm = hess::use_2sm();
+  const int64_t tiles = hess::tiles_for(c, two_sm);
+  return hess::launch(map, n, c, H, ldh, alpha, beta, status, nullptr, nullptr, tiles, tiles, two_sm, s);
 }

@@ -12,6 +12,13 @@ pytestmark = pytest.mark.gpu
 HESSIAN_RTOL = 1e-5
 
 
+@pytest.fixture(autouse=True, params=["1sm", "2sm"])
+def hessian_kernel(request, monkeypatch):
+    """Every test runs with both tcgen05 kernels: 128x256 tiles on one SM, 256x256 on a CTA pair."""
+    monkeypatch.setenv("GQ_HESSIAN_KERNEL", request.param)
+    return request.param
+
+
 def _rel(a, b):
     return float((a.double() - b.double()).norm() / b.double().norm())
 
