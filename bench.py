@@ -377,6 +377,24 @@ def profile_case(case, device):
             b.record()
             b.synchronize()
             print(f"solve launch {i}: {a.elapsed_time(b):.3f} ms ({W.numel() / a.elapsed_time(b) / 1e6:.2f} G elems/s)")
+    elif case == "affine":
+        from mlx_gptq_b200 import solve_gptq
+        from mlx_gptq_b200.gptq import _prepare_hinv
+
+        X = student_t_bf16(32768, HIDDEN, 7, device)
+        H = torch.empty(HIDDEN, HIDDEN, device=device)
+        hessian_accumulate(X, H, 1.0, 0.0)
+        W = weights_bf16(HIDDEN, HIDDEN, 8, device).unsqueeze(0)
+        for i in range(3):
+            a, m, b = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            a.record()
+            _prepare_hinv(H.unsqueeze(0).clone(), 0.01)
+            m.record()
+            solve_gptq(W, H.unsqueeze(0).clone(), 4, 64, mode="affine")
+            b.record()
+            b.synchronize()
+            print(f"affine C1 [4096x4096] g64: factor {a.elapsed_time(m):.2f} ms, full solve_gptq "
+                  f"{m.elapsed_time(b):.2f} ms ({W.numel() / m.elapsed_time(b) / 1e6:.2f} G elems/s)")
     elif case == "moe":
         from mlx_gptq_b200 import hessian_grouped
 
@@ -422,7 +440,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--profile-case", choices=["hessian", "hessian-full", "solve", "moe"], default=None,
+    ap.add_argument("--profile-case", choices=["hessian", "hessian-full", "solve", "affine", "moe"], default=None,
                     help="run a small case of one kernel for an ncu capture and exit")
     args = ap.parse_args()
     ws, rank, local = dist_env()
