@@ -136,30 +136,84 @@ __global__ void __launch_bounds__(128) mx_hinv_kernel(const float* __restrict__ 
 // MXFP column loop
 // --------------------------------------------------------------------------
 
-// e^T H e for a 32-vector held in registers (the einsum of gptq.py:123-125, 168).
-// The row index i runs as a rolled loop: the kernel's code stays small enough
-// for the instruction cache, which matters more here than halving the FMAs with
-// the symmetric form (fully unrolled it ran 2x slower). e_i comes from this
-// thread's column of the staging buffer Es, the 32-wide row dot from registers;
-// four partial sums give the FMA pipe independent chains.
-__device__ __forceinline__ float quad32(const float (&e)[32], const float (*Hs)[32], float (*Es)[129], int tid) {
+// ---------------------------------------------------------------------------
+// e^T H_g e on the tensor cores (the einsum of gptq.py:123-125, 168)
+// ---------------------------------------------------------------------------
+// Each warp evaluates the objective of its 32 rows (lane = row) at once:
+// Y = E * H_g with mma.sync m16n8k8 in 3xTF32 (x = hi + lo, hi*hi + hi*lo + lo*hi:
+// about fp32 accuracy, so candidate comparisons behave like the fp32 reference),
+// then obj_r = sum_n Y[r][n] * E[r][n]. Staging strides (40 for E and H, 36 for Y)
+// make every fragment load/store and every row access bank-conflict free.
+constexpr int kES = 40, kYS = 36;
+
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+__device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// S: this warp's staging area (E first, then reused for Y = E*H once E is in
+// fragments); Hhi/Hlo: tf32 split of H_g, row-major, stride kES.
+__device__ __forceinline__ float quad32(const float (&e)[32], float* S, const uint32_t* Hhi, const uint32_t* Hlo,
+                                        int lane) {
 #pragma unroll
-  for (int c = 0; c < 32; ++c) Es[c][tid] = e[c];
-  float obj = 0.0f;
-#pragma unroll 1
-  for (int i = 0; i < 32; ++i) {
-    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+  for (int c = 0; c < 32; ++c) S[c * kES + lane] = e[c];  // column-major E
+  __syncwarp();
+  const int g = lane >> 2, tq = lane & 3;
+  float acc[2][4][4];
 #pragma unroll
-    for (int j = 0; j < 32; j += 4) {
-      const float4 h = *reinterpret_cast<const float4*>(&Hs[i][j]);
-      a0 = fmaf(h.x, e[j], a0);
-      a1 = fmaf(h.y, e[j + 1], a1);
-      a2 = fmaf(h.z, e[j + 2], a2);
-      a3 = fmaf(h.w, e[j + 3], a3);
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) acc[mt][nt][0] = acc[mt][nt][1] = acc[mt][nt][2] = acc[mt][nt][3] = 0.0f;
+#pragma unroll
+  for (int kt = 0; kt < 4; ++kt) {
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      const float* ec = S + (8 * kt + tq) * kES + 16 * mt + g;
+      const float av[4] = {ec[0], ec[8], ec[4 * kES], ec[4 * kES + 8]};
+      uint32_t ahi[4], alo[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        ahi[i] = to_tf32(av[i]);
+        alo[i] = to_tf32(av[i] - __uint_as_float(ahi[i]));
+      }
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        const int o0 = (8 * kt + tq) * kES + 8 * nt + g, o1 = o0 + 4 * kES;
+        mma_tf32(acc[mt][nt], ahi, Hhi[o0], Hhi[o1]);
+        mma_tf32(acc[mt][nt], ahi, Hlo[o0], Hlo[o1]);
+        mma_tf32(acc[mt][nt], alo, Hhi[o0], Hhi[o1]);
+      }
     }
-    obj = fmaf(Es[i][tid], (a0 + a1) + (a2 + a3), obj);
   }
-  return obj;
+  __syncwarp();  // every lane has its E fragments: the area now holds Y
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      float* y = S + (8 * nt + 2 * tq) * kYS + 16 * mt + g;
+      y[0] = acc[mt][nt][0];
+      y[kYS] = acc[mt][nt][1];
+      y[8] = acc[mt][nt][2];
+      y[kYS + 8] = acc[mt][nt][3];
+    }
+  __syncwarp();
+  float o0 = 0.0f, o1 = 0.0f;
+#pragma unroll
+  for (int c = 0; c < 32; c += 2) {
+    o0 = fmaf(S[c * kYS + lane], e[c], o0);
+    o1 = fmaf(S[(c + 1) * kYS + lane], e[c + 1], o1);
+  }
+  __syncwarp();  // staging is reused by the next call
+  return o0 + o1;
 }
 
 // Grid value (without the scale) of w * inv for the mode.
@@ -238,8 +292,6 @@ template <int MODE> struct Codes {
   }
 };
 
-// 3 CTAs per SM (168 registers) measured fastest: occupancy hides the latency of
-// the sequential GPTQ chain better than the extra registers would.
 template <int MODE, bool SAFE, typename Tin, typename Tout>
 __global__ void __launch_bounds__(128, 3) mx_gptq_kernel(const Tin* __restrict__ W, const float* __restrict__ H,
                                                       const float* __restrict__ U, const uint8_t* __restrict__ dead,
@@ -247,9 +299,9 @@ __global__ void __launch_bounds__(128, 3) mx_gptq_kernel(const Tin* __restrict__
                                                       uint8_t* __restrict__ q, uint8_t* __restrict__ qp,
                                                       uint8_t* __restrict__ scales, Tout* __restrict__ wdq,
                                                       float* __restrict__ partials) {
-  __shared__ __align__(16) float Hs[32][32];
+  __shared__ __align__(16) uint32_t Hhi[32 * kES], Hlo[32 * kES];  // tf32 split of H_g
   __shared__ __align__(16) float Us[32][32];
-  __shared__ float Es[32][129];  // per-thread staging of the error vector for quad32
+  __shared__ __align__(16) float Sst[4][32 * kES];  // per-warp staging for quad32
   __shared__ float red[2][4];
   __shared__ uint32_t s_dmask;
   const int64_t G = C / 32;
@@ -259,7 +311,10 @@ __global__ void __launch_bounds__(128, 3) mx_gptq_kernel(const Tin* __restrict__
   const float* Hg = H + (b * C + g * 32) * C + g * 32;
   const float* Ug = U + (b * G + g) * 1024;
   for (int i = tid; i < 1024; i += 128) {
-    Hs[i >> 5][i & 31] = Hg[int64_t(i >> 5) * C + (i & 31)];
+    const float h = Hg[int64_t(i >> 5) * C + (i & 31)];
+    const uint32_t hi = to_tf32(h);
+    Hhi[(i >> 5) * kES + (i & 31)] = hi;
+    Hlo[(i >> 5) * kES + (i & 31)] = to_tf32(h - __uint_as_float(hi));
     Us[i >> 5][i & 31] = Ug[i];
   }
   if (tid < 32) {
@@ -270,11 +325,19 @@ __global__ void __launch_bounds__(128, 3) mx_gptq_kernel(const Tin* __restrict__
   __syncthreads();
   const uint32_t dmask = s_dmask;
   const int64_t r = tile * 128 + tid;
+  const int lane = tid & 31;
+  float* stage = Sst[tid >> 5];
   float num = 0.0f, den = 0.0f;
-  if (r < R) {
-    const int64_t off = (b * R + r) * C + g * 32;
+  const bool active = r < R;  // rows past R run on zeros (the objectives need whole warps)
+  {
+    const int64_t off = (b * R + (active ? r : 0)) * C + g * 32;
     float o[32];
-    load_row32<Tin>(W + off, o);
+    if (active) {
+      load_row32<Tin>(W + off, o);
+    } else {
+#pragma unroll
+      for (int c = 0; c < 32; ++c) o[c] = 0.0f;
+    }
 #pragma unroll
     for (int c = 0; c < 32; ++c) {
       den = fmaf(o[c], o[c], den);
@@ -301,7 +364,7 @@ __global__ void __launch_bounds__(128, 3) mx_gptq_kernel(const Tin* __restrict__
         float err[32];
 #pragma unroll
         for (int c = 0; c < 32; ++c) err[c] = mx_round<MODE>(o[c], inv) * sc - o[c];
-        const float obj = quad32(err, Hs, Es, tid);
+        const float obj = quad32(err, stage, Hhi, Hlo, lane);
         if (t == 0 || obj < best_obj) {
           best_obj = obj;
           best_e = e;
@@ -325,7 +388,7 @@ __global__ void __launch_bounds__(128, 3) mx_gptq_kernel(const Tin* __restrict__
       wv[c] = dq - o[c];
     }
     bool use_gptq = true;
-    if (SAFE) use_gptq = quad32(wv, Hs, Es, tid) <= best_obj;
+    if (SAFE) use_gptq = quad32(wv, stage, Hhi, Hlo, lane) <= best_obj;
     // range guard: |dq| <= max(32 * max|w|, 2^-126), else the RTN baseline
     const float limit = fmaxf(amax * 32.0f, 1.1754943508222875e-38f);
     if (use_gptq) {
@@ -349,7 +412,8 @@ __global__ void __launch_bounds__(128, 3) mx_gptq_kernel(const Tin* __restrict__
       gdq[c] = gv[c] * sc;
       gdq[c + 1] = gv[c + 1] * sc;
     }
-    // outputs
+    // outputs (active rows only)
+    if (active) {
     if (q) {
       uint32_t qw[8];
       if (MODE == GQ_MXFP4) {
@@ -382,6 +446,7 @@ __global__ void __launch_bounds__(128, 3) mx_gptq_kernel(const Tin* __restrict__
         num = fmaf(d, d, num);
       }
     }
+    }  // active
   }
   if (partials) {
     num = warp_sum(num);
