@@ -362,7 +362,7 @@ def profile_case(case, device):
             b.record()
             b.synchronize()
             flop = 2.0 * n * k * k
-            print(f"hessian launch {i} [{os.environ.get('GQ_HESSIAN_KERNEL', '1sm')}] N={n} C={k}: "
+            print(f"hessian launch {i} [{os.environ.get('GQ_HESSIAN_KERNEL', '2sm')}] N={n} C={k}: "
                   f"{a.elapsed_time(b):.3f} ms, {flop / a.elapsed_time(b) / 1e9:.1f} TFLOP/s (2*N*C^2)")
     elif case == "solve":
         X = student_t_bf16(8192, HIDDEN, 7, device)
