@@ -63,6 +63,13 @@ int gq_abi_version(void);
 const char* gq_status_string(int status);
 const char* gq_last_error(void);
 
+/* Self-test of the bounded device waits (no reference counterpart: the
+ * reference has no device code). Launches one CTA that waits, through the same
+ * wait routine as the tcgen05 pipelines, on a barrier phase that nothing
+ * completes; after limit_ns (<= 2 s) the wait gives up, writes GQ_ERR_TIMEOUT to
+ * *status and 1 to *gave_up (both device int32), and the kernel returns. */
+int gq_selftest_wait_timeout(unsigned long long limit_ns, int32_t* status, int32_t* gave_up, void* stream);
+
 /* ------------------------------------------------------------------------
  * Hessian accumulation
  * ------------------------------------------------------------------------ */

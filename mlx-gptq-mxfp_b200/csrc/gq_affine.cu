@@ -193,36 +193,38 @@ __global__ void build_reversed_kernel(const float* __restrict__ H, int64_t C, fl
 
 // Factor the 64x64 diagonal block k of Hr[b] (lower) in shared memory and store
 // its inverse (lower, zeros above) in Dinv[b][k]. Records the failing column.
+// 256 threads as a 16 x 16 grid; each right-looking step costs two barriers
+// (every thread reads the pivot and takes its square root itself).
 __global__ void __launch_bounds__(256) potrf_diag_kernel(float* __restrict__ Hr, int64_t C, int k,
                                                          float* __restrict__ Dinv, FactorState st) {
   __shared__ float S[NB][NB + 1];
   __shared__ float X[NB][NB + 1];
-  __shared__ int fail;
   const int64_t b = blockIdx.x;
   if (st.skip[b] || st.info[b]) return;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
   float* blk = Hr + (b * C + int64_t(k) * NB) * C + int64_t(k) * NB;
-  for (int i = tid; i < NB * NB; i += 256) S[i / NB][i % NB] = blk[int64_t(i / NB) * C + (i % NB)];
-  if (tid == 0) fail = 0;
+  for (int i = tid; i < NB * NB; i += 256) S[i >> 6][i & 63] = blk[int64_t(i >> 6) * C + (i & 63)];
   __syncthreads();
+  int fail = 0;
   for (int kk = 0; kk < NB; ++kk) {
-    if (tid == 0) {
-      const float piv = S[kk][kk];
-      if (!(piv > 0.0f))
-        fail = kk + 1;
-      else
-        S[kk][kk] = sqrtf(piv);
+    const float piv = S[kk][kk];
+    if (!(piv > 0.0f)) {  // uniform: every thread read the same value
+      fail = kk + 1;
+      break;
     }
+    const float d = sqrtf(piv);
+    // column kk below the pivot: L[i][kk] = A[i][kk] / d (row i handled by thread i - kk - 1)
+    const int i = kk + 1 + tid;
+    float lik = 0.0f;
+    if (i < NB) lik = S[i][kk] / d;
+    __syncthreads();  // all reads of column kk done
+    if (i < NB) S[i][kk] = lik;
+    if (tid == 0) S[kk][kk] = d;
     __syncthreads();
-    if (fail) break;
-    const float d = S[kk][kk];
-    if (tid > kk && tid < NB) S[tid][kk] = S[tid][kk] / d;
-    __syncthreads();
-    // trailing update of the lower triangle: rows i > kk, columns kk < j <= i
-    const int m = NB - kk - 1;
-    for (int e = tid; e < m * m; e += 256) {
-      const int i = kk + 1 + e / m, j = kk + 1 + e % m;
-      if (j <= i) S[i][j] = S[i][j] - S[i][kk] * S[j][kk];
+    // trailing lower triangle: rows / columns kk+1 .. 63 on the 16 x 16 thread grid
+    for (int r = kk + 1 + ty; r < NB; r += 16) {
+      const float lr = S[r][kk];
+      for (int c = kk + 1 + tx; c <= r; c += 16) S[r][c] = S[r][c] - lr * S[c][kk];
     }
     __syncthreads();
   }
@@ -230,28 +232,36 @@ __global__ void __launch_bounds__(256) potrf_diag_kernel(float* __restrict__ Hr,
     if (tid == 0) st.info[b] = k * NB + fail;
     return;
   }
-  // write L_kk back (lower) and invert it: thread t < 64 solves column t
+  // write L_kk back (lower); X = L^-1 by right-looking elimination on [L | I]:
+  // for each column kk, X[kk][:] /= L[kk][kk], then X[i][:] -= L[i][kk] * X[kk][:], i > kk
   for (int i = tid; i < NB * NB; i += 256) {
-    const int r = i / NB, c = i % NB;
+    const int r = i >> 6, c = i & 63;
     if (c <= r) blk[int64_t(r) * C + c] = S[r][c];
-  }
-  if (tid < NB) {
-    const int j = tid;
-    for (int i = 0; i < NB; ++i) {
-      float x = 0.0f;
-      if (i == j) {
-        x = 1.0f / S[i][i];
-      } else if (i > j) {
-        float acc = 0.0f;
-        for (int t = j; t < i; ++t) acc = fmaf(S[i][t], X[t][j], acc);
-        x = -acc / S[i][i];
-      }
-      X[i][j] = x;
-    }
+    X[r][c] = r == c ? 1.0f : 0.0f;
   }
   __syncthreads();
+  for (int kk = 0; kk < NB; ++kk) {
+    const float dk = S[kk][kk];
+    float xk[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) xk[u] = X[kk][tx + 16 * u] / dk;
+    __syncthreads();
+    if (ty == 0) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) X[kk][tx + 16 * u] = xk[u];
+    }
+    for (int r = kk + 1 + ty; r < NB; r += 16) {
+      const float l = S[r][kk];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int c = tx + 16 * u;
+        if (c <= kk) X[r][c] = X[r][c] - l * xk[u];
+      }
+    }
+    __syncthreads();
+  }
   float* D = Dinv + (b * (C / NB) + k) * NB * NB;
-  for (int i = tid; i < NB * NB; i += 256) D[i] = X[i / NB][i % NB];
+  for (int i = tid; i < NB * NB; i += 256) D[i] = X[i >> 6][i & 63];
 }
 
 // Panel solve: A[i][k] = A[i][k] * L_kk^-T for block rows i > k (in place, one CTA per block).
@@ -333,22 +343,28 @@ __global__ void escalate_kernel(int64_t B, FactorState st) {
 // affine column loop: one warp per (row, item); block columns [i1, i1 + 32*VPB)
 // ---------------------------------------------------------------------------
 template <int VPL, int VPB>
-__global__ void __launch_bounds__(256) affine_block_kernel(float* __restrict__ W, const float* __restrict__ U,
+__global__ void __launch_bounds__(512) affine_block_kernel(float* __restrict__ W, const float* __restrict__ U,
                                                            int64_t R, int64_t C, int64_t i1, int nslots, int bits,
                                                            int nshrink, int storage, uint8_t* __restrict__ q,
                                                            void* __restrict__ scales, void* __restrict__ biases,
                                                            float* __restrict__ Err) {
   constexpr int G = 32 * VPL, BS = 32 * VPB;
+  constexpr bool kSmemU = VPB <= 4;  // 128 x 128 U block (64 KB) staged in shared memory
   __shared__ float pr[kMaxShrinks], pf[kMaxShrinks];
-  if (threadIdx.x < kMaxShrinks) shrink_factors(threadIdx.x, bits, pr[threadIdx.x], pf[threadIdx.x]);
-  __syncthreads();
+  extern __shared__ float Us[];  // [BS][BS] when kSmemU
   const int lane = threadIdx.x & 31;
   const int64_t b = blockIdx.y;
+  const float* Ug = U + b * C * C + i1 * C + i1;  // U1 = U[i1:i2, i1:i2], row stride C
+  if (threadIdx.x < kMaxShrinks) shrink_factors(threadIdx.x, bits, pr[threadIdx.x], pf[threadIdx.x]);
+  if (kSmemU) {
+    const int n = nslots * 32;
+    for (int i = threadIdx.x; i < n * n; i += blockDim.x) Us[(i / n) * BS + (i % n)] = Ug[int64_t(i / n) * C + (i % n)];
+  }
+  __syncthreads();
   const int64_t r = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (r >= R) return;
   const int64_t ng = C / G;
   float* wrow = W + (b * R + r) * C + i1;
-  const float* Ub = U + b * C * C + i1 * C + i1;  // U1 = U[i1:i2, i1:i2], row stride C
   // nslots = columns in this block / 32 (< VPB only for the last, partial block)
   float w[VPB], dqv[VPB], ev[VPB], qv[VPB];
 #pragma unroll
@@ -375,8 +391,8 @@ __global__ void __launch_bounds__(256) affine_block_kernel(float* __restrict__ W
       const float wj = __shfl_sync(0xFFFFFFFFu, w[k], l);
       float qj;
       const float dq = affine_quant(wj, s, bb, maxq, qj);
-      const float* urow = Ub + int64_t(j) * C;
-      const float e = (wj - dq) / __ldg(urow + j);
+      const float* urow = kSmemU ? Us + j * BS : Ug + int64_t(j) * C;
+      const float e = (wj - dq) / urow[j];
       if (lane == l) {
         dqv[k] = dq;
         ev[k] = e;
@@ -385,7 +401,7 @@ __global__ void __launch_bounds__(256) affine_block_kernel(float* __restrict__ W
 #pragma unroll
       for (int kk = k; kk < VPB; ++kk) {
         const int col = 32 * kk + lane;
-        if (kk < nslots && col > j) w[kk] = w[kk] - e * __ldg(urow + col);
+        if (kk < nslots && col > j) w[kk] = w[kk] - e * urow[col];
       }
     }
   }
@@ -583,14 +599,19 @@ extern "C" int gq_gptq_affine(float* W, const void* W_orig, int w_dtype, const f
   float* Err = reinterpret_cast<float*>(workspace);
   float* partials = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + align256(size_t(B) * R * bs * 4));
   const int nshrink = clip == GQ_CLIP_MSE ? kMaxShrinks : 1;
-  const dim3 cgrid(unsigned((R + 7) / 8), unsigned(B));
+  const dim3 cgrid(unsigned((R + 15) / 16), unsigned(B));  // 16 rows (warps) per CTA
   for (int64_t i1 = 0; i1 < C; i1 += bs) {
     // the last block may be partial (gptq.py:242); it is still a whole number of groups
     const int64_t n = std::min<int64_t>(bs, C - i1);
     const int nslots = int(n / 32);
-#define AB(VPL, VPB)                                                                                                \
-  affine_block_kernel<VPL, VPB><<<cgrid, 256, 0, s>>>(W, U, R, C, i1, nslots, bits, nshrink, storage_dtype, q,     \
-                                                      scales, biases, Err)
+#define AB(VPL, VPB)                                                                                               \
+  do {                                                                                                            \
+    const size_t sm = VPB <= 4 ? size_t(32 * VPB) * (32 * VPB) * 4 : 0;                                            \
+    if (sm) GQ_CUDA_TRY(cudaFuncSetAttribute(affine_block_kernel<VPL, VPB>,                                         \
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm)));               \
+    affine_block_kernel<VPL, VPB><<<cgrid, 512, sm, s>>>(W, U, R, C, i1, nslots, bits, nshrink, storage_dtype, q,  \
+                                                         scales, biases, Err);                                     \
+  } while (0)
     if (bs == 128) {
       switch (group_size) {
         case 32: AB(1, 4); break;

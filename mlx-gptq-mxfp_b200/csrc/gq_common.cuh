@@ -279,10 +279,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity to complete. Gives up after
-// kWaitLimitNs (or as soon as another role of the CTA has given up), raising
-// *abort_flag and recording GQ_ERR_TIMEOUT in *status (device, nullable).
+// limit_ns (kWaitLimitNs by default) or as soon as another role of the CTA has
+// given up, raising *abort_flag and recording GQ_ERR_TIMEOUT in *status (device,
+// nullable).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int32_t* status) {
+                                          int32_t* status, unsigned long long limit_ns = kWaitLimitNs) {
   unsigned long long t0 = 0;
   for (uint32_t it = 0;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -291,7 +292,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
       unsigned long long now = global_ns();
       if (t0 == 0) {
         t0 = now;
-      } else if (now - t0 > kWaitLimitNs) {
+      } else if (now - t0 > limit_ns) {
         *abort_flag = 1;
         if (status) atomicExch(status, GQ_ERR_TIMEOUT);
         return false;

@@ -32,6 +32,7 @@ SIGNATURES = {
     "gq_abi_version": (I32, []),
     "gq_status_string": (ctypes.c_char_p, [I32]),
     "gq_last_error": (ctypes.c_char_p, []),
+    "gq_selftest_wait_timeout": (I32, [ctypes.c_ulonglong, P, P, P]),
     "gq_hessian_bf16": (I32, [P, I64, I64, I64, P, I64, F32, F32, P, P]),
     "gq_hessian_grouped_workspace_size": (SZ, [P, I64, I64]),
     "gq_hessian_grouped_bf16": (I32, [P, I64, I64, I64, P, P, P, I64, P, F32, F32, P, SZ, P, P]),
