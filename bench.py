@@ -432,6 +432,89 @@ def profile_case(case, device):
     print(f"profile case {case} done")
 
 
+# ---------------------------------------------------------------------------
+# C5: Qwen3-30B-A3B-shaped MoE layer stack, layer-sequential, experts sharded over ranks
+# ---------------------------------------------------------------------------
+QWEN3_30B_A3B = dict(model_type="qwen3_moe", vocab_size=151936, hidden_size=2048, intermediate_size=6144,
+                     moe_intermediate_size=768, num_hidden_layers=48, num_attention_heads=32,
+                     num_key_value_heads=4, head_dim=128, num_experts=128, num_experts_per_tok=8,
+                     decoder_sparse_step=1, norm_topk_prob=True, rms_norm_eps=1e-6, rope_theta=1e6,
+                     max_position_embeddings=40960, tie_word_embeddings=False, hidden_act="silu")
+
+
+def run_c5(args, ws, rank, local):
+    """Synthetic Qwen3-30B-A3B stack (random init, seed 0; 256 x 2048 uniform tokens,
+    seed 1) calibrated layer by layer to MXFP4 (safe-scale-search) through the
+    package's Pipeline. Every rank runs the layer forwards; experts and linears are
+    split across ranks; one all-gather per task. Reports the solve stage (Hessians,
+    factors, column loops, all-gather) and the whole layer time, max over ranks."""
+    import types
+
+    from mlx_gptq_b200 import sequential
+
+    device = torch.device("cuda", local)
+    group = None
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
+        group = dist.group.WORLD
+    cfg = dict(QWEN3_30B_A3B)
+    model = sequential.build_model(cfg)
+    src = sequential.SyntheticWeights(model, device, seed=0)
+    sargs = types.SimpleNamespace(devices=[str(device)], dtype="bfloat16", layers_attr="model.layers",
+                                  checkpoint_model_prefix=None, artifact_layers_prefix=None,
+                                  exclude=sequential.DEFAULT_EXCLUDE, group_size=32, bits=4, mode="mxfp4",
+                                  mxfp_algorithm="safe-scale-search", damp=0.01, clip="mse", overrides=[],
+                                  batch_size=args.c5_batch)
+    g = torch.Generator().manual_seed(1)
+    samples = torch.randint(0, cfg["vocab_size"], (args.c5_samples, args.c5_seqlen), generator=g)
+    pipe = sequential.Pipeline(model, src, sargs, group=group)
+    t0 = time.time()
+    pipe.run(samples, writer=None, layers=args.layers)
+    torch.cuda.synchronize()
+    wall = time.time() - t0
+    rows = [[s.capture_s, s.solve_s, s.reforward_s, s.total_s] for s in pipe.stats]
+    t = torch.tensor(rows + [[wall, 0, 0, 0]], dtype=torch.float64, device=device)
+    if group is not None:
+        import torch.distributed as dist
+
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    t = t.cpu().tolist()
+    per_layer, wall = t[:-1], t[-1][0]
+    elems = sum(s.solved_elems for s in pipe.stats)
+    solve_s = sum(r[1] for r in per_layer[1:]) or per_layer[0][1]  # layer 0 carries one-time set-up
+    n_solve = max(1, len(per_layer) - 1) if len(per_layer) > 1 else 1
+    elems_timed = elems / len(per_layer) * n_solve
+    tokens = args.c5_samples * args.c5_seqlen
+    H, I, E, k = cfg["hidden_size"], cfg["moe_intermediate_size"], cfg["num_experts"], cfg["num_experts_per_tok"]
+    qd, kvd = cfg["num_attention_heads"] * cfg["head_dim"], cfg["num_key_value_heads"] * cfg["head_dim"]
+    hess_flop = 2.0 * tokens * (H * H + qd * qd) + 2.0 * tokens * k * (H * H + I * I)
+    line = {"metric": "C5 layer stack: GPTQ-solved weight elems/s (solve stage: Hessians -> codes, all-gather)",
+            "value": elems_timed / solve_s, "unit": "elems/s", "n_gpus": ws, "layers": len(per_layer),
+            "higher_is_better": True, "scaling": "strong (one layer's experts split over ranks)",
+            "dtype": "bf16 x bf16 -> f32 (Hessian), f32 (solve)", "data": "synthetic (random init seed 0, "
+            "uniform tokens seed 1)",
+            "config": {"workload": "C5 Qwen3-30B-A3B-shaped stack, MXFP4 safe-scale-search",
+                       "tokens": tokens, "batch_size": args.c5_batch, "experts_forward": "eager F.linear loop"},
+            "solved_elems_per_layer": elems // len(per_layer),
+            "hessian_tflop_per_layer": hess_flop / 1e12,
+            "solve_ms_per_layer": solve_s / n_solve * 1e3,
+            "layer_s": [round(r[3], 3) for r in per_layer],
+            "capture_s": [round(r[0], 3) for r in per_layer],
+            "solve_s": [round(r[1], 3) for r in per_layer],
+            "reforward_s": [round(r[2], 3) for r in per_layer],
+            "wall_s": wall,
+            "rel_err_median": [round(s.rel_err_median, 5) for s in pipe.stats],
+            "rel_err_max": [round(s.rel_err_max, 5) for s in pipe.stats]}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -442,8 +525,18 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--profile-case", choices=["hessian", "hessian-full", "solve", "affine", "moe"], default=None,
                     help="run a small case of one kernel for an ncu capture and exit")
+    ap.add_argument("--config", choices=["c2", "c5"], default="c2",
+                    help="c2: the headline MLP sweep (default); c5: the synthetic Qwen3-MoE layer stack")
+    ap.add_argument("--layers", type=int, default=2, help="c5: decoder layers to calibrate")
+    ap.add_argument("--c5-samples", type=int, default=256)
+    ap.add_argument("--c5-seqlen", type=int, default=2048)
+    ap.add_argument("--c5-batch", type=int, default=16, help="c5: sequences per forward")
     args = ap.parse_args()
     ws, rank, local = dist_env()
+    if args.config == "c5":
+        torch.cuda.set_device(local)
+        run_c5(args, ws, rank, local)
+        return
     if args.profile_case:
         profile_case(args.profile_case, torch.device("cuda", 0))
         return

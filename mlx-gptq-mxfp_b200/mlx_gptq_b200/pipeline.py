@@ -105,6 +105,18 @@ def _all_gather_rows(t: torch.Tensor, counts, group):
     return torch.cat([out[r * n_max: r * n_max + counts[r]] for r in range(world)], 0)
 
 
+def _agreed_counts(counts, group, device):
+    """Rank 0's token counts on every rank, so that every rank derives the same
+    partition even if the redundant forwards routed a token differently."""
+    import torch.distributed as dist
+
+    if group is None or dist.get_world_size(group) == 1:
+        return list(counts)
+    t = torch.tensor(list(counts), dtype=torch.int64, device=device)
+    dist.broadcast(t, src=dist.get_global_rank(group, 0), group=group)
+    return [int(v) for v in t.tolist()]
+
+
 @torch.no_grad()
 def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, device, group=None) -> SolveResult:
     """Quantize every task of a captured layer; returns the artifacts (sequential.py:467-635)."""
@@ -119,7 +131,7 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
         p = task.param
         E, R, C = p.shape
         bits = args.bits_for(artifact_names_for_fused(layer_prefix, task, 0)[0])
-        tokens = [mgr.stashes[k].tokens for k in task.stash_keys]
+        tokens = _agreed_counts([mgr.stashes[k].tokens for k in task.stash_keys], group, device)
         costs = [float(t) * C * C + 3.0 * R * C for t in tokens]  # Hessian + solve work
         shares = lpt_partition(costs, world)
         mine = shares[rank]
@@ -166,7 +178,8 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
     for t in mgr.linear_tasks:
         by_stash.setdefault(t.stash_key, []).append(t)
     keys = sorted(by_stash)
-    costs = [float(mgr.stashes[k].tokens) * mgr.stashes[k].in_features ** 2 for k in keys]
+    counts = _agreed_counts([mgr.stashes[k].tokens for k in keys], group, device)
+    costs = [float(n) * mgr.stashes[k].in_features ** 2 for n, k in zip(counts, keys)]
     my_keys = [keys[i] for i in lpt_partition(costs, world)[rank]]
     local = {}
     for key in my_keys:

@@ -1,0 +1,476 @@
+"""Layer-sequential Stage A driver (mlx_gptq/sequential.py, Pipeline.run).
+
+The model is a meta-device skeleton; each decoder layer's weights are
+materialized on the forward device right before it is processed and released
+after it. Per layer (sequential.py:680-770):
+
+  1. materialize the layer's weights (from safetensors shards, or a seeded
+     synthetic source for random-init benchmarks);
+  2. forward every calibration batch with capture hooks (CaptureManager);
+  3. solve every weight matrix (pipeline.solve_layer: grouped tcgen05 Hessians,
+     batched factors, GPTQ column loops), writing W_dq back into the layer;
+  4. re-forward to produce the quantized activations for the next layer;
+  5. append the layer's artifacts.
+
+Differences from the reference, all B200-first:
+  * hidden states and per-layer call contexts stay in HBM between layers
+    (a 524,288-token window of hidden 2048 is 2.1 GB) instead of moving to host RAM;
+  * several GPUs are several processes (one per GPU, torch.distributed NCCL):
+    every rank runs the same forward, experts and linears are split across ranks
+    inside solve_layer, and one all-gather per task returns the quantized
+    weights; rank 0 alone writes artifacts. Within a process the first entry of
+    ``args.devices`` is the device.
+"""
+
+from __future__ import annotations
+
+import contextlib
+import json
+import logging
+import os
+import re
+import time
+import zlib
+from dataclasses import dataclass, field
+
+import torch
+
+from .capture import CaptureManager
+from .pipeline import LayerSolveArgs, solve_layer
+
+log = logging.getLogger("mlx_gptq_b200")
+
+DEFAULT_EXCLUDE = r"(^|\.)gate$|(^|\.)router($|\.)|shared_expert_gate|e_score"  # sequential.py:38
+
+
+# ---------------------------------------------------------------------------
+# weight sources
+# ---------------------------------------------------------------------------
+class RawShardIndex:
+    """Name -> shard lookup over a Hugging Face model directory (sequential.py:44-90)."""
+
+    def __init__(self, model_dir: str):
+        self.dir = model_dir
+        idx = os.path.join(model_dir, "model.safetensors.index.json")
+        if os.path.exists(idx):
+            with open(idx) as f:
+                self.weight_map = json.load(f)["weight_map"]
+        else:
+            single = os.path.join(model_dir, "model.safetensors")
+            if not os.path.exists(single):
+                raise FileNotFoundError(f"no safetensors found in {model_dir}")
+            from safetensors import safe_open
+
+            with safe_open(single, framework="pt") as f:
+                self.weight_map = {n: "model.safetensors" for n in f.keys()}
+        self._open = {}
+
+    def _file(self, fname):
+        if fname not in self._open:
+            from safetensors import safe_open
+
+            self._open[fname] = safe_open(os.path.join(self.dir, fname), framework="pt")
+        return self._open[fname]
+
+    def has(self, name: str) -> bool:
+        return name in self.weight_map
+
+    def get(self, name: str) -> torch.Tensor:
+        return self._file(self.weight_map[name]).get_tensor(name)
+
+    def get_rows(self, name: str, rows: list[int]) -> torch.Tensor:
+        return self._file(self.weight_map[name]).get_slice(name)[rows]
+
+    def names_with_prefix(self, prefix: str):
+        return [n for n in self.weight_map if n.startswith(prefix)]
+
+
+class SyntheticWeights:
+    """Seeded random-init stand-in for a checkpoint: every meta parameter or buffer
+    of `model` is produced on demand, on `device`, from its own generator seeded by
+    (seed, name), so every rank and every run sees the same weights. 1-D weights
+    named like norms are ones (RMSNorm init), biases zeros, the rest N(0, std)
+    (the Hugging Face initializer_range default)."""
+
+    def __init__(self, model: torch.nn.Module, device, seed: int = 0, std: float = 0.02):
+        self.device = torch.device(device)
+        self.seed = int(seed)
+        self.std = float(std)
+        self.shapes = {}
+        for n, p in model.named_parameters():
+            if p.is_meta:
+                self.shapes[n] = tuple(p.shape)
+        for n, b in model.named_buffers():
+            if b is not None and b.is_meta:
+                self.shapes[n] = tuple(b.shape)
+
+    def has(self, name: str) -> bool:
+        return name in self.shapes
+
+    def get(self, name: str) -> torch.Tensor:
+        shape = self.shapes[name]
+        leaf = name.rsplit(".", 1)[-1]
+        if leaf == "bias":
+            return torch.zeros(shape, dtype=torch.float32, device=self.device)
+        if len(shape) == 1 and ("norm" in name or "layernorm" in name):
+            return torch.ones(shape, dtype=torch.float32, device=self.device)
+        g = torch.Generator(device=self.device)
+        g.manual_seed((self.seed * 1_000_003 + zlib.crc32(name.encode())) & 0x7FFF_FFFF_FFFF)
+        return torch.randn(shape, generator=g, dtype=torch.float32, device=self.device).mul_(self.std)
+
+
+@contextlib.contextmanager
+def empty_weights():
+    """Build modules with parameters on the meta device and real buffers, the state
+    calibrate.build_model gets from init_empty_weights(include_buffers=False)."""
+    orig = torch.nn.Module.register_parameter
+
+    def register(module, name, param):
+        orig(module, name, param)
+        if param is not None and not param.is_meta:
+            p = module._parameters[name]
+            module._parameters[name] = torch.nn.Parameter(p.to("meta"), requires_grad=p.requires_grad)
+
+    torch.nn.Module.register_parameter = register
+    try:
+        yield
+    finally:
+        torch.nn.Module.register_parameter = orig
+
+
+def build_model(model_or_config, dtype: torch.dtype = torch.bfloat16):
+    """Meta-parameter skeleton of a Hugging Face causal LM with the eager expert loop
+    (calibrate.py:29-57): a model directory, a config dict, or a PretrainedConfig."""
+    from transformers import AutoConfig, AutoModelForCausalLM, PretrainedConfig
+
+    if isinstance(model_or_config, PretrainedConfig):
+        config = model_or_config
+    elif isinstance(model_or_config, dict):
+        cfg = dict(model_or_config)
+        config = AutoConfig.for_model(cfg.pop("model_type"), **cfg)
+    else:
+        config = AutoConfig.from_pretrained(model_or_config)
+    config._experts_implementation = "eager"  # F.linear per expert: the capture path
+    with empty_weights():
+        model = AutoModelForCausalLM.from_config(config, dtype=dtype, attn_implementation="sdpa")
+    model.eval()
+    model.config.use_cache = False
+    return model
+
+
+def materialize_module(module: torch.nn.Module, prefix: str, shards, device, dtype) -> None:
+    """Fill a meta module's parameters and buffers from `shards` (sequential.py:93-145),
+    fusing per-expert checkpoint tensors into the runtime 3-D layout
+    (X.gate_up_proj [E, 2I, H] <- X.{e}.gate_proj / X.{e}.up_proj; X.down_proj [E, H, I])."""
+    sd = {}
+    for pname, p in module.named_parameters():
+        raw = f"{prefix}.{pname}"
+        if shards.has(raw):
+            t = shards.get(raw)
+            sd[pname] = (t.to(dtype) if t.is_floating_point() else t).to(device)
+            continue
+        m = re.match(r"^(.*)\.(gate_up_proj|gate_proj|up_proj|down_proj)$", pname)
+        if m and p.dim() == 3:
+            base, kind = m.groups()
+            fused = torch.empty(p.shape, dtype=dtype, device=device)
+            for e in range(p.shape[0]):
+                if kind == "gate_up_proj":
+                    g = shards.get(f"{prefix}.{base}.{e}.gate_proj.weight")
+                    u = shards.get(f"{prefix}.{base}.{e}.up_proj.weight")
+                    fused[e, : g.shape[0]] = g.to(dtype)
+                    fused[e, g.shape[0]:] = u.to(dtype)
+                else:
+                    fused[e] = shards.get(f"{prefix}.{base}.{e}.{kind}.weight").to(dtype)
+            sd[pname] = fused
+            continue
+        raise KeyError(f"cannot materialize parameter {prefix}.{pname} from checkpoint")
+    for bname, b in module.named_buffers():
+        raw = f"{prefix}.{bname}"
+        if shards.has(raw):
+            v = shards.get(raw)
+            sd[bname] = (v.to(dtype) if v.is_floating_point() else v).to(device)
+        elif b.is_meta:
+            raise KeyError(f"meta buffer {prefix}.{bname} not in checkpoint")
+        else:
+            sd[bname] = b.to(device)
+    module.load_state_dict(sd, strict=False, assign=True)
+    for n, p in module.named_parameters():
+        if p.is_meta:
+            raise RuntimeError(f"parameter {prefix}.{n} still on meta after materialize")
+
+
+def free_module(module: torch.nn.Module):
+    """Release a layer's weights by putting it back on meta (sequential.py:148-150)."""
+    module.to_empty(device="meta")
+
+
+# ---------------------------------------------------------------------------
+# layer-0 inputs and per-layer call contexts
+# ---------------------------------------------------------------------------
+class _CatchDone(Exception):
+    pass
+
+
+class Catcher(torch.nn.Module):
+    """Stands in for every decoder layer during one model call and records the
+    layer-0 hidden states and each layer's (args, kwargs) (sequential.py:253-268)."""
+
+    def __init__(self, store, layer_idx: int, stop: bool = False):
+        super().__init__()
+        self.store = store
+        self.layer_idx = layer_idx
+        self.stop = stop
+
+    def forward(self, hidden_states, *args, **kwargs):
+        if self.layer_idx == 0:
+            self.store["hidden"] = hidden_states.detach().clone()
+        self.store["contexts"][self.layer_idx] = (args, kwargs)
+        if self.stop:
+            raise _CatchDone
+        return hidden_states
+
+
+def _detach_context(value, memo):
+    """Detach the tensors of a layer call context, copying tuples, lists and dicts
+    but keeping each object's identity shared across layers (one memo per batch):
+    a container that layer i mutates and layer i+1 reads stays one object
+    (sequential.py:271-293). Tensors stay on the forward device."""
+    key = id(value)
+    if key in memo:
+        return memo[key]
+    if isinstance(value, torch.Tensor):
+        out = value.detach()
+    elif isinstance(value, tuple):
+        out = tuple(_detach_context(v, memo) for v in value)
+    elif isinstance(value, list):
+        out = [_detach_context(v, memo) for v in value]
+    elif isinstance(value, dict):
+        out = {k: _detach_context(v, memo) for k, v in value.items()}
+    else:
+        out = value
+    memo[key] = out
+    return out
+
+
+# ---------------------------------------------------------------------------
+# the driver
+# ---------------------------------------------------------------------------
+@dataclass
+class LayerStats:
+    layer: int
+    linears: int
+    experts: int
+    capture_s: float
+    solve_s: float
+    reforward_s: float
+    total_s: float
+    solved_elems: int
+    rel_err_median: float
+    rel_err_max: float
+    extra: dict = field(default_factory=dict)
+
+
+class Pipeline:
+    """Layer-sequential calibration over a meta-skeleton model (sequential.py:345-770).
+
+    `args` carries the calibrate CLI fields: devices, dtype, layers_attr,
+    checkpoint_model_prefix, artifact_layers_prefix, exclude, group_size, bits,
+    mode, mxfp_algorithm, damp, clip, overrides, batch_size (and optionally
+    vram_gb). `group` is a torch.distributed process group whose ranks share the
+    solves (None: this process alone)."""
+
+    def __init__(self, model, shards, args, group=None):
+        self.model = model
+        self.shards = shards
+        self.args = args
+        self.group = group
+        self.dev0 = torch.device(args.devices[0])
+        self.dtype = torch.bfloat16 if args.dtype == "bfloat16" else torch.float16
+        self.storage_dtype = self.dtype
+        inner = model
+        for attr in args.layers_attr.split(".")[:-1]:
+            inner = getattr(inner, attr)
+        for module in model.modules():
+            for name, buf in module.named_buffers(recurse=False):
+                if buf is not None and not buf.is_meta:
+                    setattr(module, name, buf.to(self.dev0))
+        self.inner = inner
+        self.layers = getattr(inner, args.layers_attr.split(".")[-1])
+        self.runtime_model_prefix = args.layers_attr.split(".", 1)[0]
+        self.checkpoint_model_prefix = args.checkpoint_model_prefix or self.runtime_model_prefix
+        self.checkpoint_layers_prefix_fmt = self._checkpoint_name(args.layers_attr) + ".{}"
+        self.artifact_layers_prefix_fmt = (args.artifact_layers_prefix or args.layers_attr) + ".{}"
+        self.stats: list[LayerStats] = []
+
+    @property
+    def rank(self) -> int:
+        if self.group is None:
+            return 0
+        import torch.distributed as dist
+
+        return dist.get_rank(self.group)
+
+    def _checkpoint_name(self, runtime_name: str) -> str:
+        if runtime_name == self.runtime_model_prefix:
+            return self.checkpoint_model_prefix
+        prefix = self.runtime_model_prefix + "."
+        if runtime_name.startswith(prefix):
+            return self.checkpoint_model_prefix + runtime_name[len(self.runtime_model_prefix):]
+        return runtime_name
+
+    def _sync(self):
+        if self.dev0.type == "cuda":
+            torch.cuda.synchronize(self.dev0)
+
+    # ---- layer-0 inputs ----
+    @torch.no_grad()
+    def catch_layer0_inputs(self, samples: torch.Tensor, batch_size: int):
+        """Layer-0 hidden states and every layer's call context per batch
+        (sequential.py:353-418); kept on the forward device."""
+        emb = self.model.get_input_embeddings()
+        emb_name = next(n for n, m in self.model.named_modules() if m is emb)
+        materialize_module(emb, self._checkpoint_name(emb_name), self.shards, self.dev0, self.dtype)
+        batches = []
+        original = list(self.layers)
+        try:
+            for i in range(0, samples.shape[0], batch_size):
+                captured = {"hidden": None, "contexts": [None] * len(self.layers)}
+                for li in range(len(self.layers)):
+                    self.layers[li] = Catcher(captured, li, stop=li == len(self.layers) - 1)
+                ids = samples[i: i + batch_size].to(self.dev0)
+                try:
+                    self.model(input_ids=ids, use_cache=False)
+                except _CatchDone:
+                    pass
+                if captured["hidden"] is None or any(c is None for c in captured["contexts"]):
+                    raise RuntimeError("catcher did not observe every decoder layer")
+                memo = {}
+                contexts = [(_detach_context(args, memo), {k: _detach_context(v, memo) for k, v in kwargs.items()})
+                            for args, kwargs in captured["contexts"]]
+                batches.append((captured["hidden"], contexts))
+        finally:
+            for li, layer in enumerate(original):
+                self.layers[li] = layer
+        free_module(emb)
+        if not batches:
+            raise RuntimeError("catcher captured nothing; layers_attr wrong?")
+        return batches
+
+    # ---- one layer ----
+    @torch.no_grad()
+    def forward_layer(self, layer, batches, layer_idx, capture_mgr=None):
+        """Run every batch through `layer`; returns the new hidden states (sequential.py:422-437)."""
+        outs = []
+        for hid, contexts in batches:
+            if capture_mgr is not None:
+                capture_mgr.begin_batch()
+            args, kwargs = contexts[layer_idx]
+            out = layer(hid.to(self.dev0, self.dtype), *args, **kwargs)
+            if isinstance(out, tuple):
+                out = out[0]
+            outs.append(out.detach())
+        return outs
+
+    def solve_args(self) -> LayerSolveArgs:
+        a = self.args
+        return LayerSolveArgs(bits=a.bits, group_size=a.group_size, mode=a.mode,
+                              mxfp_algorithm=getattr(a, "mxfp_algorithm", "auto"), damp=a.damp, clip=a.clip,
+                              storage_dtype=self.storage_dtype, overrides=list(getattr(a, "overrides", []) or []))
+
+    @torch.no_grad()
+    def solve_layer(self, layer_idx: int, mgr: CaptureManager):
+        prefix = self.artifact_layers_prefix_fmt.format(layer_idx)
+        return solve_layer(prefix, mgr, self.solve_args(), self.dev0, group=self.group)
+
+    @torch.no_grad()
+    def apply_precomputed(self, layer, layer_idx: int, reader) -> None:
+        """Resume: write dequantized artifacts into a layer (sequential.py:637-679)."""
+        from .grid import dequantize_artifact
+
+        prefix = self.artifact_layers_prefix_fmt.format(layer_idx)
+        for name, mod in layer.named_modules():
+            if isinstance(mod, torch.nn.Linear):
+                art = f"{prefix}.{name}.weight"
+                if reader.has(art):
+                    q, s, b, info = reader.get(art)
+                    dq = dequantize_artifact(q.to(self.dev0), s.to(self.dev0), None if b is None else b.to(self.dev0),
+                                             info.get("mode", "affine"), info["group_size"])
+                    mod.weight.data.copy_(dq.reshape(q.shape).to(mod.weight.dtype))
+            for pname, p in mod.named_parameters(recurse=False):
+                if p.dim() != 3 or pname not in ("gate_up_proj", "gate_proj", "up_proj", "down_proj"):
+                    continue
+                E, R, _ = p.shape
+                for e in range(E):
+                    if pname == "gate_up_proj":
+                        arts = [f"{prefix}.{name}.{e}.gate_proj.weight", f"{prefix}.{name}.{e}.up_proj.weight"]
+                        rows = [(0, R // 2), (R // 2, R)]
+                    else:
+                        arts, rows = [f"{prefix}.{name}.{e}.{pname}.weight"], [(0, R)]
+                    for art, (r0, r1) in zip(arts, rows):
+                        if not reader.has(art):
+                            continue
+                        q, s, b, info = reader.get(art)
+                        dq = dequantize_artifact(q.to(self.dev0), s.to(self.dev0),
+                                                 None if b is None else b.to(self.dev0),
+                                                 info.get("mode", "affine"), info["group_size"])
+                        p.data[e, r0:r1].copy_(dq.reshape(q.shape).to(p.dtype))
+
+    # ---- orchestration ----
+    def run(self, samples: torch.Tensor, writer=None, reader_for_resume=None, layers=None):
+        """Calibrate every decoder layer (or the first `layers`) in order
+        (sequential.py:683-770). Only rank 0 writes artifacts."""
+        t_start = time.time()
+        batches = self.catch_layer0_inputs(samples, self.args.batch_size)
+        log.info("caught %d forward batches for layer 0", len(batches))
+        n_layers = len(self.layers) if layers is None else min(int(layers), len(self.layers))
+        for li in range(n_layers):
+            layer = self.layers[li]
+            prefix = self.checkpoint_layers_prefix_fmt.format(li)
+            t0 = time.time()
+            materialize_module(layer, prefix, self.shards, self.dev0, self.dtype)
+            if writer is not None and writer.layer_done(li):
+                self.apply_precomputed(layer, li, reader_for_resume)
+                new = self.forward_layer(layer, batches, li)
+                batches = [(h, ctx) for h, (_, ctx) in zip(new, batches)]
+                free_module(layer)
+                log.info("layer %d: resumed from artifacts (%.1fs)", li, time.time() - t0)
+                continue
+
+            mgr = CaptureManager(layer, self.args.exclude, self.args.group_size, stash_device=self.dev0)
+            n_lin = len(mgr.linear_tasks)
+            n_exp = sum(t.num_experts for t in mgr.fused_tasks)
+            with mgr:
+                self.forward_layer(layer, batches, li, capture_mgr=mgr)
+            if mgr.fused_tasks:
+                mgr.check_capture_happened()
+                for pname, (mn, med, mx, zeros) in mgr.expert_token_stats().items():
+                    log.info("layer %d %s tokens/expert min=%d med=%d max=%d zero=%d", li, pname, mn, med, mx, zeros)
+                for module_name, experts in mgr.backfill_unrouted_experts().items():
+                    log.warning("layer %d %s: activation-backfilled unrouted experts %s", li, module_name, experts)
+            self._sync()
+            t_cap = time.time()
+
+            result = self.solve_layer(li, mgr)
+            mgr.drop_all()
+            self._sync()
+            t_solve = time.time()
+
+            new = self.forward_layer(layer, batches, li)
+            batches = [(h, ctx) for h, (_, ctx) in zip(new, batches)]
+            self._sync()
+            t_fwd = time.time()
+            free_module(layer)
+            if self.dev0.type == "cuda":
+                torch.cuda.empty_cache()
+            if writer is not None and self.rank == 0:
+                writer.write_layer(li, result.tensors, result.meta)
+            errs = sorted(m["rel_err"] for m in result.meta.values())
+            elems = sum(int(m["out_features"]) * int(m["in_features"]) for m in result.meta.values())
+            st = LayerStats(li, n_lin, n_exp, t_cap - t0, t_solve - t_cap, t_fwd - t_solve, time.time() - t0, elems,
+                            errs[len(errs) // 2] if errs else -1.0, errs[-1] if errs else -1.0)
+            self.stats.append(st)
+            log.info("layer %d done: %d linears + %d experts | rel_err med=%.4f max=%.4f | capture %.1fs "
+                     "solve %.1fs reforward %.1fs total %.1fs", li, n_lin, n_exp, st.rel_err_median,
+                     st.rel_err_max, st.capture_s, st.solve_s, st.reforward_s, st.total_s)
+        log.info("%d layers done in %.1f min", n_layers, (time.time() - t_start) / 60)
+        return batches

@@ -1,0 +1,238 @@
+"""Layer-sequential driver host logic (CPU, no kernels).
+
+Mirrors what the reference's tests/test_sequential_context.py pins (checkpoint
+buffers materialized, per-layer positional/keyword call contexts preserved with
+shared containers) and runs a tiny Qwen3-MoE skeleton end to end with the GPU
+solver replaced by a deterministic fake: artifact names and metadata follow the
+reference, and a 2-rank gloo run equals the single-process run.
+"""
+
+import os
+import types
+
+import pytest
+import torch
+
+from mlx_gptq_b200 import sequential
+from mlx_gptq_b200.sequential import Pipeline, SyntheticWeights, materialize_module
+
+TINY_QWEN3_MOE = dict(model_type="qwen3_moe", vocab_size=512, hidden_size=64, intermediate_size=128,
+                      moe_intermediate_size=32, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                      head_dim=16, num_experts=8, num_experts_per_tok=2, decoder_sparse_step=1, norm_topk_prob=True,
+                      max_position_embeddings=256)
+
+
+class ContextLayer(torch.nn.Module):
+    def __init__(self, layer_idx, observations):
+        super().__init__()
+        self.layer_idx = layer_idx
+        self.observations = observations
+
+    def forward(self, hidden_states, per_layer_input, shared_state, layer_tag):
+        self.observations.append((self.layer_idx, per_layer_input.clone(), layer_tag, dict(shared_state)))
+        shared_state[self.layer_idx] = layer_tag
+        return hidden_states + per_layer_input
+
+
+class ContextModel(torch.nn.Module):
+    def __init__(self, observations):
+        super().__init__()
+        self.embed_tokens = torch.nn.Embedding(16, 4)
+        self.layers = torch.nn.ModuleList([ContextLayer(0, observations), ContextLayer(1, observations)])
+
+    def get_input_embeddings(self):
+        return self.embed_tokens
+
+    def forward(self, input_ids, use_cache=False):
+        h = self.embed_tokens(input_ids)
+        shared = {}
+        for i, layer in enumerate(self.layers):
+            h = layer(h, torch.full_like(h, i + 1), shared_state=shared, layer_tag=f"layer-{i}")
+        return h
+
+
+class FakeShards:
+    def __init__(self, tensors):
+        self.tensors = tensors
+
+    def has(self, name):
+        return name in self.tensors
+
+    def get(self, name):
+        return self.tensors[name]
+
+
+def _args(**kw):
+    base = dict(devices=["cpu"], dtype="bfloat16", layers_attr="model.layers", checkpoint_model_prefix=None,
+                artifact_layers_prefix=None, exclude=sequential.DEFAULT_EXCLUDE, group_size=32, bits=4,
+                mode="mxfp4", mxfp_algorithm="safe-scale-search", damp=0.01, clip="mse", overrides=[],
+                batch_size=2)
+    base.update(kw)
+    return types.SimpleNamespace(**base)
+
+
+def test_materialize_module_loads_non_meta_checkpoint_buffers():
+    module = torch.nn.Linear(2, 2, bias=False, device="meta")
+    module.register_buffer("layer_scalar", torch.ones(1))
+    materialize_module(module, "layer", FakeShards({"layer.weight": torch.eye(2),
+                                                   "layer.layer_scalar": torch.tensor([3.0])}),
+                       "cpu", torch.bfloat16)
+    assert module.weight.device.type == "cpu" and module.weight.dtype == torch.bfloat16
+    assert module.layer_scalar.item() == 3.0
+
+
+def test_materialize_fuses_per_expert_checkpoint_tensors():
+    class Experts(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.gate_up_proj = torch.nn.Parameter(torch.empty(3, 4, 2, device="meta"))
+            self.down_proj = torch.nn.Parameter(torch.empty(3, 2, 2, device="meta"))
+
+    m = Experts()
+    raw = {}
+    for e in range(3):
+        raw[f"x.{e}.gate_proj.weight"] = torch.full((2, 2), float(e))
+        raw[f"x.{e}.up_proj.weight"] = torch.full((2, 2), 10.0 + e)
+        raw[f"x.{e}.down_proj.weight"] = torch.full((2, 2), 20.0 + e)
+    # parameters live directly on the module: prefix "x" and names "gate_up_proj"/"down_proj"
+    wrapper = torch.nn.Module()
+    wrapper.experts = m
+    raw = {k.replace("x.", "w.experts.", 1): v for k, v in raw.items()}
+    materialize_module(wrapper, "w", FakeShards(raw), "cpu", torch.float32)
+    for e in range(3):
+        assert (m.gate_up_proj[e, :2] == e).all() and (m.gate_up_proj[e, 2:] == 10 + e).all()
+        assert (m.down_proj[e] == 20 + e).all()
+    with pytest.raises(KeyError):
+        materialize_module(torch.nn.Linear(2, 2, device="meta"), "missing", FakeShards({}), "cpu", torch.float32)
+
+
+def test_capture_preserves_positional_and_per_layer_context(monkeypatch):
+    observations = []
+    model = ContextModel(observations)
+    pipe = Pipeline(model, shards=None, args=_args(layers_attr="layers"))
+    monkeypatch.setattr(sequential, "materialize_module", lambda *a, **k: None)
+    monkeypatch.setattr(sequential, "free_module", lambda *a, **k: None)
+    batches = pipe.catch_layer0_inputs(torch.tensor([[1, 2, 3]]), batch_size=1)
+    assert observations == [] and len(batches) == 1
+    hidden, contexts = batches[0]
+    assert len(contexts) == 2
+    assert torch.equal(contexts[0][0][0], torch.ones_like(hidden))
+    assert torch.equal(contexts[1][0][0], torch.full_like(hidden, 2))
+    assert contexts[0][1]["layer_tag"] == "layer-0" and contexts[1][1]["layer_tag"] == "layer-1"
+    assert contexts[0][1]["shared_state"] is contexts[1][1]["shared_state"]
+    for i, layer in enumerate(model.layers):
+        batches[0] = (pipe.forward_layer(layer, batches, i)[0], contexts)
+    assert [o[2] for o in observations] == ["layer-0", "layer-1"]
+    assert observations[0][3] == {} and observations[1][3] == {0: "layer-0"}
+    assert torch.allclose(batches[0][0].float(), hidden.float() + 3, atol=0.02, rtol=0)
+
+
+def test_synthetic_weights_are_seeded_per_name():
+    model = sequential.build_model(TINY_QWEN3_MOE)
+    a, b = SyntheticWeights(model, "cpu", seed=0), SyntheticWeights(model, "cpu", seed=0)
+    c = SyntheticWeights(model, "cpu", seed=1)
+    name = "model.layers.0.mlp.experts.gate_up_proj"
+    assert a.has(name) and a.get(name).shape == (8, 64, 64)
+    assert torch.equal(a.get(name), b.get(name)) and not torch.equal(a.get(name), c.get(name))
+    assert not torch.equal(a.get(name), a.get("model.layers.1.mlp.experts.gate_up_proj"))
+    assert (a.get("model.layers.0.input_layernorm.weight") == 1).all()
+    assert abs(float(a.get(name).std()) - 0.02) < 0.002
+    assert not a.has("model.rotary_emb.inv_freq")  # real buffer, kept
+
+
+def _fake_solver(monkeypatch):
+    from test_pipeline_cpu import _fake_expert_hessians, _fake_solve, _fake_stash_hessian
+
+    from mlx_gptq_b200 import capture, pipeline
+
+    monkeypatch.setattr(pipeline, "_solve_batch", _fake_solve)
+    monkeypatch.setattr(capture.CaptureManager, "expert_hessians", _fake_expert_hessians)
+    monkeypatch.setattr(capture.Stash, "hessian", _fake_stash_hessian)
+
+
+class _Writer:
+    def __init__(self):
+        self.layers = {}
+
+    def layer_done(self, i):
+        return False
+
+    def write_layer(self, i, tensors, meta):
+        self.layers[i] = (tensors, meta)
+
+
+def test_tiny_qwen3_moe_stack_names_and_stats(monkeypatch):
+    _fake_solver(monkeypatch)
+    model = sequential.build_model(TINY_QWEN3_MOE)
+    pipe = Pipeline(model, SyntheticWeights(model, "cpu", seed=0), _args())
+    samples = torch.randint(0, 512, (4, 32), generator=torch.Generator().manual_seed(1))
+    w = _Writer()
+    pipe.run(samples, w)
+    assert sorted(w.layers) == [0, 1]
+    tensors, meta = w.layers[0]
+    names = set(meta)
+    for p in ("q_proj", "k_proj", "v_proj", "o_proj"):
+        assert f"model.layers.0.self_attn.{p}.weight" in names
+    for e in range(8):
+        for p in ("gate_proj", "up_proj", "down_proj"):
+            assert f"model.layers.0.mlp.experts.{e}.{p}.weight" in names
+    assert not any(".mlp.gate." in n for n in names)  # router excluded
+    assert len(names) == 4 + 3 * 8
+    assert meta["model.layers.0.mlp.experts.0.gate_proj.weight"]["out_features"] == 32
+    assert meta["model.layers.0.mlp.experts.0.down_proj.weight"]["in_features"] == 32
+    assert sum(meta[f"model.layers.0.mlp.experts.{e}.gate_proj.weight"]["tokens"] for e in range(8)) >= 4 * 32 * 2
+    assert [s.layer for s in pipe.stats] == [0, 1] and pipe.stats[0].experts == 16
+    # layers go back to meta after processing
+    assert all(p.is_meta for p in model.model.layers[0].parameters())
+
+
+def _run_stack(rank, world, port, out_dir):
+    import sys
+
+    import torch.distributed as dist
+
+    sys.path.insert(0, os.path.dirname(__file__))
+    from test_pipeline_cpu import _fake_expert_hessians, _fake_solve, _fake_stash_hessian
+
+    from mlx_gptq_b200 import capture, pipeline
+
+    pipeline._solve_batch = _fake_solve
+    capture.CaptureManager.expert_hessians = _fake_expert_hessians
+    capture.Stash.hessian = _fake_stash_hessian
+    group = None
+    if world > 1:
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+        group = dist.group.WORLD
+    model = sequential.build_model(TINY_QWEN3_MOE)
+    pipe = Pipeline(model, SyntheticWeights(model, "cpu", seed=0), _args(), group=group)
+    samples = torch.randint(0, 512, (4, 32), generator=torch.Generator().manual_seed(1))
+    w = _Writer()
+    out = pipe.run(samples, w)
+    torch.save({"layers": w.layers, "hidden": [h for h, _ in out]}, os.path.join(out_dir, f"s{world}_{rank}.pt"))
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def test_sharded_stack_matches_single_process(tmp_path):
+    import socket
+
+    import torch.multiprocessing as mp
+
+    _run_stack(0, 1, 0, str(tmp_path))
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    mp.start_processes(_run_stack, args=(2, port, str(tmp_path)), nprocs=2, start_method="spawn")
+    ref = torch.load(tmp_path / "s1_0.pt")
+    r0 = torch.load(tmp_path / "s2_0.pt")
+    r1 = torch.load(tmp_path / "s2_1.pt")
+    assert r1["layers"] == {}  # only rank 0 writes
+    assert sorted(r0["layers"]) == sorted(ref["layers"])
+    for li, (tensors, meta) in ref["layers"].items():
+        t2, m2 = r0["layers"][li]
+        assert m2 == meta
+        for k, (q, s, b) in tensors.items():
+            assert torch.equal(q, t2[k][0]) and torch.equal(s, t2[k][1])
+    for got in (r0, r1):
+        for h, h_ref in zip(got["hidden"], ref["hidden"]):
+            assert torch.equal(h, h_ref)
