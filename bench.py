@@ -468,7 +468,7 @@ def run_c5(args, ws, rank, local):
                                   checkpoint_model_prefix=None, artifact_layers_prefix=None,
                                   exclude=sequential.DEFAULT_EXCLUDE, group_size=32, bits=4, mode="mxfp4",
                                   mxfp_algorithm="safe-scale-search", damp=0.01, clip="mse", overrides=[],
-                                  batch_size=args.c5_batch)
+                                  batch_size=args.c5_batch, experts_forward=args.c5_experts_forward)
     g = torch.Generator().manual_seed(1)
     samples = torch.randint(0, cfg["vocab_size"], (args.c5_samples, args.c5_seqlen), generator=g)
     pipe = sequential.Pipeline(model, src, sargs, group=group)
@@ -501,7 +501,10 @@ def run_c5(args, ws, rank, local):
             "dtype": "bf16 x bf16 -> f32 (Hessian), f32 (solve)", "data": "synthetic (random init seed 0, "
             "uniform tokens seed 1)",
             "config": {"workload": "C5 Qwen3-30B-A3B-shaped stack, MXFP4 safe-scale-search",
-                       "tokens": tokens, "batch_size": args.c5_batch, "experts_forward": "eager F.linear loop"},
+                       "tokens": tokens, "batch_size": args.c5_batch,
+                       "experts_forward": {"grouped": "sort-based, bit-identical to the eager loop",
+                                           "eager": "eager F.linear loop"}[args.c5_experts_forward],
+                       "artifacts": "kept on the device, not written to disk"},
             "solved_elems_per_layer": elems // len(per_layer),
             "hessian_tflop_per_layer": hess_flop / 1e12,
             "solve_ms_per_layer": solve_s / n_solve * 1e3,
@@ -510,6 +513,8 @@ def run_c5(args, ws, rank, local):
             "solve_s": [round(r[1], 3) for r in per_layer],
             "reforward_s": [round(r[2], 3) for r in per_layer],
             "wall_s": wall,
+            "solve_stages_s_rank0": [{k: round(v, 4) for k, v in s.extra.get("solve_stages_s", {}).items()}
+                                     for s in pipe.stats],
             "rel_err_median": [round(s.rel_err_median, 5) for s in pipe.stats],
             "rel_err_max": [round(s.rel_err_max, 5) for s in pipe.stats]}
     print(json.dumps(line), flush=True)
@@ -531,6 +536,7 @@ def main():
     ap.add_argument("--c5-samples", type=int, default=256)
     ap.add_argument("--c5-seqlen", type=int, default=2048)
     ap.add_argument("--c5-batch", type=int, default=16, help="c5: sequences per forward")
+    ap.add_argument("--c5-experts-forward", choices=["grouped", "eager"], default="grouped")
     args = ap.parse_args()
     ws, rank, local = dist_env()
     if args.config == "c5":

@@ -193,6 +193,9 @@ class CaptureManager:
         self._fused_modules: dict[str, torch.nn.Module] = {}
         self._fused_input_stashes: dict[str, Stash] = {}
         self.fallback_experts: dict[str, str] = {}
+        self._segments: dict[str, list] = {}  # module -> per-batch (hidden, tok, counts, acts)
+        self._segment_modules: set[str] = set()
+        self._mode_registry: dict[int, str] = {}
         self._mode = None
         excl = re.compile(exclude_regex) if exclude_regex else None
         seen = set()
@@ -258,20 +261,39 @@ class CaptureManager:
             if func is F.linear and len(args) >= 2:
                 w = args[1]
                 if isinstance(w, torch.Tensor) and w.dim() == 2:
-                    key = self.mgr._ptr_registry.get(w.data_ptr())
+                    key = self.mgr._mode_registry.get(w.data_ptr())
                     if key is not None:
                         st = self.mgr.stashes[key]
                         if w.shape[-1] == st.in_features:
                             st.add(args[0])
             return func(*args, **kwargs)
 
+    def _make_segment_sink(self, module_name: str):
+        tasks = [t for t in self.fused_tasks if t.module_name == module_name]
+
+        def sink(hidden, tok, counts, acts):
+            self._segments.setdefault(module_name, []).append((hidden.detach().clone(), tok.to(torch.int32),
+                                                               list(counts), acts))
+            for t in tasks:
+                for e, n in enumerate(counts):
+                    self.stashes[t.stash_keys[e]].tokens += n
+        return sink
+
     def __enter__(self):
+        from .experts import uses_grouped
+
         for t in self.linear_tasks:
             self._hooks.append(t.module.register_forward_pre_hook(self._make_hook(t)))
         for name, module in self._fused_modules.items():
             if name in self._fused_input_stashes:
                 self._hooks.append(module.register_forward_pre_hook(self._make_fused_input_hook(name)))
-        if self._ptr_registry:
+            if uses_grouped(module):
+                # sort-based forward: rows arrive as token indices + activation segments
+                module._gq_sink = self._make_segment_sink(name)
+                self._segment_modules.add(name)
+        skip = {k for t in self.fused_tasks if t.module_name in self._segment_modules for k in t.stash_keys}
+        self._mode_registry = {p: k for p, k in self._ptr_registry.items() if k not in skip}
+        if self._mode_registry:
             self._mode = self._ExpertMode(self)
             self._mode.__enter__()
         return self
@@ -280,6 +302,8 @@ class CaptureManager:
         if self._mode is not None:
             self._mode.__exit__(*exc)
             self._mode = None
+        for name in self._segment_modules:
+            self._fused_modules[name].__dict__.pop("_gq_sink", None)
         for h in self._hooks:
             h.remove()
         self._hooks.clear()
@@ -291,7 +315,9 @@ class CaptureManager:
 
     # ---- diagnostics ----
     def total_stash_bytes(self) -> int:
-        return sum(s.nbytes() for s in self.stashes.values())
+        seg = sum(h.numel() * h.element_size() + t.numel() * 4 + (0 if a is None else a.numel() * a.element_size())
+                  for segs in self._segments.values() for h, t, _, a in segs)
+        return sum(s.nbytes() for s in self.stashes.values()) + seg
 
     def expert_token_stats(self):
         """param -> (min, median, max, zero_count) of tokens per expert (capture.py:242-251)."""
@@ -358,21 +384,80 @@ class CaptureManager:
             s.clear()
         for s in self._fused_input_stashes.values():
             s.clear()
+        self._segments.clear()
+
+    # ---- rows of one expert, wherever they were captured ----
+    def _segment_source(self, task: FusedExpertTask, device):
+        """(X, idx, offsets) for a segment-captured task: X holds the source rows
+        (the module inputs for gate/up, the activations for down_proj), idx [S]
+        int32 the rows of X grouped by expert (batch order, then slot order, as the
+        eager stash would hold them), offsets [E+1] host ints. None if the task's
+        module was captured through F.linear interception."""
+        segs = self._segments.get(task.module_name)
+        if not segs:
+            return None
+        E = task.num_experts
+        down = task.param_name == "down_proj"
+        parts, ids, experts = [], [], []
+        base = 0
+        for hidden, tok, counts, acts in segs:
+            src = acts if down else hidden
+            parts.append(src.to(device))
+            ids.append((torch.arange(tok.shape[0], device=device, dtype=torch.int64) if down
+                        else tok.to(device, torch.int64)) + base)
+            experts.append(torch.repeat_interleave(torch.arange(E, device=device),
+                                                   torch.tensor(counts, device=device)))
+            base += src.shape[0]
+        X = torch.cat(parts, 0)
+        perm = torch.argsort(torch.cat(experts), stable=True)
+        idx = torch.cat(ids)[perm].to(torch.int32)
+        totals = [sum(c[2][e] for c in segs) for e in range(E)]
+        offsets = [0]
+        for n in totals:
+            offsets.append(offsets[-1] + n)
+        return X, idx, offsets
+
+    @torch.no_grad()
+    def expert_rows(self, task: FusedExpertTask, expert: int, device) -> torch.Tensor:
+        """All captured input rows of one expert (bf16 [n, in]) on `device`."""
+        st = self.stashes[task.stash_keys[expert]]
+        src = self._segment_source(task, device)
+        chunks = [c.to(device) for c in st.chunks]
+        if src is not None:
+            X, idx, off = src
+            chunks.insert(0, X.index_select(0, idx[off[expert]:off[expert + 1]].long()))
+        if not chunks:
+            return torch.empty(0, task.param.shape[-1], dtype=torch.bfloat16, device=device)
+        return torch.cat(chunks, 0)
 
     # ---- Hessians on the tensor cores ----
     @torch.no_grad()
     def expert_hessians(self, task: FusedExpertTask, device, experts=None) -> torch.Tensor:
         """H [len(experts), C, C] float32 for the given experts of a fused task, one
-        grouped launch over their concatenated stash rows."""
+        grouped launch over their rows (token indices into the captured module
+        inputs / activation segments, plus any stashed rows)."""
         experts = list(range(task.num_experts)) if experts is None else list(experts)
         C = task.param.shape[-1]
-        rows, counts = [], []
+        src = self._segment_source(task, device)
+        parts, base = [], 0
+        if src is not None:
+            X0, idx0, off0 = src
+            parts.append(X0)
+            base = X0.shape[0]
+        idx_parts, counts = [], []
         for e in experts:
-            st = self.stashes[task.stash_keys[e]]
-            rows.extend(c.to(device) for c in st.chunks)
-            counts.append(st.tokens)
-        X = torch.cat(rows, 0) if rows else torch.zeros(1, C, dtype=torch.bfloat16, device=device)
+            n = 0
+            if src is not None and off0[e + 1] > off0[e]:
+                idx_parts.append(idx0[off0[e]:off0[e + 1]])
+                n += off0[e + 1] - off0[e]
+            for c in self.stashes[task.stash_keys[e]].chunks:
+                parts.append(c.to(device))
+                idx_parts.append(torch.arange(base, base + c.shape[0], dtype=torch.int32, device=device))
+                base += c.shape[0]
+                n += c.shape[0]
+            counts.append(n)
+        X = torch.cat(parts, 0) if parts else torch.zeros(1, C, dtype=torch.bfloat16, device=device)
         offsets = torch.zeros(len(experts) + 1, dtype=torch.int64)
         offsets[1:] = torch.cumsum(torch.tensor(counts, dtype=torch.int64), 0)
-        idx = torch.arange(max(int(offsets[-1]), 1), dtype=torch.int32, device=device)
+        idx = torch.cat(idx_parts) if idx_parts else torch.zeros(1, dtype=torch.int32, device=device)
         return hessian_grouped(X, idx, offsets, len(experts))

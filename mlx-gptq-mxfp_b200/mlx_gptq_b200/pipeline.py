@@ -24,6 +24,7 @@ from __future__ import annotations
 import heapq
 import re
 import threading
+import time
 from dataclasses import dataclass, field
 
 import torch
@@ -53,16 +54,31 @@ class LayerSolveArgs:
 
 
 class SolveResult:
-    """artifact name -> (q, scales, biases) on the CPU, plus per-tensor meta (sequential.py:321-330)."""
+    """artifact name -> (q, scales, biases), plus per-tensor meta (sequential.py:321-330).
 
-    def __init__(self):
+    On the CPU like the reference by default; with on_device=True the tensors stay
+    where the solver wrote them (views into the batched outputs) and move to the
+    host once, when the artifact writer packs them."""
+
+    def __init__(self, on_device: bool = False):
         self.tensors = {}
         self.meta = {}
+        self.on_device = on_device
+        self.timing: dict[str, float] = {}  # stage -> seconds (device-synchronised)
         self.lock = threading.Lock()
 
+    def _tick(self, stage: str, t0: float, device) -> float:
+        if device.type == "cuda":
+            torch.cuda.synchronize(device)
+        t1 = time.perf_counter()
+        self.timing[stage] = self.timing.get(stage, 0.0) + (t1 - t0)
+        return t1
+
     def add(self, name, q, s, b, info):
+        if not self.on_device:
+            q, s, b = q.cpu(), s.cpu(), None if b is None else b.cpu()
         with self.lock:
-            self.tensors[name] = (q.cpu(), s.cpu(), None if b is None else b.cpu())
+            self.tensors[name] = (q, s, b)
             self.meta[name] = info
 
 
@@ -118,15 +134,17 @@ def _agreed_counts(counts, group, device):
 
 
 @torch.no_grad()
-def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, device, group=None) -> SolveResult:
+def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, device, group=None,
+                on_device: bool = False) -> SolveResult:
     """Quantize every task of a captured layer; returns the artifacts (sequential.py:467-635)."""
     import torch.distributed as dist
 
     device = torch.device(device)
-    result = SolveResult()
+    result = SolveResult(on_device)
     world = dist.get_world_size(group) if group is not None else 1
     rank = dist.get_rank(group) if group is not None else 0
 
+    t0 = time.perf_counter()
     for task in mgr.fused_tasks:
         p = task.param
         E, R, C = p.shape
@@ -137,9 +155,11 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
         mine = shares[rank]
         if mine:
             H = mgr.expert_hessians(task, device, mine)
+            t0 = result._tick("expert_hessians", t0, device)
             W = p.detach()[mine].to(device)
             q, s, b, W_dq, rel = _solve_batch(W, H, bits, args)
             del H
+            t0 = result._tick("expert_solves", t0, device)
         else:  # this rank owns no expert of the task: empty shares
             q = torch.empty(0, R, C, dtype=torch.uint8, device=device)
             s = torch.empty(0, R, C // args.group_size, dtype=torch.uint8 if args.mode != "affine" else
@@ -157,8 +177,10 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
             W_dq = _all_gather_rows(W_dq.to(p.dtype), counts, group)
             rel = _all_gather_rows(rel, counts, group)
             order = [e for share in shares for e in share]
+            t0 = result._tick("all_gather", t0, device)
         idx = torch.tensor(order, dtype=torch.long)
         p.data[idx.to(p.device)] = W_dq.to(p.dtype).to(p.device)
+        rel_h = rel.tolist()
         for i, e in enumerate(order):
             names = artifact_names_for_fused(layer_prefix, task, e)
             if len(names) == 1:
@@ -170,7 +192,7 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
                 result.add(nm, qq, ss, bb, {
                     "bits": bits, "group_size": args.group_size, "mode": args.mode, "kind": "expert",
                     "out_features": qq.shape[0], "in_features": C,
-                    "tokens": mgr.stashes[task.stash_keys[e]].tokens, "rel_err": round(float(rel[i]), 6),
+                    "tokens": mgr.stashes[task.stash_keys[e]].tokens, "rel_err": round(rel_h[i], 6),
                     "fallback": mgr.fallback_experts.get(task.stash_keys[e])})
 
     # plain linears: one Hessian per stash, shared by the siblings that read the same input
@@ -189,12 +211,15 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
             bits = args.bits_for(name)
             W = t.module.weight.detach().to(device, torch.float32).unsqueeze(0)
             q, s, b, W_dq, rel = _solve_batch(W, H0.clone().unsqueeze(0), bits, args)
-            local[t.name] = (q[0], s[0], None if b is None else b[0], W_dq[0], float(rel[0]), bits)
+            local[t.name] = (q[0], s[0], None if b is None else b[0], W_dq[0].to(t.module.weight.dtype),
+                             float(rel[0]), bits)
+    t0 = result._tick("linears", t0, device)
     if world > 1:
         gathered = [None] * world
         dist.all_gather_object(gathered, {k: tuple(x.cpu() if torch.is_tensor(x) else x for x in v)
                                           for k, v in local.items()}, group=group)
         local = {k: v for part in gathered for k, v in part.items()}
+        t0 = result._tick("all_gather", t0, device)
     for t in mgr.linear_tasks:
         q, s, b, W_dq, rel, bits = local[t.name]
         t.module.weight.data.copy_(W_dq.to(t.module.weight.dtype).to(t.module.weight.device))

@@ -36,6 +36,7 @@ from dataclasses import dataclass, field
 import torch
 
 from .capture import CaptureManager
+from .experts import install_grouped_experts
 from .pipeline import LayerSolveArgs, solve_layer
 
 log = logging.getLogger("mlx_gptq_b200")
@@ -276,7 +277,9 @@ class Pipeline:
     `args` carries the calibrate CLI fields: devices, dtype, layers_attr,
     checkpoint_model_prefix, artifact_layers_prefix, exclude, group_size, bits,
     mode, mxfp_algorithm, damp, clip, overrides, batch_size (and optionally
-    vram_gb). `group` is a torch.distributed process group whose ranks share the
+    vram_gb, experts_forward: "grouped" (default; the sort-based expert forward
+    of experts.py, bit-identical to the eager loop) or "eager"). `group` is a
+    torch.distributed process group whose ranks share the
     solves (None: this process alone)."""
 
     def __init__(self, model, shards, args, group=None):
@@ -296,6 +299,9 @@ class Pipeline:
                     setattr(module, name, buf.to(self.dev0))
         self.inner = inner
         self.layers = getattr(inner, args.layers_attr.split(".")[-1])
+        self.grouped_experts = 0
+        if getattr(args, "experts_forward", "grouped") == "grouped":
+            self.grouped_experts = install_grouped_experts(model)
         self.runtime_model_prefix = args.layers_attr.split(".", 1)[0]
         self.checkpoint_model_prefix = args.checkpoint_model_prefix or self.runtime_model_prefix
         self.checkpoint_layers_prefix_fmt = self._checkpoint_name(args.layers_attr) + ".{}"
@@ -380,7 +386,7 @@ class Pipeline:
     @torch.no_grad()
     def solve_layer(self, layer_idx: int, mgr: CaptureManager):
         prefix = self.artifact_layers_prefix_fmt.format(layer_idx)
-        return solve_layer(prefix, mgr, self.solve_args(), self.dev0, group=self.group)
+        return solve_layer(prefix, mgr, self.solve_args(), self.dev0, group=self.group, on_device=True)
 
     @torch.no_grad()
     def apply_precomputed(self, layer, layer_idx: int, reader) -> None:
@@ -467,7 +473,8 @@ class Pipeline:
             errs = sorted(m["rel_err"] for m in result.meta.values())
             elems = sum(int(m["out_features"]) * int(m["in_features"]) for m in result.meta.values())
             st = LayerStats(li, n_lin, n_exp, t_cap - t0, t_solve - t_cap, t_fwd - t_solve, time.time() - t0, elems,
-                            errs[len(errs) // 2] if errs else -1.0, errs[-1] if errs else -1.0)
+                            errs[len(errs) // 2] if errs else -1.0, errs[-1] if errs else -1.0,
+                            extra={"solve_stages_s": dict(result.timing)})
             self.stats.append(st)
             log.info("layer %d done: %d linears + %d experts | rel_err med=%.4f max=%.4f | capture %.1fs "
                      "solve %.1fs reforward %.1fs total %.1fs", li, n_lin, n_exp, st.rel_err_median,

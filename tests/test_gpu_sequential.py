@@ -21,22 +21,23 @@ TINY = dict(model_type="qwen3_moe", vocab_size=1024, hidden_size=128, intermedia
             max_position_embeddings=256)
 
 
-def _args(mode="mxfp4"):
+def _args(mode="mxfp4", experts_forward="grouped"):
     from mlx_gptq_b200 import sequential
 
     return types.SimpleNamespace(devices=["cuda:0"], dtype="bfloat16", layers_attr="model.layers",
                                  checkpoint_model_prefix=None, artifact_layers_prefix=None,
                                  exclude=sequential.DEFAULT_EXCLUDE, group_size=32, bits=4 if mode == "mxfp4" else 8,
                                  mode=mode, mxfp_algorithm="safe-scale-search" if mode == "mxfp4" else "groupwise",
-                                 damp=0.01, clip="mse", overrides=[], batch_size=4)
+                                 damp=0.01, clip="mse", overrides=[], batch_size=4,
+                                 experts_forward=experts_forward)
 
 
 def _samples():
     return torch.randint(0, TINY["vocab_size"], (8, 64), generator=torch.Generator().manual_seed(1))
 
 
-def _rows_f32(stash):
-    return stash.rows("cuda").float().cpu().numpy()
+def _rows_f32(rows):
+    return rows.float().cpu().numpy()
 
 
 @pytest.mark.parametrize("mode", ["mxfp4", "mxfp8"])
@@ -70,7 +71,7 @@ def test_stack_layer0_matches_oracle(mode, tmp_path):
 
     checked = agree = total = 0
     for t in mgr.linear_tasks:
-        H = ohess.hessian(_rows_f32(mgr.stashes[t.stash_key]))
+        H = ohess.hessian(_rows_f32(mgr.stashes[t.stash_key].rows("cuda")))
         q, s, _, _, rel = ogptq.solve_gptq(W0[f"{t.name}.weight"][None], H[None], args.bits, 32, mode=mode,
                                            mxfp_algorithm=args.mxfp_algorithm)
         gq, gs, gb, info = reader.get(f"model.layers.0.{t.name}.weight")
@@ -82,7 +83,7 @@ def test_stack_layer0_matches_oracle(mode, tmp_path):
     for task in mgr.fused_tasks:
         Wp = W0[f"{task.module_name}.{task.param_name}"]
         for e in range(task.num_experts):
-            rows = _rows_f32(mgr.stashes[task.stash_keys[e]])
+            rows = _rows_f32(mgr.expert_rows(task, e, "cuda"))
             H = ohess.hessian(rows)
             q, s, _, _, _ = ogptq.solve_gptq(Wp[e][None], H[None], args.bits, 32, mode=mode,
                                              mxfp_algorithm=args.mxfp_algorithm)
@@ -120,3 +121,27 @@ def test_stack_resume_reproduces_hidden_states(tmp_path):
     assert pipe2.stats == []  # every layer resumed
     for (h1, _), (h2, _) in zip(out, out2):
         assert torch.equal(h1, h2)
+
+
+def test_grouped_and_eager_expert_forward_give_identical_artifacts(tmp_path):
+    """The sort-based expert forward with segment capture is the eager loop with
+    F.linear interception, bit for bit: same hidden states, same artifacts."""
+    from mlx_gptq_b200 import sequential
+    from mlx_gptq_b200.artifacts import ArtifactReader, ArtifactWriter
+
+    header = {"mode": "mxfp4", "bits": 4, "group_size": 32, "storage_dtype": "bfloat16"}
+    outs = {}
+    for fwd in ("eager", "grouped"):
+        model = sequential.build_model(TINY)
+        pipe = sequential.Pipeline(model, sequential.SyntheticWeights(model, "cuda:0", seed=0), _args(
+            experts_forward=fwd))
+        assert pipe.grouped_experts == (2 if fwd == "grouped" else 0)
+        outs[fwd] = pipe.run(_samples(), ArtifactWriter(str(tmp_path / fwd), header))
+    for (a, _), (b, _) in zip(outs["eager"], outs["grouped"]):
+        assert torch.equal(a, b)
+    ra, rb = ArtifactReader(str(tmp_path / "eager")), ArtifactReader(str(tmp_path / "grouped"))
+    assert set(ra.tensors) == set(rb.tensors)
+    for name in ra.tensors:
+        qa, sa, _, ia = ra.get(name)
+        qb, sb, _, ib = rb.get(name)
+        assert torch.equal(qa, qb) and torch.equal(sa, sb) and ia == ib, name

@@ -236,3 +236,69 @@ def test_sharded_stack_matches_single_process(tmp_path):
     for got in (r0, r1):
         for h, h_ref in zip(got["hidden"], ref["hidden"]):
             assert torch.equal(h, h_ref)
+
+
+def _tiny_layer(seed=0):
+    model = sequential.build_model(TINY_QWEN3_MOE)
+    layer = model.model.layers[0]
+    materialize_module(layer, "model.layers.0", SyntheticWeights(model, "cpu", seed=seed), "cpu", torch.bfloat16)
+    return model, layer
+
+
+def test_grouped_experts_forward_is_bit_identical_to_eager():
+    from mlx_gptq_b200.experts import grouped_experts_forward, install_grouped_experts, route
+
+    _, layer = _tiny_layer()
+    experts = layer.mlp.experts
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(96, 64, generator=g).to(torch.bfloat16)
+    logits = torch.randn(96, 8, generator=g)
+    w, idx = torch.softmax(logits, -1).topk(2, dim=-1)
+    w = (w / w.sum(-1, keepdim=True)).to(torch.bfloat16)
+    idx[:5] = torch.tensor([7, 0])  # ties in expert order across tokens
+    with torch.no_grad():
+        ref = experts(x, idx, w)
+        got = grouped_experts_forward(experts, x, idx, w)
+    assert torch.equal(ref, got)
+    tok, pos, counts = route(idx, 8)
+    assert sum(counts) == 96 * 2 and counts == torch.bincount(idx.flatten(), minlength=8).tolist()
+    for e in range(8):  # eager row order: torch.where on the [top_k, tokens] mask
+        off = sum(counts[:e])
+        j_ref, t_ref = torch.where((idx == e).T)
+        assert torch.equal(tok[off:off + counts[e]], t_ref) and torch.equal(pos[off:off + counts[e]], j_ref)
+    assert install_grouped_experts(layer) == 1
+
+
+def test_segment_capture_matches_linear_interception():
+    from mlx_gptq_b200.capture import CaptureManager
+    from mlx_gptq_b200.experts import install_grouped_experts
+
+    def capture(grouped):
+        _, layer = _tiny_layer()
+        if grouped:
+            install_grouped_experts(layer)
+        mgr = CaptureManager(layer, sequential.DEFAULT_EXCLUDE, 32)
+        g = torch.Generator().manual_seed(5)
+        pos = torch.arange(24).unsqueeze(0)
+        outs = []
+        with mgr, torch.no_grad():
+            for _ in range(2):
+                mgr.begin_batch()
+                h = torch.randn(1, 24, 64, generator=g).to(torch.bfloat16)
+                rot = sequential.build_model(TINY_QWEN3_MOE).model.rotary_emb
+                cos_sin = rot(h, pos)
+                outs.append(layer(h, position_embeddings=cos_sin, attention_mask=None, position_ids=pos))
+        return mgr, outs
+
+    m_e, out_e = capture(False)
+    m_g, out_g = capture(True)
+    for a, b in zip(out_e, out_g):
+        a = a[0] if isinstance(a, tuple) else a
+        b = b[0] if isinstance(b, tuple) else b
+        assert torch.equal(a, b)
+    assert m_g._segments and not m_e._segments
+    for te, tg in zip(m_e.fused_tasks, m_g.fused_tasks):
+        for e in range(te.num_experts):
+            assert m_e.stashes[te.stash_keys[e]].tokens == m_g.stashes[tg.stash_keys[e]].tokens
+            assert torch.equal(m_e.expert_rows(te, e, "cpu"), m_g.expert_rows(tg, e, "cpu")), (te.param_name, e)
+    assert m_e.expert_token_stats() == m_g.expert_token_stats()
