@@ -540,6 +540,8 @@ def main():
     args = ap.parse_args()
     ws, rank, local = dist_env()
     if args.config == "c5":
+        # per-layer buffers vary in size with the routing: let the allocator grow segments
+        os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
         torch.cuda.set_device(local)
         run_c5(args, ws, rank, local)
         return

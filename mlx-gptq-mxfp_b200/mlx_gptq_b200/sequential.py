@@ -465,9 +465,7 @@ class Pipeline:
             batches = [(h, ctx) for h, (_, ctx) in zip(new, batches)]
             self._sync()
             t_fwd = time.time()
-            free_module(layer)
-            if self.dev0.type == "cuda":
-                torch.cuda.empty_cache()
+            free_module(layer)  # the caching allocator keeps the blocks for the next layer
             if writer is not None and self.rank == 0:
                 writer.write_layer(li, result.tensors, result.meta)
             errs = sorted(m["rel_err"] for m in result.meta.values())

@@ -145,3 +145,30 @@ def test_grouped_and_eager_expert_forward_give_identical_artifacts(tmp_path):
         qa, sa, _, ia = ra.get(name)
         qb, sb, _, ib = rb.get(name)
         assert torch.equal(qa, qb) and torch.equal(sa, sb) and ia == ib, name
+
+
+@pytest.mark.parametrize("tokens", [4096, 1000])
+def test_grouped_forward_bit_identical_at_qwen3_30b_a3b_shapes(tokens):
+    """Hidden 2048, 128 experts of intermediate 768, top-8: the sort-based forward
+    (grouped GEMM launches) equals the eager per-expert loop bit for bit."""
+    from transformers import AutoConfig
+    from transformers.models.qwen3_moe.modeling_qwen3_moe import Qwen3MoeExperts
+
+    from mlx_gptq_b200.experts import grouped_experts_forward
+
+    cfg = AutoConfig.for_model("qwen3_moe", hidden_size=2048, moe_intermediate_size=768, num_experts=128,
+                               num_experts_per_tok=8)
+    cfg._experts_implementation = "eager"
+    g = torch.Generator(device="cuda").manual_seed(7)
+    m = Qwen3MoeExperts(cfg).to("cuda", torch.bfloat16)
+    with torch.no_grad():
+        m.gate_up_proj.copy_(torch.randn(m.gate_up_proj.shape, generator=g, device="cuda") * 0.02)
+        m.down_proj.copy_(torch.randn(m.down_proj.shape, generator=g, device="cuda") * 0.02)
+        x = torch.randn(tokens, 2048, generator=g, device="cuda").to(torch.bfloat16)
+        logits = torch.randn(tokens, 128, generator=g, device="cuda")
+        logits[:, :4] += 3.0  # skewed routing, some experts see few or no tokens
+        w, idx = torch.softmax(logits, -1).topk(8, dim=-1)
+        w = (w / w.sum(-1, keepdim=True)).to(torch.bfloat16)
+        ref = m(x, idx, w)
+        got = grouped_experts_forward(m, x, idx, w)
+    assert torch.equal(ref, got)

@@ -260,7 +260,8 @@ def test_grouped_experts_forward_is_bit_identical_to_eager():
         ref = experts(x, idx, w)
         got = grouped_experts_forward(experts, x, idx, w)
     assert torch.equal(ref, got)
-    tok, pos, counts = route(idx, 8)
+    tok, pos, counts, counts_dev = route(idx, 8)
+    assert counts_dev.tolist() == counts
     assert sum(counts) == 96 * 2 and counts == torch.bincount(idx.flatten(), minlength=8).tolist()
     for e in range(8):  # eager row order: torch.where on the [top_k, tokens] mask
         off = sum(counts[:e])
