@@ -476,8 +476,13 @@ def run_c5(args, ws, rank, local):
     pipe.run(samples, writer=None, layers=args.layers)
     torch.cuda.synchronize()
     wall = time.time() - t0
-    rows = [[s.capture_s, s.solve_s, s.reforward_s, s.total_s] for s in pipe.stats]
-    t = torch.tensor(rows + [[wall, 0, 0, 0]], dtype=torch.float64, device=device)
+    def stages(st):
+        d = st.extra.get("solve_stages_s", {})
+        return [d.get("expert_hessians", 0.0) + d.get("expert_solves", 0.0), d.get("linears", 0.0),
+                d.get("all_gather", 0.0)]
+
+    rows = [[s.capture_s, s.solve_s, s.reforward_s, s.total_s] + stages(s) for s in pipe.stats]
+    t = torch.tensor(rows + [[wall, 0, 0, 0, 0, 0, 0]], dtype=torch.float64, device=device)
     if group is not None:
         import torch.distributed as dist
 
@@ -513,8 +518,11 @@ def run_c5(args, ws, rank, local):
             "solve_s": [round(r[1], 3) for r in per_layer],
             "reforward_s": [round(r[2], 3) for r in per_layer],
             "wall_s": wall,
-            "solve_stages_s_rank0": [{k: round(v, 4) for k, v in s.extra.get("solve_stages_s", {}).items()}
-                                     for s in pipe.stats],
+            "expert_stage_ms_per_layer": statistics.mean(r[4] for r in per_layer[1:] or per_layer) * 1e3,
+            "linears_ms_per_layer": statistics.mean(r[5] for r in per_layer[1:] or per_layer) * 1e3,
+            "all_gather_ms_per_layer": statistics.mean(r[6] for r in per_layer[1:] or per_layer) * 1e3,
+            "stage_note": "max over ranks per layer; expert stage = grouped expert Hessians + batched "
+                          "expert solves; layer 0 (one-time set-up) excluded from the means",
             "rel_err_median": [round(s.rel_err_median, 5) for s in pipe.stats],
             "rel_err_max": [round(s.rel_err_max, 5) for s in pipe.stats]}
     print(json.dumps(line), flush=True)

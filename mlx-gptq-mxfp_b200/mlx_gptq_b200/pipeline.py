@@ -133,6 +133,51 @@ def _agreed_counts(counts, group, device):
     return [int(v) for v in t.tolist()]
 
 
+# Cost of solving one weight element in Hessian units (tokens x C^2 multiply-adds):
+# the MXFP4 safe-scale-search column loop costs ~2.3e-11 s per element on a B200,
+# the Hessian ~2e-15 s per unit.
+SOLVE_COST_PER_ELEM = 1.0e4
+
+
+def plan_layer(mgr: CaptureManager, world: int, group=None, device="cpu"):
+    """One longest-processing-time partition of a layer's work over `world` ranks:
+    every expert of every fused task and every linear stash (its Hessian, shared by
+    the sibling linears that read it, plus their solves) is one item. Returns, per
+    rank, {"experts": {task index: [expert, ...]}, "linears": [stash key, ...]}.
+    Token counts are rank 0's, so every rank derives the same plan."""
+    by_stash: dict[str, list] = {}
+    for t in mgr.linear_tasks:
+        by_stash.setdefault(t.stash_key, []).append(t)
+    keys = sorted(by_stash)
+    counts = []
+    for task in mgr.fused_tasks:
+        counts.extend(mgr.stashes[k].tokens for k in task.stash_keys)
+    counts.extend(mgr.stashes[k].tokens for k in keys)
+    counts = _agreed_counts(counts, group, device)
+    items, costs, i = [], [], 0
+    for ti, task in enumerate(mgr.fused_tasks):
+        E, R, C = task.param.shape
+        for e in range(E):
+            items.append(("expert", ti, e))
+            costs.append(float(counts[i]) * C * C + SOLVE_COST_PER_ELEM * R * C)
+            i += 1
+    for k in keys:
+        C = mgr.stashes[k].in_features
+        items.append(("linear", k, None))
+        costs.append(float(counts[i]) * C * C + SOLVE_COST_PER_ELEM * sum(
+            t.module.out_features * C for t in by_stash[k]))
+        i += 1
+    plans = [{"experts": {ti: [] for ti in range(len(mgr.fused_tasks))}, "linears": []} for _ in range(world)]
+    for r, share in enumerate(lpt_partition(costs, world)):
+        for j in share:
+            kind, a, e = items[j]
+            if kind == "expert":
+                plans[r]["experts"][a].append(e)
+            else:
+                plans[r]["linears"].append(a)
+    return plans, by_stash
+
+
 @torch.no_grad()
 def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, device, group=None,
                 on_device: bool = False) -> SolveResult:
@@ -143,15 +188,14 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
     result = SolveResult(on_device)
     world = dist.get_world_size(group) if group is not None else 1
     rank = dist.get_rank(group) if group is not None else 0
+    plans, by_stash = plan_layer(mgr, world, group, device)
 
     t0 = time.perf_counter()
-    for task in mgr.fused_tasks:
+    for ti, task in enumerate(mgr.fused_tasks):
         p = task.param
         E, R, C = p.shape
         bits = args.bits_for(artifact_names_for_fused(layer_prefix, task, 0)[0])
-        tokens = _agreed_counts([mgr.stashes[k].tokens for k in task.stash_keys], group, device)
-        costs = [float(t) * C * C + 3.0 * R * C for t in tokens]  # Hessian + solve work
-        shares = lpt_partition(costs, world)
+        shares = [plans[r]["experts"][ti] for r in range(world)]
         mine = shares[rank]
         if mine:
             H = mgr.expert_hessians(task, device, mine)
@@ -196,13 +240,7 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
                     "fallback": mgr.fallback_experts.get(task.stash_keys[e])})
 
     # plain linears: one Hessian per stash, shared by the siblings that read the same input
-    by_stash: dict[str, list] = {}
-    for t in mgr.linear_tasks:
-        by_stash.setdefault(t.stash_key, []).append(t)
-    keys = sorted(by_stash)
-    counts = _agreed_counts([mgr.stashes[k].tokens for k in keys], group, device)
-    costs = [float(n) * mgr.stashes[k].in_features ** 2 for n, k in zip(counts, keys)]
-    my_keys = [keys[i] for i in lpt_partition(costs, world)[rank]]
+    my_keys = plans[rank]["linears"]
     local = {}
     for key in my_keys:
         H0 = mgr.stashes[key].hessian(device)

@@ -202,3 +202,23 @@ def test_sharded_layer_solve_matches_single_process(tmp_path):
             assert torch.equal(q, q2) and torch.equal(s, s2)
         for k, v in ref["weights"].items():
             assert torch.equal(v, got["weights"][k]), k
+
+
+def test_plan_layer_covers_every_item_once_and_balances():
+    from mlx_gptq_b200.pipeline import plan_layer
+
+    torch.manual_seed(0)
+    layer = ToyMoELayer(E=6, k=2)
+    mgr = CaptureManager(layer, exclude_regex=r"(^|\.)gate$", group_size=32)
+    with mgr:
+        mgr.begin_batch()
+        layer(torch.randn(64, 32))
+    for world in (1, 2, 3, 8):
+        plans, by_stash = plan_layer(mgr, world)
+        assert len(plans) == world
+        for ti, task in enumerate(mgr.fused_tasks):
+            got = sorted(e for p in plans for e in p["experts"][ti])
+            assert got == list(range(task.num_experts))
+        assert sorted(k for p in plans for k in p["linears"]) == sorted(by_stash)
+    # q/k share one stash: one linear item
+    assert len(by_stash) == 1 and len(next(iter(by_stash.values()))) == 2
