@@ -478,8 +478,17 @@ def run_c5(args, ws, rank, local):
     wall = time.time() - t0
     def stages(st):
         d = st.extra.get("solve_stages_s", {})
-        return [d.get("expert_hessians", 0.0) + d.get("expert_solves", 0.0), d.get("linears", 0.0),
-                d.get("all_gather", 0.0)]
+        return [d.get("expert_rows", 0.0) + d.get("expert_hessians", 0.0) + d.get("expert_solves", 0.0),
+                d.get("linears", 0.0), d.get("all_gather", 0.0)]
+
+    mid = len(pipe.stats) // 2
+    my_mid = {k: round(v * 1e3, 2) for k, v in pipe.stats[mid].extra.get("solve_stages_s", {}).items()}
+    per_rank_mid = [my_mid]
+    if group is not None:
+        import torch.distributed as dist
+
+        per_rank_mid = [None] * ws
+        dist.all_gather_object(per_rank_mid, my_mid, group=group)
 
     rows = [[s.capture_s, s.solve_s, s.reforward_s, s.total_s] + stages(s) for s in pipe.stats]
     t = torch.tensor(rows + [[wall, 0, 0, 0, 0, 0, 0]], dtype=torch.float64, device=device)
@@ -521,6 +530,7 @@ def run_c5(args, ws, rank, local):
             "expert_stage_ms_per_layer": statistics.mean(r[4] for r in per_layer[1:] or per_layer) * 1e3,
             "linears_ms_per_layer": statistics.mean(r[5] for r in per_layer[1:] or per_layer) * 1e3,
             "all_gather_ms_per_layer": statistics.mean(r[6] for r in per_layer[1:] or per_layer) * 1e3,
+            "solve_stages_ms_per_rank_layer_mid": per_rank_mid,
             "stage_note": "max over ranks per layer; expert stage = grouped expert Hessians + batched "
                           "expert solves; layer 0 (one-time set-up) excluded from the means",
             "rel_err_median": [round(s.rel_err_median, 5) for s in pipe.stats],

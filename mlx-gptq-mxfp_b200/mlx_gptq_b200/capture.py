@@ -432,7 +432,7 @@ class CaptureManager:
 
     # ---- Hessians on the tensor cores ----
     @torch.no_grad()
-    def expert_hessians(self, task: FusedExpertTask, device, experts=None) -> torch.Tensor:
+    def expert_hessians(self, task: FusedExpertTask, device, experts=None, timer=None) -> torch.Tensor:
         """H [len(experts), C, C] float32 for the given experts of a fused task, one
         grouped launch over their rows (token indices into the captured module
         inputs / activation segments, plus any stashed rows)."""
@@ -460,4 +460,6 @@ class CaptureManager:
         offsets = torch.zeros(len(experts) + 1, dtype=torch.int64)
         offsets[1:] = torch.cumsum(torch.tensor(counts, dtype=torch.int64), 0)
         idx = torch.cat(idx_parts) if idx_parts else torch.zeros(1, dtype=torch.int32, device=device)
+        if timer is not None:
+            timer("expert_rows")
         return hessian_grouped(X, idx, offsets, len(experts))

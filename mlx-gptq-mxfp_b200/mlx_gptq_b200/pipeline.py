@@ -121,6 +121,23 @@ def _all_gather_rows(t: torch.Tensor, counts, group):
     return torch.cat([out[r * n_max: r * n_max + counts[r]] for r in range(world)], 0)
 
 
+def _nbytes(shape, dtype) -> int:
+    n = 1
+    for d in shape:
+        n *= d
+    return n * torch.empty(0, dtype=dtype).element_size()
+
+
+def _linear_spec(R: int, C: int, args: "LayerSolveArgs", weight_dtype):
+    """(shape, dtype) of one solved linear's outputs in packing order:
+    codes, scales, [biases,] dequantized weight, rel_err."""
+    sdt = torch.uint8 if args.mode != "affine" else args.storage_dtype
+    spec = [((R, C), torch.uint8), ((R, C // args.group_size), sdt)]
+    if args.mode == "affine":
+        spec.append(((R, C // args.group_size), sdt))
+    return spec + [((R, C), weight_dtype), ((1,), torch.float32)]
+
+
 def _agreed_counts(counts, group, device):
     """Rank 0's token counts on every rank, so that every rank derives the same
     partition even if the redundant forwards routed a token differently."""
@@ -198,7 +215,10 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
         shares = [plans[r]["experts"][ti] for r in range(world)]
         mine = shares[rank]
         if mine:
-            H = mgr.expert_hessians(task, device, mine)
+            def timer(stage):
+                nonlocal t0
+                t0 = result._tick(stage, t0, device)
+            H = mgr.expert_hessians(task, device, mine, timer=timer)
             t0 = result._tick("expert_hessians", t0, device)
             W = p.detach()[mine].to(device)
             q, s, b, W_dq, rel = _solve_batch(W, H, bits, args)
@@ -253,10 +273,31 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
                              float(rel[0]), bits)
     t0 = result._tick("linears", t0, device)
     if world > 1:
-        gathered = [None] * world
-        dist.all_gather_object(gathered, {k: tuple(x.cpu() if torch.is_tensor(x) else x for x in v)
-                                          for k, v in local.items()}, group=group)
-        local = {k: v for part in gathered for k, v in part.items()}
+        # every linear's outputs reach every rank from the rank that solved it: one
+        # broadcast of a packed byte buffer per linear, all ranks in stash-key order
+        owner = {k: r for r in range(world) for k in plans[r]["linears"]}
+        for key in sorted(by_stash):
+            src = dist.get_global_rank(group, owner[key])
+            for t in by_stash[key]:
+                R, C = t.module.out_features, t.module.in_features
+                spec = _linear_spec(R, C, args, t.module.weight.dtype)
+                if owner[key] == rank:
+                    q, s_, b, W_dq, rel, bits = local[t.name]
+                    rel_t = torch.tensor([rel], dtype=torch.float32, device=device)
+                    parts = [q, s_] + ([b] if b is not None else []) + [W_dq, rel_t]
+                    buf = torch.cat([x.contiguous().view(torch.uint8).reshape(-1) for x in parts])
+                else:
+                    buf = torch.empty(sum(_nbytes(sh, dt) for sh, dt in spec), dtype=torch.uint8, device=device)
+                dist.broadcast(buf, src=src, group=group)
+                if owner[key] != rank:
+                    out, off = [], 0
+                    for sh, dt in spec:
+                        n = _nbytes(sh, dt)
+                        out.append(buf[off:off + n].view(dt).reshape(sh))
+                        off += n
+                    b = out[2] if len(spec) == 5 else None
+                    local[t.name] = (out[0], out[1], b, out[-2], float(out[-1][0]),
+                                     args.bits_for(f"{layer_prefix}.{t.name}.weight"))
         t0 = result._tick("all_gather", t0, device)
     for t in mgr.linear_tasks:
         q, s, b, W_dq, rel, bits = local[t.name]

@@ -145,7 +145,7 @@ def _fake_solve(W, H, bits, args):
     return q, s, None, W_dq, rel
 
 
-def _fake_expert_hessians(self, task, device, experts=None):
+def _fake_expert_hessians(self, task, device, experts=None, timer=None):
     experts = list(range(task.num_experts)) if experts is None else list(experts)
     C = task.param.shape[-1]
     return torch.stack([torch.eye(C) * (self.stashes[task.stash_keys[e]].tokens + 1) for e in experts])
