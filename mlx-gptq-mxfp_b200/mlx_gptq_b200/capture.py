@@ -193,8 +193,10 @@ class CaptureManager:
         self._fused_modules: dict[str, torch.nn.Module] = {}
         self._fused_input_stashes: dict[str, Stash] = {}
         self.fallback_experts: dict[str, str] = {}
-        self._segments: dict[str, list] = {}  # module -> per-batch (hidden, tok, counts, acts)
+        # module -> per batch: (inputs, global token ids by expert, counts, offsets, activations)
+        self._segments: dict[str, list] = {}
         self._segment_modules: set[str] = set()
+        self._inputs_cache: dict[str, torch.Tensor] = {}
         self._mode_registry: dict[int, str] = {}
         self._mode = None
         excl = re.compile(exclude_regex) if exclude_regex else None
@@ -272,8 +274,12 @@ class CaptureManager:
         tasks = [t for t in self.fused_tasks if t.module_name == module_name]
 
         def sink(hidden, tok, counts, acts):
-            self._segments.setdefault(module_name, []).append((hidden.detach().clone(), tok.to(torch.int32),
-                                                               list(counts), acts))
+            segs = self._segments.setdefault(module_name, [])
+            base = sum(sg[0].shape[0] for sg in segs)  # rows of the module input captured so far
+            offs = [0]
+            for n in counts:
+                offs.append(offs[-1] + n)
+            segs.append((hidden.detach().clone(), (tok + base).to(torch.int32), list(counts), offs, acts))
             for t in tasks:
                 for e, n in enumerate(counts):
                     self.stashes[t.stash_keys[e]].tokens += n
@@ -316,7 +322,7 @@ class CaptureManager:
     # ---- diagnostics ----
     def total_stash_bytes(self) -> int:
         seg = sum(h.numel() * h.element_size() + t.numel() * 4 + (0 if a is None else a.numel() * a.element_size())
-                  for segs in self._segments.values() for h, t, _, a in segs)
+                  for segs in self._segments.values() for h, t, _, _, a in segs)
         return sum(s.nbytes() for s in self.stashes.values()) + seg
 
     def expert_token_stats(self):
@@ -385,47 +391,48 @@ class CaptureManager:
         for s in self._fused_input_stashes.values():
             s.clear()
         self._segments.clear()
+        self._inputs_cache.clear()
 
     # ---- rows of one expert, wherever they were captured ----
-    def _segment_source(self, task: FusedExpertTask, device):
-        """(X, idx, offsets) for a segment-captured task: X holds the source rows
-        (the module inputs for gate/up, the activations for down_proj), idx [S]
-        int32 the rows of X grouped by expert (batch order, then slot order, as the
-        eager stash would hold them), offsets [E+1] host ints. None if the task's
-        module was captured through F.linear interception."""
+    def _module_inputs(self, module_name: str, device) -> torch.Tensor:
+        """All captured inputs of a segment-captured expert module, one [tokens, in] tensor
+        (built once per layer; gate/up rows are token indices into it)."""
+        X = self._inputs_cache.get(module_name)
+        if X is None:
+            X = torch.cat([sg[0].to(device) for sg in self._segments[module_name]], 0)
+            self._inputs_cache[module_name] = X
+        return X
+
+    def _segment_rows(self, task: FusedExpertTask, experts, device):
+        """(X, idx, counts) covering the segment-captured rows of `experts`, expert
+        by expert in capture order (batch, then slot): X [n, in] bf16, idx int32 rows
+        of X, counts per expert. None if the task was captured through F.linear."""
         segs = self._segments.get(task.module_name)
         if not segs:
             return None
-        E = task.num_experts
-        down = task.param_name == "down_proj"
-        parts, ids, experts = [], [], []
-        base = 0
-        for hidden, tok, counts, acts in segs:
-            src = acts if down else hidden
-            parts.append(src.to(device))
-            ids.append((torch.arange(tok.shape[0], device=device, dtype=torch.int64) if down
-                        else tok.to(device, torch.int64)) + base)
-            experts.append(torch.repeat_interleave(torch.arange(E, device=device),
-                                                   torch.tensor(counts, device=device)))
-            base += src.shape[0]
-        X = torch.cat(parts, 0)
-        perm = torch.argsort(torch.cat(experts), stable=True)
-        idx = torch.cat(ids)[perm].to(torch.int32)
-        totals = [sum(c[2][e] for c in segs) for e in range(E)]
-        offsets = [0]
-        for n in totals:
-            offsets.append(offsets[-1] + n)
-        return X, idx, offsets
+        counts = [sum(sg[2][e] for sg in segs) for e in experts]
+        if task.param_name == "down_proj":  # activation rows: copy only these experts' blocks
+            blocks = [sg[4][sg[3][e]:sg[3][e + 1]] for e in experts for sg in segs if sg[2][e]]
+            C = task.param.shape[-1]
+            X = torch.cat([b.to(device) for b in blocks], 0) if blocks else \
+                torch.zeros(0, C, dtype=torch.bfloat16, device=device)
+            idx = torch.arange(X.shape[0], dtype=torch.int32, device=device)
+            return X, idx, counts
+        X = self._module_inputs(task.module_name, device)
+        pieces = [sg[1][sg[3][e]:sg[3][e + 1]] for e in experts for sg in segs if sg[2][e]]
+        idx = torch.cat([p.to(device) for p in pieces]) if pieces else \
+            torch.zeros(0, dtype=torch.int32, device=device)
+        return X, idx, counts
 
     @torch.no_grad()
     def expert_rows(self, task: FusedExpertTask, expert: int, device) -> torch.Tensor:
         """All captured input rows of one expert (bf16 [n, in]) on `device`."""
         st = self.stashes[task.stash_keys[expert]]
-        src = self._segment_source(task, device)
         chunks = [c.to(device) for c in st.chunks]
-        if src is not None:
-            X, idx, off = src
-            chunks.insert(0, X.index_select(0, idx[off[expert]:off[expert + 1]].long()))
+        seg = self._segment_rows(task, [expert], device)
+        if seg is not None:
+            X, idx, _ = seg
+            chunks.insert(0, X.index_select(0, idx.long()))
         if not chunks:
             return torch.empty(0, task.param.shape[-1], dtype=torch.bfloat16, device=device)
         return torch.cat(chunks, 0)
@@ -435,28 +442,30 @@ class CaptureManager:
     def expert_hessians(self, task: FusedExpertTask, device, experts=None, timer=None) -> torch.Tensor:
         """H [len(experts), C, C] float32 for the given experts of a fused task, one
         grouped launch over their rows (token indices into the captured module
-        inputs / activation segments, plus any stashed rows)."""
+        inputs, or this share's activation blocks, plus any stashed rows)."""
         experts = list(range(task.num_experts)) if experts is None else list(experts)
         C = task.param.shape[-1]
-        src = self._segment_source(task, device)
-        parts, base = [], 0
-        if src is not None:
-            X0, idx0, off0 = src
+        seg = self._segment_rows(task, experts, device)
+        parts, idx_parts, counts, base = [], [], [], 0
+        seg_off = 0
+        if seg is not None:
+            X0, idx0, seg_counts = seg
             parts.append(X0)
             base = X0.shape[0]
-        idx_parts, counts = [], []
-        for e in experts:
+        for i, e in enumerate(experts):
             n = 0
-            if src is not None and off0[e + 1] > off0[e]:
-                idx_parts.append(idx0[off0[e]:off0[e + 1]])
-                n += off0[e + 1] - off0[e]
+            if seg is not None and seg_counts[i]:
+                idx_parts.append(idx0[seg_off:seg_off + seg_counts[i]])
+                seg_off += seg_counts[i]
+                n += seg_counts[i]
             for c in self.stashes[task.stash_keys[e]].chunks:
                 parts.append(c.to(device))
                 idx_parts.append(torch.arange(base, base + c.shape[0], dtype=torch.int32, device=device))
                 base += c.shape[0]
                 n += c.shape[0]
             counts.append(n)
-        X = torch.cat(parts, 0) if parts else torch.zeros(1, C, dtype=torch.bfloat16, device=device)
+        X = (parts[0] if len(parts) == 1 else torch.cat(parts, 0)) if parts else \
+            torch.zeros(1, C, dtype=torch.bfloat16, device=device)
         offsets = torch.zeros(len(experts) + 1, dtype=torch.int64)
         offsets[1:] = torch.cumsum(torch.tensor(counts, dtype=torch.int64), 0)
         idx = torch.cat(idx_parts) if idx_parts else torch.zeros(1, dtype=torch.int32, device=device)

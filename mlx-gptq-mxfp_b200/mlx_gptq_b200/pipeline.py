@@ -207,41 +207,69 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
     rank = dist.get_rank(group) if group is not None else 0
     plans, by_stash = plan_layer(mgr, world, group, device)
 
+    # phase 1: this rank's own work, no collectives (a rank with a large linear does
+    # not hold the others up at an expert all-gather)
     t0 = time.perf_counter()
+
+    def timer(stage):
+        nonlocal t0
+        t0 = result._tick(stage, t0, device)
+
+    fused_out = []
     for ti, task in enumerate(mgr.fused_tasks):
         p = task.param
         E, R, C = p.shape
         bits = args.bits_for(artifact_names_for_fused(layer_prefix, task, 0)[0])
-        shares = [plans[r]["experts"][ti] for r in range(world)]
-        mine = shares[rank]
+        mine = plans[rank]["experts"][ti]
         if mine:
-            def timer(stage):
-                nonlocal t0
-                t0 = result._tick(stage, t0, device)
             H = mgr.expert_hessians(task, device, mine, timer=timer)
-            t0 = result._tick("expert_hessians", t0, device)
+            timer("expert_hessians")
             W = p.detach()[mine].to(device)
             q, s, b, W_dq, rel = _solve_batch(W, H, bits, args)
-            del H
-            t0 = result._tick("expert_solves", t0, device)
+            W_dq = W_dq.to(p.dtype)
+            del H, W
+            timer("expert_solves")
         else:  # this rank owns no expert of the task: empty shares
             q = torch.empty(0, R, C, dtype=torch.uint8, device=device)
             s = torch.empty(0, R, C // args.group_size, dtype=torch.uint8 if args.mode != "affine" else
                             args.storage_dtype, device=device)
             b = None if args.mode != "affine" else torch.empty_like(s)
-            W_dq = torch.empty(0, R, C, dtype=torch.float32, device=device)
+            W_dq = torch.empty(0, R, C, dtype=p.dtype, device=device)
             rel = torch.empty(0, dtype=torch.float32, device=device)
-        order = list(mine)
+        fused_out.append((bits, q, s, b, W_dq, rel))
+
+    # plain linears: one Hessian per stash, shared by the siblings that read the same input
+    my_keys = plans[rank]["linears"]
+    local = {}
+    for key in my_keys:
+        H0 = mgr.stashes[key].hessian(device)
+        for t in by_stash[key]:
+            name = f"{layer_prefix}.{t.name}.weight"
+            bits = args.bits_for(name)
+            W = t.module.weight.detach().to(device, torch.float32).unsqueeze(0)
+            q, s, b, W_dq, rel = _solve_batch(W, H0.clone().unsqueeze(0), bits, args)
+            local[t.name] = (q[0], s[0], None if b is None else b[0], W_dq[0].to(t.module.weight.dtype),
+                             float(rel[0]), bits)
+    timer("linears")
+
+    # phase 2: exchange (one all-gather per expert output tensor, one broadcast per
+    # linear), then every rank writes the dequantized weights back into its layer
+    for ti, task in enumerate(mgr.fused_tasks):
+        p = task.param
+        E, R, C = p.shape
+        bits, q, s, b, W_dq, rel = fused_out[ti]
+        shares = [plans[r]["experts"][ti] for r in range(world)]
+        order = list(shares[rank])
         if world > 1:
             counts = [len(x) for x in shares]
             q = _all_gather_rows(q, counts, group)
             s = _all_gather_rows(s, counts, group)
             if b is not None:
                 b = _all_gather_rows(b, counts, group)
-            W_dq = _all_gather_rows(W_dq.to(p.dtype), counts, group)
+            W_dq = _all_gather_rows(W_dq, counts, group)
             rel = _all_gather_rows(rel, counts, group)
             order = [e for share in shares for e in share]
-            t0 = result._tick("all_gather", t0, device)
+            timer("all_gather")
         idx = torch.tensor(order, dtype=torch.long)
         p.data[idx.to(p.device)] = W_dq.to(p.dtype).to(p.device)
         rel_h = rel.tolist()
@@ -258,20 +286,8 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
                     "out_features": qq.shape[0], "in_features": C,
                     "tokens": mgr.stashes[task.stash_keys[e]].tokens, "rel_err": round(rel_h[i], 6),
                     "fallback": mgr.fallback_experts.get(task.stash_keys[e])})
+        timer("write_back")
 
-    # plain linears: one Hessian per stash, shared by the siblings that read the same input
-    my_keys = plans[rank]["linears"]
-    local = {}
-    for key in my_keys:
-        H0 = mgr.stashes[key].hessian(device)
-        for t in by_stash[key]:
-            name = f"{layer_prefix}.{t.name}.weight"
-            bits = args.bits_for(name)
-            W = t.module.weight.detach().to(device, torch.float32).unsqueeze(0)
-            q, s, b, W_dq, rel = _solve_batch(W, H0.clone().unsqueeze(0), bits, args)
-            local[t.name] = (q[0], s[0], None if b is None else b[0], W_dq[0].to(t.module.weight.dtype),
-                             float(rel[0]), bits)
-    t0 = result._tick("linears", t0, device)
     if world > 1:
         # every linear's outputs reach every rank from the rank that solved it: one
         # broadcast of a packed byte buffer per linear, all ranks in stash-key order
@@ -298,7 +314,7 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
                     b = out[2] if len(spec) == 5 else None
                     local[t.name] = (out[0], out[1], b, out[-2], float(out[-1][0]),
                                      args.bits_for(f"{layer_prefix}.{t.name}.weight"))
-        t0 = result._tick("all_gather", t0, device)
+        timer("all_gather")
     for t in mgr.linear_tasks:
         q, s, b, W_dq, rel, bits = local[t.name]
         t.module.weight.data.copy_(W_dq.to(t.module.weight.dtype).to(t.module.weight.device))
