@@ -321,8 +321,10 @@ class CaptureManager:
 
     # ---- diagnostics ----
     def total_stash_bytes(self) -> int:
-        seg = sum(h.numel() * h.element_size() + t.numel() * 4 + (0 if a is None else a.numel() * a.element_size())
-                  for segs in self._segments.values() for h, t, _, _, a in segs)
+        seg = sum(x.numel() * x.element_size() for segs in self._segments.values() for sg in segs
+                  for x in (sg[0], sg[1], sg[4]) if x is not None)
+        seg += sum(x.numel() * x.element_size() for c in self._inputs_cache.values()
+                   for x in (c["inputs"], c["acts"], c["slot_tok"], c["slot_expert"]) if x is not None)
         return sum(s.nbytes() for s in self.stashes.values()) + seg
 
     def expert_token_stats(self):
@@ -394,35 +396,42 @@ class CaptureManager:
         self._inputs_cache.clear()
 
     # ---- rows of one expert, wherever they were captured ----
-    def _module_inputs(self, module_name: str, device) -> torch.Tensor:
-        """All captured inputs of a segment-captured expert module, one [tokens, in] tensor
-        (built once per layer; gate/up rows are token indices into it)."""
-        X = self._inputs_cache.get(module_name)
-        if X is None:
-            X = torch.cat([sg[0].to(device) for sg in self._segments[module_name]], 0)
-            self._inputs_cache[module_name] = X
-        return X
+    def _module_cache(self, module_name: str, device) -> dict:
+        """The captured batches of a segment-captured expert module joined once per
+        layer: inputs [tokens, in], activations [slots, inter], and per slot its
+        global token id (int32) and expert (int64). The per-batch copies are dropped."""
+        cache = self._inputs_cache.get(module_name)
+        if cache is not None:
+            return cache
+        segs = self._segments[module_name]
+        E = len(segs[0][2])
+        experts = [torch.repeat_interleave(torch.arange(E, device=device),
+                                           torch.tensor(sg[2], device=device), output_size=sg[3][-1])
+                   for sg in segs]
+        cache = {"inputs": torch.cat([sg[0].to(device) for sg in segs], 0),
+                 "acts": torch.cat([sg[4].to(device) for sg in segs], 0) if segs[0][4] is not None else None,
+                 "slot_tok": torch.cat([sg[1].to(device) for sg in segs]),
+                 "slot_expert": torch.cat(experts),
+                 "counts": [sum(sg[2][e] for sg in segs) for e in range(E)]}
+        self._segments[module_name] = [(None, None, sg[2], sg[3], None) for sg in segs]
+        self._inputs_cache[module_name] = cache
+        return cache
 
     def _segment_rows(self, task: FusedExpertTask, experts, device):
         """(X, idx, counts) covering the segment-captured rows of `experts`, expert
-        by expert in capture order (batch, then slot): X [n, in] bf16, idx int32 rows
-        of X, counts per expert. None if the task was captured through F.linear."""
-        segs = self._segments.get(task.module_name)
-        if not segs:
+        by expert in capture order (batch, then slot): idx int32 rows of X, counts
+        per expert. None if the task was captured through F.linear."""
+        if not self._segments.get(task.module_name):
             return None
-        counts = [sum(sg[2][e] for sg in segs) for e in experts]
-        if task.param_name == "down_proj":  # activation rows: copy only these experts' blocks
-            blocks = [sg[4][sg[3][e]:sg[3][e + 1]] for e in experts for sg in segs if sg[2][e]]
-            C = task.param.shape[-1]
-            X = torch.cat([b.to(device) for b in blocks], 0) if blocks else \
-                torch.zeros(0, C, dtype=torch.bfloat16, device=device)
-            idx = torch.arange(X.shape[0], dtype=torch.int32, device=device)
-            return X, idx, counts
-        X = self._module_inputs(task.module_name, device)
-        pieces = [sg[1][sg[3][e]:sg[3][e + 1]] for e in experts for sg in segs if sg[2][e]]
-        idx = torch.cat([p.to(device) for p in pieces]) if pieces else \
-            torch.zeros(0, dtype=torch.int32, device=device)
-        return X, idx, counts
+        c = self._module_cache(task.module_name, device)
+        counts = [c["counts"][e] for e in experts]
+        S = c["slot_expert"].shape[0]
+        pos = torch.full((len(c["counts"]),), len(experts), dtype=torch.int64, device=device)
+        pos[torch.tensor(experts, dtype=torch.int64, device=device)] = torch.arange(len(experts), device=device)
+        order = torch.argsort(pos[c["slot_expert"]] * S + torch.arange(S, device=device))[:sum(counts)]
+        if task.param_name == "down_proj":
+            return c["acts"], order.to(torch.int32), counts
+        return c["inputs"], c["slot_tok"][order], counts
 
     @torch.no_grad()
     def expert_rows(self, task: FusedExpertTask, expert: int, device) -> torch.Tensor:
