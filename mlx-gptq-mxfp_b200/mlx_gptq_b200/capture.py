@@ -171,6 +171,71 @@ class FusedExpertTask:
     stash_keys: list = field(default_factory=list)  # one per expert
 
 
+class SegmentStore:
+    """Rows captured from one sort-based expert module (experts.py), kept where the
+    layer runs: the module inputs [tokens, in], the activations that feed
+    down_proj [slots, inter] in expert order per batch, and each slot's global
+    token id. Buffers are sized once from `reserve_tokens` (tokens per layer) and
+    grow by doubling otherwise; the forward writes its activations straight into
+    them."""
+
+    def __init__(self, num_experts: int, reserve_tokens: int | None = None):
+        self.E = num_experts
+        self.reserve = reserve_tokens
+        self.inputs = self.acts = self.tok = None
+        self.n_tok = self.n_slot = 0
+        self.batch_counts: list[list[int]] = []
+        self.counts = [0] * num_experts
+        self._pending = None  # activation slice handed to the running forward
+
+    @staticmethod
+    def _grow(buf, used: int, need: int, row_shape, dtype, device, hint):
+        if buf is not None and buf.shape[0] >= need:
+            return buf
+        cap = max(need, hint or 0, 2 * (buf.shape[0] if buf is not None else 0))
+        new = torch.empty((cap,) + tuple(row_shape), dtype=dtype, device=device)
+        if buf is not None and used:
+            new[:used].copy_(buf[:used])
+        return new
+
+    def _slot_hint(self, slots: int, tokens: int):
+        """Slots per layer expected from the reservation (tokens x slots per token)."""
+        return None if self.reserve is None else self.reserve * max(1, -(-slots // max(1, tokens)))
+
+    def acts_out(self, slots: int, tokens: int, inter: int, dtype, device) -> torch.Tensor:
+        """Where the forward should write this batch's activation rows."""
+        self.acts = self._grow(self.acts, self.n_slot, self.n_slot + slots, (inter,), dtype, device,
+                               self._slot_hint(slots, tokens))
+        self._pending = self.acts[self.n_slot:self.n_slot + slots]
+        return self._pending
+
+    def add(self, hidden: torch.Tensor, tok: torch.Tensor, counts, acts: torch.Tensor):
+        T, S = hidden.shape[0], tok.shape[0]
+        dev = hidden.device
+        self.inputs = self._grow(self.inputs, self.n_tok, self.n_tok + T, hidden.shape[1:], hidden.dtype, dev,
+                                 self.reserve)
+        self.inputs[self.n_tok:self.n_tok + T].copy_(hidden)
+        self.tok = self._grow(self.tok, self.n_slot, self.n_slot + S, (), torch.int32, dev, self._slot_hint(S, T))
+        self.tok[self.n_slot:self.n_slot + S].copy_(tok + self.n_tok)
+        if acts is not None and (self._pending is None or acts.data_ptr() != self._pending.data_ptr()):
+            self.acts = self._grow(self.acts, self.n_slot, self.n_slot + S, acts.shape[1:], acts.dtype, dev, None)
+            self.acts[self.n_slot:self.n_slot + S].copy_(acts)
+        self._pending = None
+        self.batch_counts.append(list(counts))
+        for e, n in enumerate(counts):
+            self.counts[e] += n
+        self.n_tok += T
+        self.n_slot += S
+
+    def slot_experts(self, device) -> torch.Tensor:
+        E = self.E
+        return torch.cat([torch.repeat_interleave(torch.arange(E, device=device), torch.tensor(c, device=device),
+                                                  output_size=sum(c)) for c in self.batch_counts])
+
+    def nbytes(self) -> int:
+        return sum(x.numel() * x.element_size() for x in (self.inputs, self.acts, self.tok) if x is not None)
+
+
 class CaptureManager:
     """Owns all stashes and hooks for one decoder layer (capture.py:100-343).
 
@@ -181,7 +246,8 @@ class CaptureManager:
     tensor in one batch share one stash; fused experts are captured from the
     ``F.linear`` calls whose weight is one expert's slice."""
 
-    def __init__(self, layer: torch.nn.Module, exclude_regex, group_size: int, stash_device=None):
+    def __init__(self, layer: torch.nn.Module, exclude_regex, group_size: int, stash_device=None,
+                 reserve_tokens: int | None = None):
         self.layer = layer
         self.stash_device = stash_device
         self.stashes: dict[str, Stash] = {}
@@ -193,10 +259,10 @@ class CaptureManager:
         self._fused_modules: dict[str, torch.nn.Module] = {}
         self._fused_input_stashes: dict[str, Stash] = {}
         self.fallback_experts: dict[str, str] = {}
-        # module -> per batch: (inputs, global token ids by expert, counts, offsets, activations)
-        self._segments: dict[str, list] = {}
+        self._segments: dict[str, SegmentStore] = {}  # sort-based expert modules
+        self.reserve_tokens = reserve_tokens
         self._segment_modules: set[str] = set()
-        self._inputs_cache: dict[str, torch.Tensor] = {}
+        self._slot_experts: dict[str, torch.Tensor] = {}
         self._mode_registry: dict[int, str] = {}
         self._mode = None
         excl = re.compile(exclude_regex) if exclude_regex else None
@@ -272,17 +338,15 @@ class CaptureManager:
 
     def _make_segment_sink(self, module_name: str):
         tasks = [t for t in self.fused_tasks if t.module_name == module_name]
+        E = tasks[0].num_experts
+        store = self._segments.setdefault(module_name, SegmentStore(E, self.reserve_tokens))
 
         def sink(hidden, tok, counts, acts):
-            segs = self._segments.setdefault(module_name, [])
-            base = sum(sg[0].shape[0] for sg in segs)  # rows of the module input captured so far
-            offs = [0]
-            for n in counts:
-                offs.append(offs[-1] + n)
-            segs.append((hidden.detach().clone(), (tok + base).to(torch.int32), list(counts), offs, acts))
+            store.add(hidden.detach(), tok, counts, acts)
             for t in tasks:
                 for e, n in enumerate(counts):
                     self.stashes[t.stash_keys[e]].tokens += n
+        sink.acts_out = store.acts_out
         return sink
 
     def __enter__(self):
@@ -321,10 +385,7 @@ class CaptureManager:
 
     # ---- diagnostics ----
     def total_stash_bytes(self) -> int:
-        seg = sum(x.numel() * x.element_size() for segs in self._segments.values() for sg in segs
-                  for x in (sg[0], sg[1], sg[4]) if x is not None)
-        seg += sum(x.numel() * x.element_size() for c in self._inputs_cache.values()
-                   for x in (c["inputs"], c["acts"], c["slot_tok"], c["slot_expert"]) if x is not None)
+        seg = sum(st.nbytes() for st in self._segments.values())
         return sum(s.nbytes() for s in self.stashes.values()) + seg
 
     def expert_token_stats(self):
@@ -393,45 +454,27 @@ class CaptureManager:
         for s in self._fused_input_stashes.values():
             s.clear()
         self._segments.clear()
-        self._inputs_cache.clear()
+        self._slot_experts.clear()
 
     # ---- rows of one expert, wherever they were captured ----
-    def _module_cache(self, module_name: str, device) -> dict:
-        """The captured batches of a segment-captured expert module joined once per
-        layer: inputs [tokens, in], activations [slots, inter], and per slot its
-        global token id (int32) and expert (int64). The per-batch copies are dropped."""
-        cache = self._inputs_cache.get(module_name)
-        if cache is not None:
-            return cache
-        segs = self._segments[module_name]
-        E = len(segs[0][2])
-        experts = [torch.repeat_interleave(torch.arange(E, device=device),
-                                           torch.tensor(sg[2], device=device), output_size=sg[3][-1])
-                   for sg in segs]
-        cache = {"inputs": torch.cat([sg[0].to(device) for sg in segs], 0),
-                 "acts": torch.cat([sg[4].to(device) for sg in segs], 0) if segs[0][4] is not None else None,
-                 "slot_tok": torch.cat([sg[1].to(device) for sg in segs]),
-                 "slot_expert": torch.cat(experts),
-                 "counts": [sum(sg[2][e] for sg in segs) for e in range(E)]}
-        self._segments[module_name] = [(None, None, sg[2], sg[3], None) for sg in segs]
-        self._inputs_cache[module_name] = cache
-        return cache
-
     def _segment_rows(self, task: FusedExpertTask, experts, device):
         """(X, idx, counts) covering the segment-captured rows of `experts`, expert
         by expert in capture order (batch, then slot): idx int32 rows of X, counts
         per expert. None if the task was captured through F.linear."""
-        if not self._segments.get(task.module_name):
+        st = self._segments.get(task.module_name)
+        if st is None or st.n_slot == 0:
             return None
-        c = self._module_cache(task.module_name, device)
-        counts = [c["counts"][e] for e in experts]
-        S = c["slot_expert"].shape[0]
-        pos = torch.full((len(c["counts"]),), len(experts), dtype=torch.int64, device=device)
+        se = self._slot_experts.get(task.module_name)
+        if se is None:
+            se = self._slot_experts[task.module_name] = st.slot_experts(device)
+        counts = [st.counts[e] for e in experts]
+        S = st.n_slot
+        pos = torch.full((st.E,), len(experts), dtype=torch.int64, device=device)
         pos[torch.tensor(experts, dtype=torch.int64, device=device)] = torch.arange(len(experts), device=device)
-        order = torch.argsort(pos[c["slot_expert"]] * S + torch.arange(S, device=device))[:sum(counts)]
+        order = torch.argsort(pos[se] * S + torch.arange(S, device=device))[:sum(counts)]
         if task.param_name == "down_proj":
-            return c["acts"], order.to(torch.int32), counts
-        return c["inputs"], c["slot_tok"][order], counts
+            return st.acts[:S], order.to(torch.int32), counts
+        return st.inputs[:st.n_tok], st.tok[:S][order], counts
 
     @torch.no_grad()
     def expert_rows(self, task: FusedExpertTask, expert: int, device) -> torch.Tensor:

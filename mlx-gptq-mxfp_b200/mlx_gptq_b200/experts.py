@@ -120,7 +120,9 @@ def grouped_experts_forward(self, hidden_states: torch.Tensor, top_k_index: torc
     gu = _expert_gemm(x, self.gate_up_proj, counts, offs)
     del x
     gate, up = gu.chunk(2, dim=-1)
-    h = self.act_fn(gate) * up
+    sink = getattr(self, "_gq_sink", None)
+    h_out = sink.acts_out(S, T, self.down_proj.shape[-1], hidden_states.dtype, hidden_states.device) if sink is not None else None
+    h = torch.mul(self.act_fn(gate), up, out=h_out) if h_out is not None else self.act_fn(gate) * up
     del gu, gate, up
     y = _expert_gemm(h, self.down_proj, counts, offs)
     y = y * top_k_weights[tok, pos, None]
@@ -135,7 +137,6 @@ def grouped_experts_forward(self, hidden_states: torch.Tensor, top_k_index: torc
             sel = by_rank[off:off + n]
             out.index_add_(0, tok.index_select(0, sel), y.index_select(0, sel))
             off += n
-    sink = getattr(self, "_gq_sink", None)
     if sink is not None:
         sink(hidden_states, tok, counts, h)
     return out

@@ -31,8 +31,9 @@ import torch
 
 from . import _lib as L
 from .capture import CaptureManager, FusedExpertTask
+from .artifacts import pack_nibbles, unpack_nibbles
 from .gptq import solve_gptq
-from .grid import MX_GROUP_SIZE
+from .grid import MX_GROUP_SIZE, dequantize_artifact
 
 
 @dataclass
@@ -128,14 +129,15 @@ def _nbytes(shape, dtype) -> int:
     return n * torch.empty(0, dtype=dtype).element_size()
 
 
-def _linear_spec(R: int, C: int, args: "LayerSolveArgs", weight_dtype):
-    """(shape, dtype) of one solved linear's outputs in packing order:
-    codes, scales, [biases,] dequantized weight, rel_err."""
+def _linear_spec(R: int, C: int, args: "LayerSolveArgs", bits: int, weight_dtype):
+    """(shape, dtype) of one solved linear's outputs in broadcast order: codes
+    (nibble-packed when bits <= 4), scales, [biases, dequantized weight (affine),]
+    rel_err. MXFP weights are dequantized by each receiver."""
     sdt = torch.uint8 if args.mode != "affine" else args.storage_dtype
-    spec = [((R, C), torch.uint8), ((R, C // args.group_size), sdt)]
+    spec = [((R, C // 2 if bits <= 4 else C), torch.uint8), ((R, C // args.group_size), sdt)]
     if args.mode == "affine":
-        spec.append(((R, C // args.group_size), sdt))
-    return spec + [((R, C), weight_dtype), ((1,), torch.float32)]
+        spec += [((R, C // args.group_size), sdt), ((R, C), weight_dtype)]
+    return spec + [((1,), torch.float32)]
 
 
 def _agreed_counts(counts, group, device):
@@ -253,7 +255,10 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
     timer("linears")
 
     # phase 2: exchange (one all-gather per expert output tensor, one broadcast per
-    # linear), then every rank writes the dequantized weights back into its layer
+    # linear), then every rank writes the dequantized weights back into its layer.
+    # MXFP codes travel nibble-packed and every rank dequantizes them itself: the
+    # dequantized artifact is bit-identical to the solver's W_dq on these grids.
+    local_dq = args.mode != "affine"
     for ti, task in enumerate(mgr.fused_tasks):
         p = task.param
         E, R, C = p.shape
@@ -262,30 +267,39 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
         order = list(shares[rank])
         if world > 1:
             counts = [len(x) for x in shares]
-            q = _all_gather_rows(q, counts, group)
+            packed = bits <= 4
+            q = _all_gather_rows(pack_nibbles(q) if packed else q, counts, group)
+            q = unpack_nibbles(q) if packed else q
             s = _all_gather_rows(s, counts, group)
             if b is not None:
                 b = _all_gather_rows(b, counts, group)
-            W_dq = _all_gather_rows(W_dq, counts, group)
             rel = _all_gather_rows(rel, counts, group)
+            if local_dq:
+                W_dq = dequantize_artifact(q, s, None, args.mode, args.group_size).to(p.dtype)
+            else:
+                W_dq = _all_gather_rows(W_dq, counts, group)
             order = [e for share in shares for e in share]
             timer("all_gather")
-        idx = torch.tensor(order, dtype=torch.long)
-        p.data[idx.to(p.device)] = W_dq.to(p.dtype).to(p.device)
+        if order == list(range(E)):
+            p.data.copy_(W_dq.to(p.dtype))
+        else:
+            p.data.index_copy_(0, torch.tensor(order, dtype=torch.long, device=p.device),
+                               W_dq.to(p.dtype).to(p.device))
         rel_h = rel.tolist()
+        split = task.param_name == "gate_up_proj"
+        parts = 2 if split else 1
+        qv = q.reshape(len(order) * parts, R // parts, C).unbind(0)
+        sv = s.reshape(len(order) * parts, R // parts, -1).unbind(0)
+        bv = b.reshape(len(order) * parts, R // parts, -1).unbind(0) if b is not None else [None] * len(qv)
         for i, e in enumerate(order):
             names = artifact_names_for_fused(layer_prefix, task, e)
-            if len(names) == 1:
-                halves = [(q[i], s[i], None if b is None else b[i])]
-            else:
-                halves = [(q[i, : R // 2], s[i, : R // 2], None if b is None else b[i, : R // 2]),
-                          (q[i, R // 2:], s[i, R // 2:], None if b is None else b[i, R // 2:])]
-            for nm, (qq, ss, bb) in zip(names, halves):
-                result.add(nm, qq, ss, bb, {
-                    "bits": bits, "group_size": args.group_size, "mode": args.mode, "kind": "expert",
-                    "out_features": qq.shape[0], "in_features": C,
+            info = {"bits": bits, "group_size": args.group_size, "mode": args.mode, "kind": "expert",
+                    "out_features": R // parts, "in_features": C,
                     "tokens": mgr.stashes[task.stash_keys[e]].tokens, "rel_err": round(rel_h[i], 6),
-                    "fallback": mgr.fallback_experts.get(task.stash_keys[e])})
+                    "fallback": mgr.fallback_experts.get(task.stash_keys[e])}
+            for h, nm in enumerate(names):
+                j = i * parts + h
+                result.add(nm, qv[j], sv[j], bv[j], dict(info))
         timer("write_back")
 
     if world > 1:
@@ -296,12 +310,15 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
             src = dist.get_global_rank(group, owner[key])
             for t in by_stash[key]:
                 R, C = t.module.out_features, t.module.in_features
-                spec = _linear_spec(R, C, args, t.module.weight.dtype)
+                bits = args.bits_for(f"{layer_prefix}.{t.name}.weight")
+                spec = _linear_spec(R, C, args, bits, t.module.weight.dtype)
                 if owner[key] == rank:
-                    q, s_, b, W_dq, rel, bits = local[t.name]
+                    q, s_, b, W_dq, rel, _ = local[t.name]
                     rel_t = torch.tensor([rel], dtype=torch.float32, device=device)
-                    parts = [q, s_] + ([b] if b is not None else []) + [W_dq, rel_t]
-                    buf = torch.cat([x.contiguous().view(torch.uint8).reshape(-1) for x in parts])
+                    parts = [pack_nibbles(q) if bits <= 4 else q, s_]
+                    if args.mode == "affine":
+                        parts += [b, W_dq]
+                    buf = torch.cat([x.contiguous().view(torch.uint8).reshape(-1) for x in parts + [rel_t]])
                 else:
                     buf = torch.empty(sum(_nbytes(sh, dt) for sh, dt in spec), dtype=torch.uint8, device=device)
                 dist.broadcast(buf, src=src, group=group)
@@ -311,9 +328,14 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
                         n = _nbytes(sh, dt)
                         out.append(buf[off:off + n].view(dt).reshape(sh))
                         off += n
-                    b = out[2] if len(spec) == 5 else None
-                    local[t.name] = (out[0], out[1], b, out[-2], float(out[-1][0]),
-                                     args.bits_for(f"{layer_prefix}.{t.name}.weight"))
+                    q = unpack_nibbles(out[0]) if bits <= 4 else out[0]
+                    if args.mode == "affine":
+                        b, W_dq = out[2], out[3]
+                    else:
+                        b = None
+                        W_dq = dequantize_artifact(q, out[1], None, args.mode, args.group_size).to(
+                            t.module.weight.dtype)
+                    local[t.name] = (q, out[1], b, W_dq, float(out[-1][0]), bits)
         timer("all_gather")
     for t in mgr.linear_tasks:
         q, s, b, W_dq, rel, bits = local[t.name]

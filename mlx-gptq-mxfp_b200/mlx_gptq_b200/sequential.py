@@ -442,7 +442,8 @@ class Pipeline:
                 log.info("layer %d: resumed from artifacts (%.1fs)", li, time.time() - t0)
                 continue
 
-            mgr = CaptureManager(layer, self.args.exclude, self.args.group_size, stash_device=self.dev0)
+            mgr = CaptureManager(layer, self.args.exclude, self.args.group_size, stash_device=self.dev0,
+                                 reserve_tokens=sum(h.shape[0] * h.shape[1] for h, _ in batches))
             n_lin = len(mgr.linear_tasks)
             n_exp = sum(t.num_experts for t in mgr.fused_tasks)
             with mgr:

@@ -135,14 +135,38 @@ def test_lpt_partition_balances_and_covers():
     assert lpt_partition([], 4) == [[], [], [], []]
 
 
+def _fake_dequant(q, s, b, mode, group_size):
+    return q.float() * 0.01 * s.float().repeat_interleave(group_size, dim=-1)
+
+
+def _fake_pack(q):
+    return q[..., 0::2] | (q[..., 1::2] << 4)
+
+
+def _fake_unpack(p):
+    return torch.stack([p & 15, p >> 4], dim=-1).reshape(*p.shape[:-1], -1)
+
+
 def _fake_solve(W, H, bits, args):
-    """Deterministic stand-in for the GPU solver (CPU tensors)."""
+    """Deterministic stand-in for the GPU solver (CPU tensors); W_dq is the
+    dequantization of (q, s), as it is for the real MXFP solver."""
     B, R, C = W.shape
-    q = (W.abs() * 7).round().clamp(0, 15).to(torch.uint8)
+    d = H.diagonal(dim1=-2, dim2=-1).unsqueeze(1)
+    q = (W.abs() * 7 + d * 1e-3).round().clamp(0, 15).to(torch.uint8)
     s = torch.full((B, R, C // args.group_size), 3, dtype=torch.uint8)
-    W_dq = W * 0.5 + H.diagonal(dim1=-2, dim2=-1).unsqueeze(1) * 1e-3
+    W_dq = _fake_dequant(q, s, None, args.mode, args.group_size)
     rel = W_dq.flatten(1).norm(dim=1)
     return q, s, None, W_dq, rel
+
+
+def install_fakes(pipeline_mod, capture_mod):
+    """Replace the CUDA pieces the layer solve calls with CPU stand-ins."""
+    pipeline_mod._solve_batch = _fake_solve
+    pipeline_mod.dequantize_artifact = _fake_dequant
+    pipeline_mod.pack_nibbles = _fake_pack
+    pipeline_mod.unpack_nibbles = _fake_unpack
+    capture_mod.CaptureManager.expert_hessians = _fake_expert_hessians
+    capture_mod.Stash.hessian = _fake_stash_hessian
 
 
 def _fake_expert_hessians(self, task, device, experts=None, timer=None):
@@ -160,9 +184,7 @@ def _run_layer(rank, world, port, out_dir):
 
     from mlx_gptq_b200 import capture, pipeline
 
-    pipeline._solve_batch = _fake_solve
-    capture.CaptureManager.expert_hessians = _fake_expert_hessians
-    capture.Stash.hessian = _fake_stash_hessian
+    install_fakes(pipeline, capture)
     group = None
     if world > 1:
         dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)

@@ -141,13 +141,16 @@ def test_synthetic_weights_are_seeded_per_name():
 
 
 def _fake_solver(monkeypatch):
-    from test_pipeline_cpu import _fake_expert_hessians, _fake_solve, _fake_stash_hessian
+    import test_pipeline_cpu as fakes
 
     from mlx_gptq_b200 import capture, pipeline
 
-    monkeypatch.setattr(pipeline, "_solve_batch", _fake_solve)
-    monkeypatch.setattr(capture.CaptureManager, "expert_hessians", _fake_expert_hessians)
-    monkeypatch.setattr(capture.Stash, "hessian", _fake_stash_hessian)
+    monkeypatch.setattr(pipeline, "_solve_batch", fakes._fake_solve)
+    monkeypatch.setattr(pipeline, "dequantize_artifact", fakes._fake_dequant)
+    monkeypatch.setattr(pipeline, "pack_nibbles", fakes._fake_pack)
+    monkeypatch.setattr(pipeline, "unpack_nibbles", fakes._fake_unpack)
+    monkeypatch.setattr(capture.CaptureManager, "expert_hessians", fakes._fake_expert_hessians)
+    monkeypatch.setattr(capture.Stash, "hessian", fakes._fake_stash_hessian)
 
 
 class _Writer:
@@ -192,13 +195,11 @@ def _run_stack(rank, world, port, out_dir):
     import torch.distributed as dist
 
     sys.path.insert(0, os.path.dirname(__file__))
-    from test_pipeline_cpu import _fake_expert_hessians, _fake_solve, _fake_stash_hessian
+    from test_pipeline_cpu import install_fakes
 
     from mlx_gptq_b200 import capture, pipeline
 
-    pipeline._solve_batch = _fake_solve
-    capture.CaptureManager.expert_hessians = _fake_expert_hessians
-    capture.Stash.hessian = _fake_stash_hessian
+    install_fakes(pipeline, capture)
     group = None
     if world > 1:
         dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
