@@ -85,6 +85,16 @@ int gq_selftest_wait_timeout(unsigned long long limit_ns, int32_t* status, int32
 int gq_hessian_bf16(const void* X, int64_t n, int64_t c, int64_t ldx, float* H, int64_t ldh, float alpha,
                     float beta, int32_t* status, void* stream);
 
+/* The same over output tiles [tile_begin, tile_end) of the kernel's schedule
+ * (gq_hessian_tile_count(c) tiles in all, each a block on or above the diagonal
+ * plus its mirror): only those blocks of H are written, with exactly the values
+ * the full call writes there. Ranks that each hold every row of X split one H
+ * this way and merge disjoint blocks; no reference counterpart (the reference
+ * forms each H on one device, mlx_gptq/sequential.py:479-487). */
+int64_t gq_hessian_tile_count(int64_t c);
+int gq_hessian_bf16_range(const void* X, int64_t n, int64_t c, int64_t ldx, float* H, int64_t ldh, float alpha,
+                          float beta, int64_t tile_begin, int64_t tile_end, int32_t* status, void* stream);
+
 /* Per-expert Hessians in one launch:
  * H[e] = beta * H[e] + alpha * sum over t in token_idx[offsets[e] .. offsets[e+1]) of X[t]^T X[t],
  * for e < E. X: bf16 [n, c] (ldx % 8 == 0, c % 8 == 0); token_idx: int32 row indices into X;

@@ -107,7 +107,7 @@ __device__ __forceinline__ void store_row_slab(float* __restrict__ H, int64_t ld
 __global__ void __launch_bounds__(THREADS, 1)
     hessian_kernel(const __grid_constant__ CUtensorMap tmap, int64_t n, int64_t c, float* __restrict__ H,
                    int64_t ldh, float alpha, float beta, int32_t* status, const int32_t* __restrict__ sched,
-                   const int64_t* __restrict__ seg, int64_t tiles_per_expert) {
+                   const int64_t* __restrict__ seg, int64_t tiles_per_expert, int64_t tile_begin) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
@@ -119,7 +119,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t mt = (c + BM - 1) / BM;
-  int64_t t = blockIdx.x, tn = 0, y0 = 0;
+  int64_t t = blockIdx.x + tile_begin, tn = 0, y0 = 0;
   if (sched) {
     const int64_t v = sched[blockIdx.x], e = v / tiles_per_expert;
     t = v % tiles_per_expert;
@@ -347,7 +347,8 @@ __device__ __forceinline__ void umma_commit_2sm(uint64_t* bar) {
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     hessian2_kernel(const __grid_constant__ CUtensorMap tmap, int64_t n, int64_t c, float* __restrict__ H,
                     int64_t ldh, float alpha, float beta, int32_t* status, const int32_t* __restrict__ sched,
-                    const int64_t* __restrict__ seg, int64_t tiles_per_expert) {
+                    const int64_t* __restrict__ seg, int64_t tiles_per_expert,
+                    int64_t tile_begin) {
   constexpr int STAGES = two::STAGES;
   constexpr uint32_t STAGE_BYTES = two::STAGE_BYTES, HALF_BYTES = two::HALF_BYTES;
   using two::arrive_remote;
@@ -368,7 +369,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cta_rank();
-  int64_t q = blockIdx.x >> 1, y0 = 0;
+  int64_t q = (blockIdx.x >> 1) + tile_begin, y0 = 0;
   if (sched) {
     const int64_t v = sched[q], e = v / tiles_per_expert;
     q = v % tiles_per_expert;
@@ -603,17 +604,17 @@ static int64_t tiles_for(int64_t c, bool two_sm) { return two_sm ? two::tiles(c)
 
 static int launch(const CUtensorMap& map, int64_t n, int64_t c, float* H, int64_t ldh, float alpha, float beta,
                   int32_t* status, const int32_t* sched, const int64_t* seg, int64_t tpe, int64_t units,
-                  bool two_sm, cudaStream_t s) {
+                  bool two_sm, cudaStream_t s, int64_t tile_begin = 0) {
   if (two_sm) {
     GQ_CUDA_TRY(cudaFuncSetAttribute(hessian2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      int(two::SMEM_BYTES)));
     hessian2_kernel<<<unsigned(2 * units), THREADS, two::SMEM_BYTES, s>>>(map, n, c, H, ldh, alpha, beta, status,
-                                                                         sched, seg, tpe);
+                                                                         sched, seg, tpe, tile_begin);
     return check_launch("hessian2_kernel");
   }
   GQ_CUDA_TRY(cudaFuncSetAttribute(hessian_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(SMEM_BYTES)));
   hessian_kernel<<<unsigned(units), THREADS, SMEM_BYTES, s>>>(map, n, c, H, ldh, alpha, beta, status, sched, seg,
-                                                              tpe);
+                                                              tpe, tile_begin);
   return check_launch("hessian_kernel");
 }
 }  // namespace hess
@@ -670,13 +671,26 @@ extern "C" int gq_hessian_grouped_bf16(const void* X, int64_t n, int64_t c, int6
   return hess::launch(map, 0, c, H, c, alpha, beta, status, sched, seg, tpe, int64_t(plan.sched.size()), two_sm, s);
 }
 
-extern "C" int gq_hessian_bf16(const void* X, int64_t n, int64_t c, int64_t ldx, float* H, int64_t ldh, float alpha,
-                               float beta, int32_t* status, void* stream) {
+extern "C" int64_t gq_hessian_tile_count(int64_t c) {
+  if (c <= 0) return 0;
+  return gq::hess::tiles_for(c, gq::hess::use_2sm());
+}
+
+extern "C" int gq_hessian_bf16_range(const void* X, int64_t n, int64_t c, int64_t ldx, float* H, int64_t ldh,
+                                     float alpha, float beta, int64_t tile_begin, int64_t tile_end, int32_t* status,
+                                     void* stream) {
   GQ_REQUIRE(H && (X || n == 0), "gq_hessian_bf16: null pointer");
   GQ_REQUIRE(n >= 0 && c > 0 && n < (int64_t(1) << 31) && c < (int64_t(1) << 31), "gq_hessian_bf16: sizes");
   GQ_REQUIRE(ldh >= c && ldh % 4 == 0 && aligned16(H), "gq_hessian_bf16: H must be 16-byte aligned, ldh %% 4 == 0");
+  const bool two_sm = hess::use_2sm();
+  const int64_t tiles = hess::tiles_for(c, two_sm);
+  GQ_REQUIRE(tile_begin >= 0 && tile_begin <= tile_end && tile_end <= tiles,
+             "gq_hessian_bf16_range: tile range [%lld, %lld) outside [0, %lld)", (long long)tile_begin,
+             (long long)tile_end, (long long)tiles);
   cudaStream_t s = (cudaStream_t)stream;
+  if (tile_end == tile_begin) return GQ_OK;
   if (n == 0) {
+    GQ_REQUIRE(tile_begin == 0 && tile_end == tiles, "gq_hessian_bf16_range: n == 0 needs the full tile range");
     if (beta == 1.0f) return GQ_OK;
     hess::scale_kernel<<<unsigned((c * c + 255) / 256), 256, 0, s>>>(H, c, ldh, beta);
     return check_launch("hessian scale_kernel");
@@ -685,7 +699,12 @@ extern "C" int gq_hessian_bf16(const void* X, int64_t n, int64_t c, int64_t ldx,
   CUtensorMap map;
   int st = hess::make_x_map(&map, X, n, c, ldx);
   if (st != GQ_OK) return st;
-  const bool two_sm = hess::use_2sm();
-  const int64_t tiles = hess::tiles_for(c, two_sm);
-  return hess::launch(map, n, c, H, ldh, alpha, beta, status, nullptr, nullptr, tiles, tiles, two_sm, s);
+  return hess::launch(map, n, c, H, ldh, alpha, beta, status, nullptr, nullptr, tiles, tile_end - tile_begin, two_sm,
+                      s, tile_begin);
+}
+
+extern "C" int gq_hessian_bf16(const void* X, int64_t n, int64_t c, int64_t ldx, float* H, int64_t ldh, float alpha,
+                               float beta, int32_t* status, void* stream) {
+  GQ_REQUIRE(c > 0, "gq_hessian_bf16: sizes");
+  return gq_hessian_bf16_range(X, n, c, ldx, H, ldh, alpha, beta, 0, gq_hessian_tile_count(c), status, stream);
 }

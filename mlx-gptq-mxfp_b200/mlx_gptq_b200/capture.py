@@ -33,11 +33,17 @@ log = logging.getLogger(__name__)
 FUSED_EXPERT_PARAMS = ("gate_up_proj", "gate_proj", "up_proj", "down_proj")
 
 
+def hessian_tile_count(c: int) -> int:
+    """Output tiles of the Hessian kernel for c features (see hessian_accumulate's `tiles`)."""
+    return int(L.lib().gq_hessian_tile_count(int(c)))
+
+
 @torch.no_grad()
 def hessian_accumulate(X: torch.Tensor, H: torch.Tensor, alpha: float = 1.0, beta: float = 1.0,
-                       status: torch.Tensor | None = None) -> torch.Tensor:
+                       status: torch.Tensor | None = None, tiles: tuple[int, int] | None = None) -> torch.Tensor:
     """H = beta * H + alpha * X^T X for bf16 rows X [n, c] and float32 H [c, c], both on
-    the same CUDA device. Returns H."""
+    the same CUDA device. Returns H. With tiles=(begin, end) only the blocks of those
+    output tiles (of hessian_tile_count(c)) are written, bit-identical to a full call."""
     L.require_cuda(X, H)
     if X.dtype != torch.bfloat16:
         raise ValueError("X must be bfloat16 (the capture dtype)")
@@ -50,8 +56,13 @@ def hessian_accumulate(X: torch.Tensor, H: torch.Tensor, alpha: float = 1.0, bet
     if H.stride(1) != 1 or H.stride(0) % 4 or H.data_ptr() % 16:
         raise ValueError("H must be row-major, 16-byte aligned, row stride % 4 == 0")
     n, c = X.shape
-    L.check(L.lib().gq_hessian_bf16(L.ptr(X), n, c, X.stride(0), L.ptr(H), H.stride(0), float(alpha),
-                                    float(beta), L.ptr(status), L.stream_ptr(X.device)), "hessian")
+    if tiles is None:
+        L.check(L.lib().gq_hessian_bf16(L.ptr(X), n, c, X.stride(0), L.ptr(H), H.stride(0), float(alpha),
+                                        float(beta), L.ptr(status), L.stream_ptr(X.device)), "hessian")
+    else:
+        L.check(L.lib().gq_hessian_bf16_range(L.ptr(X), n, c, X.stride(0), L.ptr(H), H.stride(0), float(alpha),
+                                              float(beta), int(tiles[0]), int(tiles[1]), L.ptr(status),
+                                              L.stream_ptr(X.device)), "hessian")
     return H
 
 
@@ -130,12 +141,15 @@ class Stash:
         return sum(c.numel() * 2 for c in self.chunks)
 
     @torch.no_grad()
-    def hessian(self, device, chunk_rows: int = 65536) -> torch.Tensor:
-        """H = X^T X in float32 on `device` (a CUDA device)."""
+    def hessian(self, device, chunk_rows: int = 65536, tiles: tuple[int, int] | None = None) -> torch.Tensor:
+        """H = X^T X in float32 on `device` (a CUDA device). With tiles=(begin, end)
+        only those output tiles are formed and the rest of H is zero."""
         device = torch.device(device)
         if device.type != "cuda":
             raise RuntimeError("mlx_gptq_b200 forms Hessians on CUDA devices only")
         H = torch.empty(self.in_features, self.in_features, dtype=torch.float32, device=device)
+        if tiles is not None:
+            H.zero_()
         beta = 0.0
         for c in self.chunks:
             for i in range(0, c.shape[0], chunk_rows):
@@ -143,9 +157,9 @@ class Stash:
                 if x.shape[0] == 0:
                     continue
                 xd = x.to(device, torch.bfloat16, non_blocking=True)
-                hessian_accumulate(xd, H, 1.0, beta)
+                hessian_accumulate(xd, H, 1.0, beta, tiles=tiles)
                 beta = 1.0
-        if beta == 0.0:
+        if beta == 0.0 and tiles is None:
             H.zero_()
         return H
 

@@ -30,7 +30,7 @@ from dataclasses import dataclass, field
 import torch
 
 from . import _lib as L
-from .capture import CaptureManager, FusedExpertTask
+from .capture import CaptureManager, FusedExpertTask, hessian_tile_count
 from .artifacts import pack_nibbles, unpack_nibbles
 from .gptq import solve_gptq
 from .grid import MX_GROUP_SIZE, dequantize_artifact
@@ -159,11 +159,16 @@ SOLVE_COST_PER_ELEM = 1.0e4
 
 
 def plan_layer(mgr: CaptureManager, world: int, group=None, device="cpu"):
-    """One longest-processing-time partition of a layer's work over `world` ranks:
-    every expert of every fused task and every linear stash (its Hessian, shared by
-    the sibling linears that read it, plus their solves) is one item. Returns, per
-    rank, {"experts": {task index: [expert, ...]}, "linears": [stash key, ...]}.
-    Token counts are rank 0's, so every rank derives the same plan."""
+    """One longest-processing-time partition of a layer's work over `world` ranks.
+
+    Items: every expert of every fused task (its Hessian and solve) and every plain
+    linear (its solve). With one rank a linear stash's Hessian is formed once and
+    shared by the sibling linears that read it; with several, every rank forms an
+    equal share of the tiles of every linear Hessian, so those costs are the same on
+    every rank and stay out of the partition. Returns, per rank,
+    {"experts": {task index: [expert, ...]}, "linears": [linear name, ...]} and the
+    stash key -> linear tasks map. Token counts are rank 0's, so every rank derives
+    the same plan."""
     by_stash: dict[str, list] = {}
     for t in mgr.linear_tasks:
         by_stash.setdefault(t.stash_key, []).append(t)
@@ -182,9 +187,12 @@ def plan_layer(mgr: CaptureManager, world: int, group=None, device="cpu"):
             i += 1
     for k in keys:
         C = mgr.stashes[k].in_features
-        items.append(("linear", k, None))
-        costs.append(float(counts[i]) * C * C + SOLVE_COST_PER_ELEM * sum(
-            t.module.out_features * C for t in by_stash[k]))
+        if world == 1:
+            items.append(("stash", k, None))
+            costs.append(float(counts[i]) * C * C)
+        for t in by_stash[k]:
+            items.append(("linear", t.name, None))
+            costs.append(SOLVE_COST_PER_ELEM * t.module.out_features * C)
         i += 1
     plans = [{"experts": {ti: [] for ti in range(len(mgr.fused_tasks))}, "linears": []} for _ in range(world)]
     for r, share in enumerate(lpt_partition(costs, world)):
@@ -192,7 +200,7 @@ def plan_layer(mgr: CaptureManager, world: int, group=None, device="cpu"):
             kind, a, e = items[j]
             if kind == "expert":
                 plans[r]["experts"][a].append(e)
-            else:
+            elif kind == "linear":
                 plans[r]["linears"].append(a)
     return plans, by_stash
 
@@ -209,13 +217,29 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
     rank = dist.get_rank(group) if group is not None else 0
     plans, by_stash = plan_layer(mgr, world, group, device)
 
-    # phase 1: this rank's own work, no collectives (a rank with a large linear does
-    # not hold the others up at an expert all-gather)
     t0 = time.perf_counter()
 
     def timer(stage):
         nonlocal t0
         t0 = result._tick(stage, t0, device)
+
+    # phase 0 (several ranks): every rank forms an equal share of the output tiles of
+    # every linear Hessian from its own copy of the stashed rows; the shares are
+    # disjoint blocks, so their sum over ranks is the single-device H bit for bit
+    # (each element has one non-zero contribution)
+    lin_H: dict[str, torch.Tensor] = {}
+    if world > 1 and by_stash:
+        for key in sorted(by_stash):
+            st = mgr.stashes[key]
+            T = hessian_tile_count(st.in_features)
+            lin_H[key] = st.hessian(device, tiles=(rank * T // world, (rank + 1) * T // world))
+        timer("linear_hessians")
+        for key in sorted(by_stash):
+            dist.all_reduce(lin_H[key], op=dist.ReduceOp.SUM, group=group)
+        timer("hessian_merge")
+
+    # phase 1: this rank's own work, no collectives (a rank with a large item does
+    # not hold the others up at an all-gather)
 
     fused_out = []
     for ti, task in enumerate(mgr.fused_tasks):
@@ -241,17 +265,21 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
         fused_out.append((bits, q, s, b, W_dq, rel))
 
     # plain linears: one Hessian per stash, shared by the siblings that read the same input
-    my_keys = plans[rank]["linears"]
+    mine = set(plans[rank]["linears"])
     local = {}
-    for key in my_keys:
-        H0 = mgr.stashes[key].hessian(device)
-        for t in by_stash[key]:
+    for key in sorted(by_stash):
+        todo = [t for t in by_stash[key] if t.name in mine]
+        if not todo:
+            continue
+        H0 = lin_H[key] if key in lin_H else mgr.stashes[key].hessian(device)
+        for t in todo:
             name = f"{layer_prefix}.{t.name}.weight"
             bits = args.bits_for(name)
             W = t.module.weight.detach().to(device, torch.float32).unsqueeze(0)
             q, s, b, W_dq, rel = _solve_batch(W, H0.clone().unsqueeze(0), bits, args)
             local[t.name] = (q[0], s[0], None if b is None else b[0], W_dq[0].to(t.module.weight.dtype),
                              float(rel[0]), bits)
+    del lin_H
     timer("linears")
 
     # phase 2: exchange (one all-gather per expert output tensor, one broadcast per
@@ -305,14 +333,14 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
     if world > 1:
         # every linear's outputs reach every rank from the rank that solved it: one
         # broadcast of a packed byte buffer per linear, all ranks in stash-key order
-        owner = {k: r for r in range(world) for k in plans[r]["linears"]}
+        owner = {name: r for r in range(world) for name in plans[r]["linears"]}
         for key in sorted(by_stash):
-            src = dist.get_global_rank(group, owner[key])
             for t in by_stash[key]:
+                src = dist.get_global_rank(group, owner[t.name])
                 R, C = t.module.out_features, t.module.in_features
                 bits = args.bits_for(f"{layer_prefix}.{t.name}.weight")
                 spec = _linear_spec(R, C, args, bits, t.module.weight.dtype)
-                if owner[key] == rank:
+                if owner[t.name] == rank:
                     q, s_, b, W_dq, rel, _ = local[t.name]
                     rel_t = torch.tensor([rel], dtype=torch.float32, device=device)
                     parts = [pack_nibbles(q) if bits <= 4 else q, s_]
@@ -322,7 +350,7 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
                 else:
                     buf = torch.empty(sum(_nbytes(sh, dt) for sh, dt in spec), dtype=torch.uint8, device=device)
                 dist.broadcast(buf, src=src, group=group)
-                if owner[key] != rank:
+                if owner[t.name] != rank:
                     out, off = [], 0
                     for sh, dt in spec:
                         n = _nbytes(sh, dt)

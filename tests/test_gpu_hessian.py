@@ -144,3 +144,29 @@ def test_hessian_grouped_vs_oracle_and_beta():
     for e in range(E):
         den = max(float(np.linalg.norm(ref[e])), 1e-30)
         assert float(np.linalg.norm(got[e] - ref[e])) / den < 1e-5 or den < 1e-20
+
+
+@pytest.mark.parametrize("parts", [3, 8])
+@pytest.mark.parametrize("c", [1088, 2048])
+def test_hessian_tile_ranges_compose_bit_exact(parts, c):
+    """Disjoint tile ranges write disjoint blocks whose union is the full H, bit for bit
+    (how ranks holding every row of X split one Hessian)."""
+    from mlx_gptq_b200.capture import hessian_accumulate, hessian_from_rows, hessian_tile_count
+
+    g = torch.Generator(device="cuda").manual_seed(c + parts)
+    X = torch.randn(3000, c, generator=g, device="cuda").to(torch.bfloat16)
+    full = hessian_from_rows(X)
+    T = hessian_tile_count(c)
+    assert T > parts
+    total = torch.zeros(c, c, device="cuda")
+    written = torch.zeros(c, c, dtype=torch.int32, device="cuda")
+    for r in range(parts):
+        Hr = torch.full((c, c), float("nan"), device="cuda")
+        hessian_accumulate(X, Hr, 1.0, 0.0, tiles=(r * T // parts, (r + 1) * T // parts))
+        mine = ~torch.isnan(Hr)
+        written += mine.int()
+        total += torch.where(mine, Hr, torch.zeros_like(Hr))
+    assert bool((written == 1).all())  # every element written by exactly one range
+    assert torch.equal(total, full)
+    with pytest.raises(ValueError):
+        hessian_accumulate(X, full, 1.0, 0.0, tiles=(0, T + 1))

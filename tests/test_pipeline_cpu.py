@@ -165,6 +165,7 @@ def install_fakes(pipeline_mod, capture_mod):
     pipeline_mod.dequantize_artifact = _fake_dequant
     pipeline_mod.pack_nibbles = _fake_pack
     pipeline_mod.unpack_nibbles = _fake_unpack
+    pipeline_mod.hessian_tile_count = _fake_tile_count
     capture_mod.CaptureManager.expert_hessians = _fake_expert_hessians
     capture_mod.Stash.hessian = _fake_stash_hessian
 
@@ -175,8 +176,18 @@ def _fake_expert_hessians(self, task, device, experts=None, timer=None):
     return torch.stack([torch.eye(C) * (self.stashes[task.stash_keys[e]].tokens + 1) for e in experts])
 
 
-def _fake_stash_hessian(self, device, chunk_rows=65536):
-    return torch.eye(self.in_features) * (self.tokens + 1)
+def _fake_stash_hessian(self, device, chunk_rows=65536, tiles=None):
+    """A stand-in H; with tiles=(b, e) only rows b..e (one "tile" per row), zero elsewhere."""
+    H = torch.eye(self.in_features) * (self.tokens + 1) + 0.01 * torch.arange(self.in_features).float()
+    if tiles is not None:
+        mask = torch.zeros(self.in_features, 1)
+        mask[tiles[0]:tiles[1]] = 1
+        H = H * mask
+    return H
+
+
+def _fake_tile_count(c):
+    return c
 
 
 def _run_layer(rank, world, port, out_dir):
@@ -241,6 +252,6 @@ def test_plan_layer_covers_every_item_once_and_balances():
         for ti, task in enumerate(mgr.fused_tasks):
             got = sorted(e for p in plans for e in p["experts"][ti])
             assert got == list(range(task.num_experts))
-        assert sorted(k for p in plans for k in p["linears"]) == sorted(by_stash)
+        assert sorted(k for p in plans for k in p["linears"]) == sorted(t.name for t in mgr.linear_tasks)
     # q/k share one stash: one linear item
     assert len(by_stash) == 1 and len(next(iter(by_stash.values()))) == 2

@@ -149,6 +149,7 @@ def _fake_solver(monkeypatch):
     monkeypatch.setattr(pipeline, "dequantize_artifact", fakes._fake_dequant)
     monkeypatch.setattr(pipeline, "pack_nibbles", fakes._fake_pack)
     monkeypatch.setattr(pipeline, "unpack_nibbles", fakes._fake_unpack)
+    monkeypatch.setattr(pipeline, "hessian_tile_count", fakes._fake_tile_count)
     monkeypatch.setattr(capture.CaptureManager, "expert_hessians", fakes._fake_expert_hessians)
     monkeypatch.setattr(capture.Stash, "hessian", fakes._fake_stash_hessian)
 
