@@ -92,6 +92,10 @@ int gq_hessian_bf16(const void* X, int64_t n, int64_t c, int64_t ldx, float* H, 
  * this way and merge disjoint blocks; no reference counterpart (the reference
  * forms each H on one device, mlx_gptq/sequential.py:479-487). */
 int64_t gq_hessian_tile_count(int64_t c);
+/* Tiles the kernel runs at once on a GPU with sm_count SMs (one per CTA pair for
+ * the default kernel). Each tile sweeps every row of X, so a range of at most this
+ * many tiles takes about as long as one wave. */
+int64_t gq_hessian_concurrent_tiles(int64_t sm_count);
 int gq_hessian_bf16_range(const void* X, int64_t n, int64_t c, int64_t ldx, float* H, int64_t ldh, float alpha,
                           float beta, int64_t tile_begin, int64_t tile_end, int32_t* status, void* stream);
 

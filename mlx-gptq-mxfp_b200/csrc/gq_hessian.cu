@@ -676,6 +676,11 @@ extern "C" int64_t gq_hessian_tile_count(int64_t c) {
   return gq::hess::tiles_for(c, gq::hess::use_2sm());
 }
 
+extern "C" int64_t gq_hessian_concurrent_tiles(int64_t sm_count) {
+  if (sm_count <= 0) return 0;
+  return gq::hess::use_2sm() ? sm_count / 2 : sm_count;  // one tile per CTA pair, or per CTA
+}
+
 extern "C" int gq_hessian_bf16_range(const void* X, int64_t n, int64_t c, int64_t ldx, float* H, int64_t ldh,
                                      float alpha, float beta, int64_t tile_begin, int64_t tile_end, int32_t* status,
                                      void* stream) {

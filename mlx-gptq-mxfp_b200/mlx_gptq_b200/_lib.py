@@ -35,6 +35,7 @@ SIGNATURES = {
     "gq_selftest_wait_timeout": (I32, [ctypes.c_ulonglong, P, P, P]),
     "gq_hessian_bf16": (I32, [P, I64, I64, I64, P, I64, F32, F32, P, P]),
     "gq_hessian_tile_count": (I64, [I64]),
+    "gq_hessian_concurrent_tiles": (I64, [I64]),
     "gq_hessian_bf16_range": (I32, [P, I64, I64, I64, P, I64, F32, F32, I64, I64, P, P]),
     "gq_hessian_grouped_workspace_size": (SZ, [P, I64, I64]),
     "gq_hessian_grouped_bf16": (I32, [P, I64, I64, I64, P, P, P, I64, P, F32, F32, P, SZ, P, P]),

@@ -38,6 +38,12 @@ def hessian_tile_count(c: int) -> int:
     return int(L.lib().gq_hessian_tile_count(int(c)))
 
 
+def hessian_tiles_per_wave(device=None) -> int:
+    """Output tiles the Hessian kernel runs at once on `device`."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    return int(L.lib().gq_hessian_concurrent_tiles(torch.cuda.get_device_properties(dev).multi_processor_count))
+
+
 @torch.no_grad()
 def hessian_accumulate(X: torch.Tensor, H: torch.Tensor, alpha: float = 1.0, beta: float = 1.0,
                        status: torch.Tensor | None = None, tiles: tuple[int, int] | None = None) -> torch.Tensor:

@@ -30,7 +30,7 @@ from dataclasses import dataclass, field
 import torch
 
 from . import _lib as L
-from .capture import CaptureManager, FusedExpertTask, hessian_tile_count
+from .capture import CaptureManager, FusedExpertTask, hessian_tile_count, hessian_tiles_per_wave
 from .artifacts import pack_nibbles, unpack_nibbles
 from .gptq import solve_gptq
 from .grid import MX_GROUP_SIZE, dequantize_artifact
@@ -158,17 +158,24 @@ def _agreed_counts(counts, group, device):
 SOLVE_COST_PER_ELEM = 1.0e4
 
 
-def plan_layer(mgr: CaptureManager, world: int, group=None, device="cpu"):
+def _wave_parts(tiles: int, per_wave: int, world: int) -> list[tuple[int, int]]:
+    """Split a Hessian's output tiles into the fewest ranges of at most one wave each
+    (each tile sweeps every token, so a range takes about one wave however few
+    tiles it has), and no more ranges than ranks."""
+    parts = 1 if world == 1 else min(world, max(1, -(-tiles // max(1, per_wave))))
+    return [(i * tiles // parts, (i + 1) * tiles // parts) for i in range(parts)]
+
+
+def plan_layer(mgr: CaptureManager, world: int, group=None, device="cpu", per_wave: int | None = None):
     """One longest-processing-time partition of a layer's work over `world` ranks.
 
-    Items: every expert of every fused task (its Hessian and solve) and every plain
-    linear (its solve). With one rank a linear stash's Hessian is formed once and
-    shared by the sibling linears that read it; with several, every rank forms an
-    equal share of the tiles of every linear Hessian, so those costs are the same on
-    every rank and stay out of the partition. Returns, per rank,
-    {"experts": {task index: [expert, ...]}, "linears": [linear name, ...]} and the
-    stash key -> linear tasks map. Token counts are rank 0's, so every rank derives
-    the same plan."""
+    Items: every expert of every fused task (its Hessian and solve), every part of
+    every plain-linear stash Hessian (a range of output tiles of at most one wave;
+    a single part with one rank) and every plain linear's solve. Returns, per rank,
+    {"experts": {task index: [expert, ...]}, "hessian_parts": [(stash key, begin,
+    end), ...], "linears": [linear name, ...]}, the stash key -> linear tasks map
+    and the stash key -> tile ranges map. Token counts are rank 0's, so every rank
+    derives the same plan."""
     by_stash: dict[str, list] = {}
     for t in mgr.linear_tasks:
         by_stash.setdefault(t.stash_key, []).append(t)
@@ -185,24 +192,30 @@ def plan_layer(mgr: CaptureManager, world: int, group=None, device="cpu"):
             items.append(("expert", ti, e))
             costs.append(float(counts[i]) * C * C + SOLVE_COST_PER_ELEM * R * C)
             i += 1
+    ranges = {}
     for k in keys:
         C = mgr.stashes[k].in_features
-        if world == 1:
-            items.append(("stash", k, None))
-            costs.append(float(counts[i]) * C * C)
+        T = hessian_tile_count(C) if world > 1 else 1
+        ranges[k] = _wave_parts(T, per_wave or T, world)
+        for b, e in ranges[k]:
+            items.append(("hessian", k, (b, e)))
+            costs.append(float(counts[i]) * C * C / len(ranges[k]))
         for t in by_stash[k]:
             items.append(("linear", t.name, None))
             costs.append(SOLVE_COST_PER_ELEM * t.module.out_features * C)
         i += 1
-    plans = [{"experts": {ti: [] for ti in range(len(mgr.fused_tasks))}, "linears": []} for _ in range(world)]
+    plans = [{"experts": {ti: [] for ti in range(len(mgr.fused_tasks))}, "hessian_parts": [], "linears": []}
+             for _ in range(world)]
     for r, share in enumerate(lpt_partition(costs, world)):
         for j in share:
             kind, a, e = items[j]
             if kind == "expert":
                 plans[r]["experts"][a].append(e)
-            elif kind == "linear":
+            elif kind == "hessian":
+                plans[r]["hessian_parts"].append((a,) + tuple(e))
+            else:
                 plans[r]["linears"].append(a)
-    return plans, by_stash
+    return plans, by_stash, ranges
 
 
 @torch.no_grad()
@@ -215,7 +228,8 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
     result = SolveResult(on_device)
     world = dist.get_world_size(group) if group is not None else 1
     rank = dist.get_rank(group) if group is not None else 0
-    plans, by_stash = plan_layer(mgr, world, group, device)
+    per_wave = hessian_tiles_per_wave(device) if world > 1 else None
+    plans, by_stash, ranges = plan_layer(mgr, world, group, device, per_wave)
 
     t0 = time.perf_counter()
 
@@ -223,20 +237,18 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
         nonlocal t0
         t0 = result._tick(stage, t0, device)
 
-    # phase 0 (several ranks): every rank forms an equal share of the output tiles of
-    # every linear Hessian from its own copy of the stashed rows; the shares are
-    # disjoint blocks, so their sum over ranks is the single-device H bit for bit
-    # (each element has one non-zero contribution)
+    # linear Hessians: a stash whose tiles fill more than one wave is formed in parts
+    # (disjoint output-tile ranges, on different ranks); the parts are summed over
+    # ranks, which is the single-device H bit for bit (one non-zero term per element)
     lin_H: dict[str, torch.Tensor] = {}
-    if world > 1 and by_stash:
-        for key in sorted(by_stash):
-            st = mgr.stashes[key]
-            T = hessian_tile_count(st.in_features)
-            lin_H[key] = st.hessian(device, tiles=(rank * T // world, (rank + 1) * T // world))
-        timer("linear_hessians")
-        for key in sorted(by_stash):
-            dist.all_reduce(lin_H[key], op=dist.ReduceOp.SUM, group=group)
-        timer("hessian_merge")
+    for key, b, e in plans[rank]["hessian_parts"]:
+        st = mgr.stashes[key]
+        if len(ranges[key]) == 1:
+            lin_H[key] = st.hessian(device)
+        else:
+            part = st.hessian(device, tiles=(b, e))
+            lin_H[key] = part if key not in lin_H else lin_H[key].add_(part)
+    timer("linear_hessians")
 
     # phase 1: this rank's own work, no collectives (a rank with a large item does
     # not hold the others up at an all-gather)
@@ -264,6 +276,20 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
             rel = torch.empty(0, dtype=torch.float32, device=device)
         fused_out.append((bits, q, s, b, W_dq, rel))
 
+    # every rank that solves a linear needs its stash's whole H: one exchange per stash
+    # (a broadcast from the rank holding it, or a sum of the parts)
+    if world > 1:
+        for key in sorted(by_stash):
+            holders = [r for r in range(world) if any(k == key for k, _, _ in plans[r]["hessian_parts"])]
+            C = mgr.stashes[key].in_features
+            if key not in lin_H:
+                lin_H[key] = torch.zeros(C, C, dtype=torch.float32, device=device)
+            if len(holders) == 1:
+                dist.broadcast(lin_H[key], src=dist.get_global_rank(group, holders[0]), group=group)
+            else:
+                dist.all_reduce(lin_H[key], op=dist.ReduceOp.SUM, group=group)
+        timer("hessian_merge")
+
     # plain linears: one Hessian per stash, shared by the siblings that read the same input
     mine = set(plans[rank]["linears"])
     local = {}
@@ -271,7 +297,7 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
         todo = [t for t in by_stash[key] if t.name in mine]
         if not todo:
             continue
-        H0 = lin_H[key] if key in lin_H else mgr.stashes[key].hessian(device)
+        H0 = lin_H[key]
         for t in todo:
             name = f"{layer_prefix}.{t.name}.weight"
             bits = args.bits_for(name)

@@ -166,6 +166,7 @@ def install_fakes(pipeline_mod, capture_mod):
     pipeline_mod.pack_nibbles = _fake_pack
     pipeline_mod.unpack_nibbles = _fake_unpack
     pipeline_mod.hessian_tile_count = _fake_tile_count
+    pipeline_mod.hessian_tiles_per_wave = _fake_tiles_per_wave
     capture_mod.CaptureManager.expert_hessians = _fake_expert_hessians
     capture_mod.Stash.hessian = _fake_stash_hessian
 
@@ -188,6 +189,10 @@ def _fake_stash_hessian(self, device, chunk_rows=65536, tiles=None):
 
 def _fake_tile_count(c):
     return c
+
+
+def _fake_tiles_per_wave(device=None):
+    return 20  # a 32-feature stash (32 "tiles") is formed in two parts
 
 
 def _run_layer(rank, world, port, out_dir):
@@ -237,8 +242,11 @@ def test_sharded_layer_solve_matches_single_process(tmp_path):
             assert torch.equal(v, got["weights"][k]), k
 
 
-def test_plan_layer_covers_every_item_once_and_balances():
+def test_plan_layer_covers_every_item_once_and_balances(monkeypatch):
+    from mlx_gptq_b200 import pipeline
     from mlx_gptq_b200.pipeline import plan_layer
+
+    monkeypatch.setattr(pipeline, "hessian_tile_count", _fake_tile_count)
 
     torch.manual_seed(0)
     layer = ToyMoELayer(E=6, k=2)
@@ -247,8 +255,13 @@ def test_plan_layer_covers_every_item_once_and_balances():
         mgr.begin_batch()
         layer(torch.randn(64, 32))
     for world in (1, 2, 3, 8):
-        plans, by_stash = plan_layer(mgr, world)
+        plans, by_stash, ranges = plan_layer(mgr, world, per_wave=10)
         assert len(plans) == world
+        for key, rs in ranges.items():  # tile ranges tile the stash's H, each part on one rank
+            assert [r for p in plans for r in p["hessian_parts"] if r[0] == key] is not None
+            got = sorted((b, e) for p in plans for k, b, e in p["hessian_parts"] if k == key)
+            assert got == rs and rs[0][0] == 0 and all(a[1] == b[0] for a, b in zip(rs, rs[1:]))
+            assert len(rs) == (1 if world == 1 else min(world, 4))
         for ti, task in enumerate(mgr.fused_tasks):
             got = sorted(e for p in plans for e in p["experts"][ti])
             assert got == list(range(task.num_experts))

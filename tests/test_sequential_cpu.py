@@ -150,6 +150,7 @@ def _fake_solver(monkeypatch):
     monkeypatch.setattr(pipeline, "pack_nibbles", fakes._fake_pack)
     monkeypatch.setattr(pipeline, "unpack_nibbles", fakes._fake_unpack)
     monkeypatch.setattr(pipeline, "hessian_tile_count", fakes._fake_tile_count)
+    monkeypatch.setattr(pipeline, "hessian_tiles_per_wave", fakes._fake_tiles_per_wave)
     monkeypatch.setattr(capture.CaptureManager, "expert_hessians", fakes._fake_expert_hessians)
     monkeypatch.setattr(capture.Stash, "hessian", fakes._fake_stash_hessian)
 
