@@ -46,6 +46,7 @@ class LayerSolveArgs:
     clip: str = "mse"
     storage_dtype: torch.dtype = torch.bfloat16
     overrides: list = field(default_factory=list)  # [(compiled regex, bits)]
+    vram_gb: float | None = None  # expert-solve budget per batched solve (None: one batch)
 
     def bits_for(self, artifact_name: str) -> int:
         for pattern, bits in self.overrides:
@@ -102,6 +103,12 @@ def lpt_partition(costs, parts: int):
         bins[p].append(i)
         heapq.heappush(heap, (load + costs[i], p))
     return [sorted(b) for b in bins]
+
+
+def expert_chunk_size(C: int, R: int, vram_gb: float) -> int:
+    """Experts per batched solve within a budget (sequential.py:314-318)."""
+    per = (3 * C * C + 3 * R * C) * 4  # H, factor temporaries, W copies (fp32)
+    return max(1, int(vram_gb * (1 << 30) // per))
 
 
 def _solve_batch(W, H, bits, args: LayerSolveArgs):
@@ -260,13 +267,23 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
         bits = args.bits_for(artifact_names_for_fused(layer_prefix, task, 0)[0])
         mine = plans[rank]["experts"][ti]
         if mine:
-            H = mgr.expert_hessians(task, device, mine, timer=timer)
-            timer("expert_hessians")
-            W = p.detach()[mine].to(device)
-            q, s, b, W_dq, rel = _solve_batch(W, H, bits, args)
-            W_dq = W_dq.to(p.dtype)
-            del H, W
-            timer("expert_solves")
+            chunk = len(mine) if args.vram_gb is None else expert_chunk_size(C, R, args.vram_gb)
+            outs = []
+            for i in range(0, len(mine), chunk):
+                sub = mine[i:i + chunk]
+                H = mgr.expert_hessians(task, device, sub, timer=timer)
+                timer("expert_hessians")
+                W = p.detach()[sub].to(device)
+                qi, si, bi, Wi, ri = _solve_batch(W, H, bits, args)
+                outs.append((qi, si, bi, Wi.to(p.dtype), ri))
+                del H, W
+                timer("expert_solves")
+            if len(outs) == 1:
+                q, s, b, W_dq, rel = outs[0]
+            else:
+                q, s, W_dq, rel = (torch.cat([o[j] for o in outs]) for j in (0, 1, 3, 4))
+                b = None if outs[0][2] is None else torch.cat([o[2] for o in outs])
+            del outs
         else:  # this rank owns no expert of the task: empty shares
             q = torch.empty(0, R, C, dtype=torch.uint8, device=device)
             s = torch.empty(0, R, C // args.group_size, dtype=torch.uint8 if args.mode != "affine" else

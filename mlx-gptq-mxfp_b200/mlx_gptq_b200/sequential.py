@@ -379,9 +379,13 @@ class Pipeline:
 
     def solve_args(self) -> LayerSolveArgs:
         a = self.args
+        vram = getattr(a, "vram_gb", None)
+        if isinstance(vram, dict):
+            vram = vram.get(str(self.dev0), next(iter(vram.values())) if vram else None)
         return LayerSolveArgs(bits=a.bits, group_size=a.group_size, mode=a.mode,
                               mxfp_algorithm=getattr(a, "mxfp_algorithm", "auto"), damp=a.damp, clip=a.clip,
-                              storage_dtype=self.storage_dtype, overrides=list(getattr(a, "overrides", []) or []))
+                              storage_dtype=self.storage_dtype, overrides=list(getattr(a, "overrides", []) or []),
+                              vram_gb=vram)
 
     @torch.no_grad()
     def solve_layer(self, layer_idx: int, mgr: CaptureManager):

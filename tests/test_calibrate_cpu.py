@@ -1,0 +1,169 @@
+"""Stage A command line (mlx_gptq_b200.calibrate): flag rules, budgets, data windows,
+checkpoint prefixes, and a CPU run over a tiny on-disk Qwen3-MoE checkpoint with the
+GPU pieces replaced by deterministic stand-ins (reference tests: test_vram_budgets.py,
+test_prefix_mapping.py; calibrate.py:97-293)."""
+
+import json
+import os
+import types
+
+import numpy as np
+import pytest
+import torch
+
+from mlx_gptq_b200 import calibrate, sequential
+
+TINY = dict(model_type="qwen3_moe", vocab_size=512, hidden_size=64, intermediate_size=128, moe_intermediate_size=32,
+            num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2, head_dim=16, num_experts=8,
+            num_experts_per_tok=2, decoder_sparse_step=1, norm_topk_prob=True, max_position_embeddings=256)
+
+
+def test_single_budget_is_broadcast_to_all_devices():
+    assert calibrate.parse_vram_budgets("12", ["cuda:0", "cuda:1"]) == {"cuda:0": 12.0, "cuda:1": 12.0}
+
+
+def test_per_device_budgets_preserve_heterogeneous_capacity():
+    assert calibrate.parse_vram_budgets("4.2,18.6,83.4", ["cuda:0", "cuda:1", "cuda:2"]) == {
+        "cuda:0": 4.2, "cuda:1": 18.6, "cuda:2": 83.4}
+
+
+def test_per_device_budget_count_must_match():
+    with pytest.raises(ValueError, match="one comma-separated value per device"):
+        calibrate.parse_vram_budgets("4,8", ["cuda:0", "cuda:1", "cuda:2"])
+    with pytest.raises(ValueError, match="positive"):
+        calibrate.parse_vram_budgets("0", ["cuda:0"])
+
+
+def _resolve(argv):
+    return calibrate.resolve_args(calibrate.build_parser(), argv)
+
+
+def test_mode_rules():
+    base = ["--model", "m", "--output", "o", "--calibration-tokens", "t.npy", "--devices", "cpu"]
+    a = _resolve(base + ["--mode", "mxfp4"])
+    assert (a.group_size, a.bits, a.mxfp_algorithm) == (32, 4, "safe-scale-search")
+    a = _resolve(base + ["--mode", "mxfp8"])
+    assert (a.group_size, a.bits, a.mxfp_algorithm) == (32, 8, "groupwise")
+    a = _resolve(base + ["--mode", "affine", "--override", ".*down_proj.*=8"])
+    assert (a.group_size, a.bits, a.mxfp_algorithm) == (64, 4, "none")
+    assert a.overrides[0][0].search("mlp.down_proj.weight") and a.overrides[0][1] == 8
+    assert a.vram_gb == {"cpu": 16.0}
+    for bad in (["--mode", "mxfp4", "--bits", "8"], ["--mode", "mxfp8", "--group-size", "64"],
+                ["--mode", "mxfp4", "--override", "x=8"], ["--lazy-ple"]):
+        with pytest.raises(SystemExit):
+            _resolve(base + bad)
+    with pytest.raises(SystemExit):
+        _resolve(["--model", "m", "--output", "o"])  # neither --dataset nor --calibration-tokens
+
+
+class _Tok:
+    """Whitespace tokenizer: word i of a fixed vocabulary -> id i."""
+    eos_token_id = 0
+
+    def __call__(self, text, add_special_tokens=False):
+        return types.SimpleNamespace(input_ids=[1 + (hash(w) % 400) for w in text.split()])
+
+    def __len__(self):
+        return 512
+
+
+def test_load_calibration_windows(tmp_path):
+    txt = tmp_path / "a.txt"
+    txt.write_text(" ".join(f"w{i}" for i in range(3000)))
+    jl = tmp_path / "b.jsonl"
+    jl.write_text("\n".join(json.dumps({"body": " ".join(f"v{i}" for i in range(500))}) for _ in range(3)))
+    s = calibrate.load_calibration(_Tok(), f"{txt},{jl}:body", nsamples=8, seqlen=128, seed=3)
+    assert s.shape == (8, 128) and s.dtype == torch.int64
+    s2 = calibrate.load_calibration(_Tok(), f"{txt},{jl}:body", nsamples=8, seqlen=128, seed=3)
+    assert torch.equal(s, s2)
+    with pytest.raises(ValueError, match="offline"):
+        calibrate.load_calibration(_Tok(), "hf:wikitext", 1, 8)
+    with pytest.raises(ValueError, match="tokens < seqlen"):
+        calibrate.load_calibration(_Tok(), str(txt), 1, 5000)
+
+
+def test_multimodal_checkpoint_prefixes_are_independent():
+    class Backbone(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.layers = torch.nn.ModuleList([torch.nn.Linear(4, 4, bias=False)])
+
+    class Runtime(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.model = Backbone()
+
+    args = types.SimpleNamespace(devices=["cpu"], dtype="bfloat16", layers_attr="model.layers",
+                                 checkpoint_model_prefix="model.language_model",
+                                 artifact_layers_prefix="language_model.model.layers")
+    p = sequential.Pipeline(Runtime(), shards=None, args=args)
+    assert p._checkpoint_name("model.embed_tokens") == "model.language_model.embed_tokens"
+    assert p.checkpoint_layers_prefix_fmt.format(7) == "model.language_model.layers.7"
+    assert p.artifact_layers_prefix_fmt.format(7) == "language_model.model.layers.7"
+
+
+def write_tiny_checkpoint(path, cfg=TINY, seed=0):
+    """config.json + model.safetensors with per-expert tensors, as Hugging Face ships them."""
+    from safetensors.torch import save_file
+
+    os.makedirs(path, exist_ok=True)
+    with open(os.path.join(path, "config.json"), "w") as f:
+        json.dump(cfg, f)
+    model = sequential.build_model(dict(cfg))
+    src = sequential.SyntheticWeights(model, "cpu", seed=seed)
+    tensors = {}
+    for name in src.shapes:
+        t = src.get(name).to(torch.bfloat16)
+        if name.endswith(("experts.gate_up_proj", "experts.down_proj")):
+            base, kind = name.rsplit(".", 1)
+            for e in range(t.shape[0]):
+                if kind == "gate_up_proj":
+                    half = t.shape[1] // 2
+                    tensors[f"{base}.{e}.gate_proj.weight"] = t[e, :half].contiguous()
+                    tensors[f"{base}.{e}.up_proj.weight"] = t[e, half:].contiguous()
+                else:
+                    tensors[f"{base}.{e}.down_proj.weight"] = t[e].contiguous()
+        else:
+            tensors[name] = t.contiguous()
+    save_file(tensors, os.path.join(path, "model.safetensors"))
+    return path
+
+
+def test_cli_runs_and_resumes_on_cpu(tmp_path, monkeypatch):
+    import test_pipeline_cpu as fakes
+
+    from mlx_gptq_b200 import artifacts, grid, pipeline
+
+    from mlx_gptq_b200 import capture
+
+    for mod, name, fn in ((pipeline, "_solve_batch", fakes._fake_solve),
+                          (pipeline, "dequantize_artifact", fakes._fake_dequant),
+                          (pipeline, "pack_nibbles", fakes._fake_pack), (pipeline, "unpack_nibbles", fakes._fake_unpack),
+                          (pipeline, "hessian_tile_count", fakes._fake_tile_count),
+                          (artifacts, "pack_nibbles", fakes._fake_pack), (artifacts, "unpack_nibbles", fakes._fake_unpack),
+                          (grid, "dequantize_artifact", fakes._fake_dequant),
+                          (capture.CaptureManager, "expert_hessians", fakes._fake_expert_hessians),
+                          (capture.Stash, "hessian", fakes._fake_stash_hessian)):
+        monkeypatch.setattr(mod, name, fn)
+    model_dir = write_tiny_checkpoint(str(tmp_path / "model"))
+    toks = tmp_path / "t.npy"
+    np.save(toks, np.random.default_rng(1).integers(0, 512, (4, 32)).astype(np.int64))
+    out = str(tmp_path / "out")
+    argv = ["--model", model_dir, "--output", out, "--calibration-tokens", str(toks), "--mode", "mxfp4",
+            "--devices", "cpu", "--batch-size", "2"]
+    calibrate.main(argv)
+    man = json.load(open(os.path.join(out, "manifest.json")))
+    assert man["layers_done"] == [0, 1] and man["mode"] == "mxfp4" and man["algorithm"] == "safe-scale-search"
+    assert man["nsamples"] == 4 and man["seqlen"] == 32 and len(man["calibration_tokens_sha256"]) == 64
+    names = set(man["tensors"])
+    assert "model.layers.1.self_attn.o_proj.weight" in names
+    assert "model.layers.0.mlp.experts.7.down_proj.weight" in names and len(names) == 2 * (4 + 3 * 8)
+    assert os.path.exists(os.path.join(out, "calib_tokens.npy"))
+    before = open(os.path.join(out, "manifest.json")).read()
+    calibrate.main(argv)  # every layer resumes from its artifacts
+    assert open(os.path.join(out, "manifest.json")).read() == before
+    bad = tmp_path / "bad.npy"
+    np.save(bad, np.full((2, 8), 999, np.int64))
+    with pytest.raises(ValueError, match="exceed vocabulary"):
+        calibrate.main(["--model", model_dir, "--output", str(tmp_path / "o2"), "--calibration-tokens", str(bad),
+                        "--devices", "cpu"])
