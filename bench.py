@@ -242,7 +242,9 @@ def cpu_baseline(wl, n_tokens=4096, n_groups=4):
 # clocks during the timed region
 # ---------------------------------------------------------------------------
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi samples every 50 ms from before the warm-up on; the summary keeps the
+    samples whose timestamps fall inside the timed region (begin()/end())."""
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -250,6 +252,7 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.path = None
+        self.t0 = self.t1 = None
 
     def start(self):
         try:
@@ -260,6 +263,25 @@ class ClockSampler:
                  "-lms", "50"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
+            return
+        deadline = time.time() + 5.0
+        while time.time() < deadline and os.path.getsize(self.path) == 0:  # first sample written
+            time.sleep(0.02)
+
+    def begin(self):
+        self.t0 = time.time()
+
+    def end(self):
+        self.t1 = time.time()
+
+    @staticmethod
+    def _when(stamp: str):
+        import datetime
+
+        try:
+            return datetime.datetime.strptime(stamp.strip(), "%Y/%m/%d %H:%M:%S.%f").timestamp()
+        except ValueError:
+            return None
 
     def stop(self):
         if self.proc is None:
@@ -272,11 +294,18 @@ class ClockSampler:
         rows = []
         for line in open(self.path):
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                rows.append(parts)
+            if len(parts) >= 10:
+                rows.append((self._when(parts[0]), parts[1:]))
         os.unlink(self.path)
         if not rows:
             return None
+        inside = rows
+        if self.t0 is not None and self.t1 is not None:
+            inside = [r for r in rows if r[0] is not None and self.t0 - 0.06 <= r[0] <= self.t1 + 0.06]
+            if not inside:  # a region shorter than the sampling period: the nearest sample after it began
+                after = [r for r in rows if r[0] is not None and r[0] >= self.t0]
+                inside = after[:1] or rows[-1:]
+        rows = [r[1] for r in inside]
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
@@ -395,10 +424,10 @@ def profile_case(case, device):
             b.synchronize()
             print(f"affine C1 [4096x4096] g64: factor {a.elapsed_time(m):.2f} ms, full solve_gptq "
                   f"{m.elapsed_time(b):.2f} ms ({W.numel() / m.elapsed_time(b) / 1e6:.2f} G elems/s)")
-    elif case == "moe":
+    elif case in ("moe", "moe-small"):
         from mlx_gptq_b200 import hessian_grouped
 
-        T, E, K, I = 524288, 128, 2048, 768
+        T, E, K, I = (524288 if case == "moe" else 32768), 128, 2048, 768
         X = (torch.randn(T, K, generator=torch.Generator(device=device).manual_seed(1), device=device)
              .to(torch.bfloat16))
         token_idx, offsets = moe_routing(T, E, 8, 2, device)
@@ -546,7 +575,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--profile-case", choices=["hessian", "hessian-full", "solve", "affine", "moe"], default=None,
+    ap.add_argument("--profile-case", choices=["hessian", "hessian-full", "solve", "affine", "moe", "moe-small"],
+                    default=None,
                     help="run a small case of one kernel for an ncu capture and exit")
     ap.add_argument("--config", choices=["c2", "c5"], default="c2",
                     help="c2: the headline MLP sweep (default); c5: the synthetic Qwen3-MoE layer stack")
@@ -585,6 +615,8 @@ def main():
 
     wl = make_workload(rank % 3, device)
     step = Step(wl, device)
+    clocks = ClockSampler(local)
+    clocks.start()  # sampling from before the warm-up; the summary keeps the timed region
     for _ in range(args.warmup):
         step.run()
     torch.cuda.synchronize()
@@ -595,8 +627,7 @@ def main():
     if pg:
         pg.barrier()
     torch.cuda.synchronize()
-    clocks = ClockSampler(local)
-    clocks.start()
+    clocks.begin()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     hess_ms, solve_ms, hess_big_ms = [], [], []
     t0.record()
@@ -606,6 +637,7 @@ def main():
         hess_ms.append(ev)
     t1.record()
     torch.cuda.synchronize()
+    clocks.end()
     if pg:
         pg.barrier()
     clk = clocks.stop()
