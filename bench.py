@@ -500,7 +500,7 @@ def run_c5(args, ws, rank, local):
                                   batch_size=args.c5_batch, experts_forward=args.c5_experts_forward)
     g = torch.Generator().manual_seed(1)
     samples = torch.randint(0, cfg["vocab_size"], (args.c5_samples, args.c5_seqlen), generator=g)
-    pipe = sequential.Pipeline(model, src, sargs, group=group)
+    pipe = sequential.Pipeline(model, src, sargs, group=group, dp=args.c5_dp)
     t0 = time.time()
     pipe.run(samples, writer=None, layers=args.layers)
     torch.cuda.synchronize()
@@ -540,7 +540,8 @@ def run_c5(args, ws, rank, local):
     hess_flop = 2.0 * tokens * (H * H + qd * qd) + 2.0 * tokens * k * (H * H + I * I)
     line = {"metric": "C5 layer stack: GPTQ-solved weight elems/s (solve stage: Hessians -> codes, all-gather)",
             "value": elems_timed / solve_s, "unit": "elems/s", "n_gpus": ws, "layers": len(per_layer),
-            "higher_is_better": True, "scaling": "strong (one layer's experts split over ranks)",
+            "higher_is_better": True, "scaling": "strong (one layer's experts split over ranks)" + (
+                ", windows split over ranks (dp)" if args.c5_dp else ", forward on every rank"),
             "dtype": "bf16 x bf16 -> f32 (Hessian), f32 (solve)", "data": "synthetic (random init seed 0, "
             "uniform tokens seed 1)",
             "config": {"workload": "C5 Qwen3-30B-A3B-shaped stack, MXFP4 safe-scale-search",
@@ -549,6 +550,8 @@ def run_c5(args, ws, rank, local):
                                            "eager": "eager F.linear loop"}[args.c5_experts_forward],
                        "artifacts": "kept on the device, not written to disk"},
             "solved_elems_per_layer": elems // len(per_layer),
+            "stack_elems_per_s": elems_timed / sum(r[3] for r in (per_layer[1:] or per_layer)),
+            "layer_ms_mean": statistics.mean(r[3] for r in (per_layer[1:] or per_layer)) * 1e3,
             "hessian_tflop_per_layer": hess_flop / 1e12,
             "solve_ms_per_layer": solve_s / n_solve * 1e3,
             "layer_s": [round(r[3], 3) for r in per_layer],
@@ -585,6 +588,8 @@ def main():
     ap.add_argument("--c5-seqlen", type=int, default=2048)
     ap.add_argument("--c5-batch", type=int, default=16, help="c5: sequences per forward")
     ap.add_argument("--c5-experts-forward", choices=["grouped", "eager"], default="grouped")
+    ap.add_argument("--c5-dp", action="store_true",
+                    help="c5: each rank forwards 1/N of the windows; Hessians summed over ranks")
     args = ap.parse_args()
     ws, rank, local = dist_env()
     if args.config == "c5":

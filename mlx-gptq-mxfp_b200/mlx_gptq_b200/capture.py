@@ -284,6 +284,7 @@ class CaptureManager:
         self._segment_modules: set[str] = set()
         self._slot_experts: dict[str, torch.Tensor] = {}
         self._mode_registry: dict[int, str] = {}
+        self.global_tokens: dict[str, int] | None = None  # summed over data-parallel ranks
         self._mode = None
         excl = re.compile(exclude_regex) if exclude_regex else None
         seen = set()
@@ -403,6 +404,23 @@ class CaptureManager:
     def begin_batch(self):
         self._batch_seen.clear()
 
+    def tokens(self, key: str) -> int:
+        """Rows captured for a stash: this process's, or the sum over data-parallel
+        ranks after sync_token_counts."""
+        if self.global_tokens is not None:
+            return self.global_tokens[key]
+        return self.stashes[key].tokens
+
+    def sync_token_counts(self, group, device):
+        """Sum every stash's row count over the ranks of `group` (each rank captured its
+        own calibration windows); the local counts stay in Stash.tokens."""
+        import torch.distributed as dist
+
+        keys = sorted(self.stashes)
+        t = torch.tensor([self.stashes[k].tokens for k in keys], dtype=torch.int64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
+        self.global_tokens = dict(zip(keys, t.tolist()))
+
     # ---- diagnostics ----
     def total_stash_bytes(self) -> int:
         seg = sum(st.nbytes() for st in self._segments.values())
@@ -412,7 +430,7 @@ class CaptureManager:
         """param -> (min, median, max, zero_count) of tokens per expert (capture.py:242-251)."""
         out = {}
         for t in self.fused_tasks:
-            counts = sorted(self.stashes[k].tokens for k in t.stash_keys)
+            counts = sorted(self.tokens(k) for k in t.stash_keys)
             out[f"{t.module_name}.{t.param_name}"] = (counts[0], counts[len(counts) // 2], counts[-1],
                                                       sum(1 for c in counts if c == 0))
         return out
@@ -432,7 +450,7 @@ class CaptureManager:
             input_task = next((tasks[n] for n in ("gate_up_proj", "gate_proj", "up_proj") if n in tasks), None)
             if input_task is None:
                 continue
-            missing = [e for e, key in enumerate(input_task.stash_keys) if self.stashes[key].tokens == 0]
+            missing = [e for e, key in enumerate(input_task.stash_keys) if self.tokens(key) == 0]
             for expert in missing:
                 for task in tasks.values():
                     if task.param_name == "down_proj":
@@ -462,7 +480,7 @@ class CaptureManager:
     def check_capture_happened(self):
         """capture.py:328-337: fused experts must have gone through F.linear."""
         for t in self.fused_tasks:
-            if all(self.stashes[k].tokens == 0 for k in t.stash_keys):
+            if all(self.tokens(k) == 0 for k in t.stash_keys):
                 raise RuntimeError(
                     f"No tokens captured for fused experts {t.module_name}.{t.param_name}. "
                     "The model is probably not using the eager experts implementation; "
@@ -517,19 +535,24 @@ class CaptureManager:
         inputs, or this share's activation blocks, plus any stashed rows)."""
         experts = list(range(task.num_experts)) if experts is None else list(experts)
         C = task.param.shape[-1]
-        seg = self._segment_rows(task, experts, device)
+        real = [e for e in experts if e is not None]  # None: a padding slot (H = 0)
+        seg = self._segment_rows(task, real, device)
         parts, idx_parts, counts, base = [], [], [], 0
-        seg_off = 0
+        seg_off, j = 0, 0
         if seg is not None:
             X0, idx0, seg_counts = seg
             parts.append(X0)
             base = X0.shape[0]
-        for i, e in enumerate(experts):
+        for e in experts:
             n = 0
-            if seg is not None and seg_counts[i]:
-                idx_parts.append(idx0[seg_off:seg_off + seg_counts[i]])
-                seg_off += seg_counts[i]
-                n += seg_counts[i]
+            if e is None:
+                counts.append(0)
+                continue
+            if seg is not None and seg_counts[j]:
+                idx_parts.append(idx0[seg_off:seg_off + seg_counts[j]])
+                seg_off += seg_counts[j]
+                n += seg_counts[j]
+            j += 1
             for c in self.stashes[task.stash_keys[e]].chunks:
                 parts.append(c.to(device))
                 idx_parts.append(torch.arange(base, base + c.shape[0], dtype=torch.int32, device=device))

@@ -173,7 +173,8 @@ def _wave_parts(tiles: int, per_wave: int, world: int) -> list[tuple[int, int]]:
     return [(i * tiles // parts, (i + 1) * tiles // parts) for i in range(parts)]
 
 
-def plan_layer(mgr: CaptureManager, world: int, group=None, device="cpu", per_wave: int | None = None):
+def plan_layer(mgr: CaptureManager, world: int, group=None, device="cpu", per_wave: int | None = None,
+               dp: bool = False):
     """One longest-processing-time partition of a layer's work over `world` ranks.
 
     Items: every expert of every fused task (its Hessian and solve), every part of
@@ -189,9 +190,10 @@ def plan_layer(mgr: CaptureManager, world: int, group=None, device="cpu", per_wa
     keys = sorted(by_stash)
     counts = []
     for task in mgr.fused_tasks:
-        counts.extend(mgr.stashes[k].tokens for k in task.stash_keys)
-    counts.extend(mgr.stashes[k].tokens for k in keys)
-    counts = _agreed_counts(counts, group, device)
+        counts.extend(mgr.tokens(k) for k in task.stash_keys)
+    counts.extend(mgr.tokens(k) for k in keys)
+    if not dp:
+        counts = _agreed_counts(counts, group, device)
     items, costs, i = [], [], 0
     for ti, task in enumerate(mgr.fused_tasks):
         E, R, C = task.param.shape
@@ -202,11 +204,12 @@ def plan_layer(mgr: CaptureManager, world: int, group=None, device="cpu", per_wa
     ranges = {}
     for k in keys:
         C = mgr.stashes[k].in_features
-        T = hessian_tile_count(C) if world > 1 else 1
-        ranges[k] = _wave_parts(T, per_wave or T, world)
-        for b, e in ranges[k]:
-            items.append(("hessian", k, (b, e)))
-            costs.append(float(counts[i]) * C * C / len(ranges[k]))
+        if not dp:
+            T = hessian_tile_count(C) if world > 1 else 1
+            ranges[k] = _wave_parts(T, per_wave or T, world)
+            for b, e in ranges[k]:
+                items.append(("hessian", k, (b, e)))
+                costs.append(float(counts[i]) * C * C / len(ranges[k]))
         for t in by_stash[k]:
             items.append(("linear", t.name, None))
             costs.append(SOLVE_COST_PER_ELEM * t.module.out_features * C)
@@ -227,16 +230,24 @@ def plan_layer(mgr: CaptureManager, world: int, group=None, device="cpu", per_wa
 
 @torch.no_grad()
 def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, device, group=None,
-                on_device: bool = False) -> SolveResult:
-    """Quantize every task of a captured layer; returns the artifacts (sequential.py:467-635)."""
+                on_device: bool = False, dp: bool = False) -> SolveResult:
+    """Quantize every task of a captured layer; returns the artifacts (sequential.py:467-635).
+
+    dp: the ranks of `group` captured different calibration windows (counts already
+    summed by CaptureManager.sync_token_counts); each rank forms partial Hessians over
+    its own rows, expert Hessians reach their owners by one reduce-scatter per fused
+    parameter and linear Hessians by one all-reduce per stash. The sums over ranks
+    change the fp32 summation order, so the result matches one process within the
+    Hessian tolerance rather than bit for bit."""
     import torch.distributed as dist
 
     device = torch.device(device)
     result = SolveResult(on_device)
     world = dist.get_world_size(group) if group is not None else 1
     rank = dist.get_rank(group) if group is not None else 0
-    per_wave = hessian_tiles_per_wave(device) if world > 1 else None
-    plans, by_stash, ranges = plan_layer(mgr, world, group, device, per_wave)
+    dp = dp and world > 1
+    per_wave = hessian_tiles_per_wave(device) if world > 1 and not dp else None
+    plans, by_stash, ranges = plan_layer(mgr, world, group, device, per_wave, dp)
 
     t0 = time.perf_counter()
 
@@ -248,6 +259,13 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
     # (disjoint output-tile ranges, on different ranks); the parts are summed over
     # ranks, which is the single-device H bit for bit (one non-zero term per element)
     lin_H: dict[str, torch.Tensor] = {}
+    if dp:  # partial over this rank's windows on every rank, summed
+        for key in sorted(by_stash):
+            lin_H[key] = mgr.stashes[key].hessian(device)
+        timer("linear_hessians")
+        for key in sorted(by_stash):
+            dist.all_reduce(lin_H[key], op=dist.ReduceOp.SUM, group=group)
+        timer("hessian_merge")
     for key, b, e in plans[rank]["hessian_parts"]:
         st = mgr.stashes[key]
         if len(ranges[key]) == 1:
@@ -266,13 +284,31 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
         E, R, C = p.shape
         bits = args.bits_for(artifact_names_for_fused(layer_prefix, task, 0)[0])
         mine = plans[rank]["experts"][ti]
+        H_dp = None
+        if dp:
+            # partial H of every expert over this rank's rows, laid out rank by rank
+            # (shares padded to the largest), then one reduce-scatter: each rank
+            # receives the summed H of its own experts
+            shares = [plans[r]["experts"][ti] for r in range(world)]
+            m = max(len(x) for x in shares)
+            if m:
+                padded = [e for x in shares for e in x + [None] * (m - len(x))]
+                H_all = mgr.expert_hessians(task, device, padded, timer=timer)
+                timer("expert_hessians")
+                H_dp = torch.empty(m, C, C, dtype=torch.float32, device=device)
+                dist.reduce_scatter_tensor(H_dp, H_all, op=dist.ReduceOp.SUM, group=group)
+                del H_all
+                timer("hessian_merge")
         if mine:
             chunk = len(mine) if args.vram_gb is None else expert_chunk_size(C, R, args.vram_gb)
             outs = []
             for i in range(0, len(mine), chunk):
                 sub = mine[i:i + chunk]
-                H = mgr.expert_hessians(task, device, sub, timer=timer)
-                timer("expert_hessians")
+                if H_dp is not None:
+                    H = H_dp[i:i + len(sub)]
+                else:
+                    H = mgr.expert_hessians(task, device, sub, timer=timer)
+                    timer("expert_hessians")
                 W = p.detach()[sub].to(device)
                 qi, si, bi, Wi, ri = _solve_batch(W, H, bits, args)
                 outs.append((qi, si, bi, Wi.to(p.dtype), ri))
@@ -295,7 +331,7 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
 
     # every rank that solves a linear needs its stash's whole H: one exchange per stash
     # (a broadcast from the rank holding it, or a sum of the parts)
-    if world > 1:
+    if world > 1 and not dp:
         for key in sorted(by_stash):
             holders = [r for r in range(world) if any(k == key for k, _, _ in plans[r]["hessian_parts"])]
             C = mgr.stashes[key].in_features
@@ -366,7 +402,7 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
             names = artifact_names_for_fused(layer_prefix, task, e)
             info = {"bits": bits, "group_size": args.group_size, "mode": args.mode, "kind": "expert",
                     "out_features": R // parts, "in_features": C,
-                    "tokens": mgr.stashes[task.stash_keys[e]].tokens, "rel_err": round(rel_h[i], 6),
+                    "tokens": mgr.tokens(task.stash_keys[e]), "rel_err": round(rel_h[i], 6),
                     "fallback": mgr.fallback_experts.get(task.stash_keys[e])}
             for h, nm in enumerate(names):
                 j = i * parts + h
@@ -414,5 +450,5 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
         result.add(f"{layer_prefix}.{t.name}.weight", q, s, b, {
             "bits": bits, "group_size": args.group_size, "mode": args.mode, "kind": "linear",
             "out_features": W_dq.shape[0], "in_features": W_dq.shape[1],
-            "tokens": mgr.stashes[t.stash_key].tokens, "rel_err": round(rel, 6)})
+            "tokens": mgr.tokens(t.stash_key), "rel_err": round(rel, 6)})
     return result

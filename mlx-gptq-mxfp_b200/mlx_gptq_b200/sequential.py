@@ -279,14 +279,18 @@ class Pipeline:
     mode, mxfp_algorithm, damp, clip, overrides, batch_size (and optionally
     vram_gb, experts_forward: "grouped" (default; the sort-based expert forward
     of experts.py, bit-identical to the eager loop) or "eager"). `group` is a
-    torch.distributed process group whose ranks share the
-    solves (None: this process alone)."""
+    torch.distributed process group whose ranks share the solves (None: this
+    process alone). Every rank runs every calibration window through each layer
+    unless dp=True: then rank r forwards only its contiguous share of the windows,
+    Hessians are summed over ranks, and the forward scales with the ranks too (the
+    result matches one process within the Hessian tolerance, not bit for bit)."""
 
-    def __init__(self, model, shards, args, group=None):
+    def __init__(self, model, shards, args, group=None, dp: bool = False):
         self.model = model
         self.shards = shards
         self.args = args
         self.group = group
+        self.dp = bool(dp) and group is not None
         self.dev0 = torch.device(args.devices[0])
         self.dtype = torch.bfloat16 if args.dtype == "bfloat16" else torch.float16
         self.storage_dtype = self.dtype
@@ -390,7 +394,7 @@ class Pipeline:
     @torch.no_grad()
     def solve_layer(self, layer_idx: int, mgr: CaptureManager):
         prefix = self.artifact_layers_prefix_fmt.format(layer_idx)
-        return solve_layer(prefix, mgr, self.solve_args(), self.dev0, group=self.group, on_device=True)
+        return solve_layer(prefix, mgr, self.solve_args(), self.dev0, group=self.group, on_device=True, dp=self.dp)
 
     @torch.no_grad()
     def apply_precomputed(self, layer, layer_idx: int, reader) -> None:
@@ -428,8 +432,17 @@ class Pipeline:
     # ---- orchestration ----
     def run(self, samples: torch.Tensor, writer=None, reader_for_resume=None, layers=None):
         """Calibrate every decoder layer (or the first `layers`) in order
-        (sequential.py:683-770). Only rank 0 writes artifacts."""
+        (sequential.py:683-770). Only rank 0 writes artifacts. Returns this rank's
+        batches (all of them, or its share of the windows with dp)."""
         t_start = time.time()
+        if self.dp:
+            import torch.distributed as dist
+
+            world = dist.get_world_size(self.group)
+            if samples.shape[0] < world:
+                raise ValueError(f"dp needs at least one calibration window per rank ({samples.shape[0]} < {world})")
+            per = -(-samples.shape[0] // world)
+            samples = samples[self.rank * per:(self.rank + 1) * per]
         batches = self.catch_layer0_inputs(samples, self.args.batch_size)
         log.info("caught %d forward batches for layer 0", len(batches))
         n_layers = len(self.layers) if layers is None else min(int(layers), len(self.layers))
@@ -452,12 +465,16 @@ class Pipeline:
             n_exp = sum(t.num_experts for t in mgr.fused_tasks)
             with mgr:
                 self.forward_layer(layer, batches, li, capture_mgr=mgr)
+            if self.dp:
+                mgr.sync_token_counts(self.group, self.dev0)
             if mgr.fused_tasks:
                 mgr.check_capture_happened()
                 for pname, (mn, med, mx, zeros) in mgr.expert_token_stats().items():
                     log.info("layer %d %s tokens/expert min=%d med=%d max=%d zero=%d", li, pname, mn, med, mx, zeros)
                 for module_name, experts in mgr.backfill_unrouted_experts().items():
                     log.warning("layer %d %s: activation-backfilled unrouted experts %s", li, module_name, experts)
+                if self.dp:  # backfilled rows were added on every rank
+                    mgr.sync_token_counts(self.group, self.dev0)
             self._sync()
             t_cap = time.time()
 

@@ -306,3 +306,90 @@ def test_segment_capture_matches_linear_interception():
             assert m_e.stashes[te.stash_keys[e]].tokens == m_g.stashes[tg.stash_keys[e]].tokens
             assert torch.equal(m_e.expert_rows(te, e, "cpu"), m_g.expert_rows(tg, e, "cpu")), (te.param_name, e)
     assert m_e.expert_token_stats() == m_g.expert_token_stats()
+
+
+def _dp_expert_hessians(self, task, device, experts=None, timer=None):
+    """Additive stand-in: H = rows^T rows of the captured rows (float64 -> float32)."""
+    experts = list(range(task.num_experts)) if experts is None else list(experts)
+    C = task.param.shape[-1]
+    out = []
+    for e in experts:
+        if e is None:
+            out.append(torch.zeros(C, C))
+            continue
+        r = self.expert_rows(task, e, "cpu").double()
+        out.append((r.T @ r).float())
+    return torch.stack(out)
+
+
+def _dp_stash_hessian(self, device, chunk_rows=65536, tiles=None):
+    r = self.rows("cpu").double()
+    return (r.T @ r).float()
+
+
+def _dp_fake_solve(W, H, bits, args):
+    """Codes from W alone; the Hessian reaches the result through rel_err = trace(H),
+    which the test compares within the fp32 summation tolerance."""
+    B, R, C = W.shape
+    q = (W.abs() * 7).round().clamp(0, 15).to(torch.uint8)
+    s = torch.full((B, R, C // args.group_size), 3, dtype=torch.uint8)
+    import test_pipeline_cpu as fakes
+
+    W_dq = fakes._fake_dequant(q, s, None, args.mode, args.group_size)
+    return q, s, None, W_dq, H.diagonal(dim1=-2, dim2=-1).sum(-1)
+
+
+def _run_dp(rank, world, port, out_dir):
+    import sys
+
+    import torch.distributed as dist
+
+    sys.path.insert(0, os.path.dirname(__file__))
+    from test_pipeline_cpu import install_fakes
+
+    from mlx_gptq_b200 import capture, pipeline
+
+    install_fakes(pipeline, capture)
+    pipeline._solve_batch = _dp_fake_solve
+    capture.CaptureManager.expert_hessians = _dp_expert_hessians
+    capture.Stash.hessian = _dp_stash_hessian
+    group = None
+    if world > 1:
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+        group = dist.group.WORLD
+    model = sequential.build_model(TINY_QWEN3_MOE)
+    pipe = Pipeline(model, SyntheticWeights(model, "cpu", seed=0), _args(), group=group, dp=world > 1)
+    samples = torch.randint(0, 512, (8, 32), generator=torch.Generator().manual_seed(1))
+    w = _Writer()
+    out = pipe.run(samples, w)
+    torch.save({"layers": w.layers, "hidden": [h for h, _ in out]}, os.path.join(out_dir, f"dp{world}_{rank}.pt"))
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def test_dp_windows_stack_matches_single_process(tmp_path):
+    """Each rank forwards half the windows; summed Hessians and token counts give the
+    single-process artifacts and, across the two ranks, the same hidden states."""
+    import socket
+
+    import torch.multiprocessing as mp
+
+    _run_dp(0, 1, 0, str(tmp_path))
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    mp.start_processes(_run_dp, args=(2, port, str(tmp_path)), nprocs=2, start_method="spawn")
+    ref = torch.load(tmp_path / "dp1_0.pt")
+    r0, r1 = torch.load(tmp_path / "dp2_0.pt"), torch.load(tmp_path / "dp2_1.pt")
+    assert r1["layers"] == {}
+    for li, (tensors, meta) in ref["layers"].items():
+        t2, m2 = r0["layers"][li]
+        assert {k: v["tokens"] for k, v in m2.items()} == {k: v["tokens"] for k, v in meta.items()}
+        for k, (q, s, b) in tensors.items():
+            assert torch.equal(q, t2[k][0]) and torch.equal(s, t2[k][1]), k
+            # trace of the summed Hessian == trace of the single-process one (fp32 order)
+            assert abs(m2[k]["rel_err"] - meta[k]["rel_err"]) <= 1e-5 * abs(meta[k]["rel_err"]) + 1e-5, k
+    hidden = r0["hidden"] + r1["hidden"]
+    assert len(hidden) == len(ref["hidden"])
+    for a, b in zip(hidden, ref["hidden"]):
+        assert torch.equal(a, b)
