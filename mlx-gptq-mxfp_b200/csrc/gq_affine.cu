@@ -25,18 +25,43 @@ namespace aff {
 constexpr int NB = 64;  // factorization block
 
 // ---------------------------------------------------------------------------
-// 64x64 float32 tile GEMM building block (256 threads, 4x4 outputs each)
-// acc[r][c] += sum_t A(r, t) * B(t, c) over K, with
+// 64x64 float32 tile GEMM building block on the tensor cores (256 threads)
+// acc += sum_t A(r, t) * B(t, c) over K, with
 //   A(r, t) = TRANS_A ? A[t * lda + r] : A[r * lda + t]
 //   B(t, c) = TRANS_B ? B[c * ldb + t] : B[t * ldb + c]
-// Rows >= m_lim / columns >= n_lim read as zero.
+// Rows >= m_lim / columns >= n_lim read as zero. 16-deep chunks of A and B are
+// staged k-major in shared memory (stride 72: the fragment loads below are
+// bank-conflict free); warp w computes rows 16*(w&3).. and columns 32*(w>>2).. as
+// four m16n8k8 fragments, each product in 3xTF32 (x = hi + lo with hi = tf32(x);
+// hi*hi + hi*lo + lo*hi), which keeps float32 accuracy.
 // ---------------------------------------------------------------------------
+constexpr int TS = 72;  // staging row stride (floats)
+
+__device__ __forceinline__ uint32_t tf32_of(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+__device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
+  hi = tf32_of(x);
+  lo = tf32_of(x - __uint_as_float(hi));
+}
+
+__device__ __forceinline__ void mma_tf32_acc(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
 template <bool TRANS_A, bool TRANS_B>
 __device__ __forceinline__ void tile_gemm(const float* __restrict__ A, int64_t lda, const float* __restrict__ Bm,
                                           int64_t ldb, int K, int m_lim, int n_lim, float (&acc)[4][4],
-                                          float (*As)[68], float (*Bs)[68]) {
-  const int tid = threadIdx.x;
-  const int ty = tid >> 4, tx = tid & 15;
+                                          float (*As)[TS], float (*Bs)[TS]) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, tq = lane & 3;
+  const int mb = 16 * (warp & 3), nb = 32 * (warp >> 2);
   for (int k0 = 0; k0 < K; k0 += 16) {
     // A chunk 64 x 16 into As[t][r]
     if (TRANS_A) {
@@ -71,36 +96,42 @@ __device__ __forceinline__ void tile_gemm(const float* __restrict__ A, int64_t l
     }
     __syncthreads();
 #pragma unroll
-    for (int t = 0; t < 16; ++t) {
-      const float4 a = *reinterpret_cast<const float4*>(&As[t][ty * 4]);
-      const float4 b = *reinterpret_cast<const float4*>(&Bs[t][tx * 4]);
-      const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+    for (int ks = 0; ks < 16; ks += 8) {
+      uint32_t ahi[4], alo[4];
+      split_tf32(As[ks + tq][mb + g], ahi[0], alo[0]);
+      split_tf32(As[ks + tq][mb + g + 8], ahi[1], alo[1]);
+      split_tf32(As[ks + tq + 4][mb + g], ahi[2], alo[2]);
+      split_tf32(As[ks + tq + 4][mb + g + 8], ahi[3], alo[3]);
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+      for (int nt = 0; nt < 4; ++nt) {
+        uint32_t bh0, bl0, bh1, bl1;
+        split_tf32(Bs[ks + tq][nb + 8 * nt + g], bh0, bl0);
+        split_tf32(Bs[ks + tq + 4][nb + 8 * nt + g], bh1, bl1);
+        mma_tf32_acc(acc[nt], alo, bh0, bh1);
+        mma_tf32_acc(acc[nt], ahi, bl0, bl1);
+        mma_tf32_acc(acc[nt], ahi, bh0, bh1);
+      }
     }
     __syncthreads();
   }
 }
 
-// C(r, c) = alpha * acc + beta * C(r, c) for the thread's 4x4 outputs.
+// C(r, c) = alpha * acc + beta * C(r, c) for the thread's fragment outputs:
+// acc[nt][i] is row 16*(w&3) + g + 8*(i >> 1), column 32*(w>>2) + 8*nt + 2*tq + (i & 1).
 __device__ __forceinline__ void tile_store(float* __restrict__ Cm, int64_t ldc, int m_lim, int n_lim,
                                            const float (&acc)[4][4], float alpha, float beta) {
-  const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
+  const int mb = 16 * (warp & 3), nb = 32 * (warp >> 2);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int r = ty * 4 + i;
-    if (r >= m_lim) continue;
+  for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int cc = tx * 4 + j;
-      if (cc >= n_lim) continue;
+    for (int i = 0; i < 4; ++i) {
+      const int r = mb + g + 8 * (i >> 1), cc = nb + 8 * nt + 2 * tq + (i & 1);
+      if (r >= m_lim || cc >= n_lim) continue;
       float* p = Cm + int64_t(r) * ldc + cc;
-      const float v = alpha * acc[i][j];
+      const float v = alpha * acc[nt][i];
       *p = beta == 0.0f ? v : beta * *p + v;
     }
-  }
 }
 
 // Batched GEMM C = alpha*A*B + beta*C on 64x64 tiles; batch index z = outer*n_inner + inner.
@@ -119,8 +150,8 @@ struct GemmBatch {
 
 template <bool TRANS_A, bool TRANS_B>
 __global__ void __launch_bounds__(256) gemm_kernel(GemmBatch p) {
-  __shared__ __align__(16) float As[16][68];
-  __shared__ __align__(16) float Bs[16][68];
+  __shared__ __align__(16) float As[16][TS];
+  __shared__ __align__(16) float Bs[16][TS];
   const int64_t z = blockIdx.z;
   const int64_t o = z / p.n_inner, in = z % p.n_inner;
   if (p.skip && p.skip[o]) return;
@@ -191,84 +222,135 @@ __global__ void build_reversed_kernel(const float* __restrict__ H, int64_t C, fl
   }
 }
 
-// Factor the 64x64 diagonal block k of Hr[b] (lower) in shared memory and store
-// its inverse (lower, zeros above) in Dinv[b][k]. Records the failing column.
-// 256 threads as a 16 x 16 grid; each right-looking step costs two barriers
-// (every thread reads the pivot and takes its square root itself).
-__global__ void __launch_bounds__(256) potrf_diag_kernel(float* __restrict__ Hr, int64_t C, int k,
+// One warp, 32 x 32 blocks held in registers, lane i owning row i (a[0..31]).
+// Cholesky, right-looking: the pivot and column k come from lane k / lane j by
+// shuffles; every update of a step is independent. Returns 0, or the failing
+// column + 1 (a non-positive pivot); a[] then holds L (lower; upper part garbage).
+__device__ __forceinline__ int warp_potrf32_reg(float (&a)[32], int lane) {
+#pragma unroll
+  for (int k = 0; k < 32; ++k) {
+    const float piv = __shfl_sync(0xFFFFFFFFu, a[k], k);
+    if (!(piv > 0.0f)) return k + 1;  // uniform across the warp
+    const float d = sqrtf(piv);
+    const float lik = lane == k ? d : a[k] / d;
+    a[k] = lane >= k ? lik : a[k];
+#pragma unroll
+    for (int j = k + 1; j < 32; ++j) {
+      const float ljk = __shfl_sync(0xFFFFFFFFu, lik, j);
+      a[j] = a[j] - lik * ljk;
+    }
+  }
+  return 0;
+}
+
+// Column `lane` of X = L^-1 for a 32x32 lower L in shared memory: L x = e_lane.
+__device__ __forceinline__ void col_trinv32(float (&x)[32], const float* L, int ld, int lane) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) x[i] = i == lane ? 1.0f : 0.0f;
+#pragma unroll
+  for (int t = 0; t < 32; ++t) {
+    x[t] = x[t] / L[t * ld + t];
+#pragma unroll
+    for (int i = t + 1; i < 32; ++i) x[i] = x[i] - L[i * ld + t] * x[t];
+  }
+}
+
+// Factor the 64x64 diagonal block k of Hr[b] (lower) and store its inverse (lower,
+// zeros above) in Dinv[b][k]; records the failing column. As a 2 x 2 block of 32 x 32
+// pieces: for each half h (one copy of the code, so the unrolled register loops fit
+// the instruction cache), warp 0 factors the diagonal piece in registers
+// (L_hh = chol(A_hh)) and inverts it (X_hh = L_hh^-1); after the first half all four
+// warps form L21 = A21 X11^T and A22 -= L21 L21^T in shared memory; at the end
+// X21 = -X22 (L21 X11).
+__global__ void __launch_bounds__(128) potrf_diag_kernel(float* __restrict__ Hr, int64_t C, int k,
                                                          float* __restrict__ Dinv, FactorState st) {
-  __shared__ float S[NB][NB + 1];
-  __shared__ float X[NB][NB + 1];
+  constexpr int LD = NB + 1;
+  __shared__ float S[NB * LD];   // the block, then L (lower)
+  __shared__ float X[NB * LD];   // L^-1 (lower)
+  __shared__ float T[32 * 33];   // A21 / L21 X11 scratch
+  __shared__ int fail_s;
   const int64_t b = blockIdx.x;
   if (st.skip[b] || st.info[b]) return;
-  const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   float* blk = Hr + (b * C + int64_t(k) * NB) * C + int64_t(k) * NB;
-  for (int i = tid; i < NB * NB; i += 256) S[i >> 6][i & 63] = blk[int64_t(i >> 6) * C + (i & 63)];
+  for (int i = tid; i < NB * NB; i += 128) S[(i >> 6) * LD + (i & 63)] = blk[int64_t(i >> 6) * C + (i & 63)];
+  if (tid == 0) fail_s = 0;
   __syncthreads();
-  int fail = 0;
-  for (int kk = 0; kk < NB; ++kk) {
-    const float piv = S[kk][kk];
-    if (!(piv > 0.0f)) {  // uniform: every thread read the same value
-      fail = kk + 1;
-      break;
-    }
-    const float d = sqrtf(piv);
-    // column kk below the pivot: L[i][kk] = A[i][kk] / d (row i handled by thread i - kk - 1)
-    const int i = kk + 1 + tid;
-    float lik = 0.0f;
-    if (i < NB) lik = S[i][kk] / d;
-    __syncthreads();  // all reads of column kk done
-    if (i < NB) S[i][kk] = lik;
-    if (tid == 0) S[kk][kk] = d;
-    __syncthreads();
-    // trailing lower triangle: rows / columns kk+1 .. 63 on the 16 x 16 thread grid
-    for (int r = kk + 1 + ty; r < NB; r += 16) {
-      const float lr = S[r][kk];
-      for (int c = kk + 1 + tx; c <= r; c += 16) S[r][c] = S[r][c] - lr * S[c][kk];
-    }
-    __syncthreads();
-  }
-  if (fail) {
-    if (tid == 0) st.info[b] = k * NB + fail;
-    return;
-  }
-  // write L_kk back (lower); X = L^-1 by right-looking elimination on [L | I]:
-  // for each column kk, X[kk][:] /= L[kk][kk], then X[i][:] -= L[i][kk] * X[kk][:], i > kk
-  for (int i = tid; i < NB * NB; i += 256) {
-    const int r = i >> 6, c = i & 63;
-    if (c <= r) blk[int64_t(r) * C + c] = S[r][c];
-    X[r][c] = r == c ? 1.0f : 0.0f;
-  }
-  __syncthreads();
-  for (int kk = 0; kk < NB; ++kk) {
-    const float dk = S[kk][kk];
-    float xk[4];
+#pragma unroll 1
+  for (int h = 0; h < 2; ++h) {
+    const int o = 32 * h;
+    if (warp == 0) {
+      float a[32];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) xk[u] = X[kk][tx + 16 * u] / dk;
-    __syncthreads();
-    if (ty == 0) {
+      for (int j = 0; j < 32; ++j) a[j] = S[(o + lane) * LD + o + j];
+      const int f = warp_potrf32_reg(a, lane);
+      if (f) {
+        if (lane == 0) fail_s = o + f;
+      } else {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) X[kk][tx + 16 * u] = xk[u];
-    }
-    for (int r = kk + 1 + ty; r < NB; r += 16) {
-      const float l = S[r][kk];
+        for (int j = 0; j < 32; ++j)
+          if (j <= lane) S[(o + lane) * LD + o + j] = a[j];
+        __syncwarp();
+        col_trinv32(a, S + o * LD + o, LD, lane);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int c = tx + 16 * u;
-        if (c <= kk) X[r][c] = X[r][c] - l * xk[u];
+        for (int i = 0; i < 32; ++i) X[(o + i) * LD + o + lane] = a[i];
       }
     }
     __syncthreads();
+    if (fail_s) {
+      if (tid == 0) st.info[b] = k * NB + fail_s;
+      return;
+    }
+    if (h == 0) {
+      for (int e = tid; e < 32 * 32; e += 128) T[(e >> 5) * 33 + (e & 31)] = S[(32 + (e >> 5)) * LD + (e & 31)];
+      __syncthreads();
+      for (int e = tid; e < 32 * 32; e += 128) {  // L21 = A21 X11^T (X11 lower: t <= j)
+        const int i = e >> 5, j = e & 31;
+        float acc = 0.0f;
+        for (int t = 0; t <= j; ++t) acc = acc + T[i * 33 + t] * X[j * LD + t];
+        S[(32 + i) * LD + j] = acc;
+      }
+      __syncthreads();
+      for (int e = tid; e < 32 * 32; e += 128) {  // A22 -= L21 L21^T (lower)
+        const int i = e >> 5, j = e & 31;
+        if (j > i) continue;
+        float acc = 0.0f;
+        for (int t = 0; t < 32; ++t) acc = acc + S[(32 + i) * LD + t] * S[(32 + j) * LD + t];
+        S[(32 + i) * LD + 32 + j] = S[(32 + i) * LD + 32 + j] - acc;
+      }
+      __syncthreads();
+    }
   }
+  for (int i = tid; i < NB * NB; i += 128) {  // write L back (lower)
+    const int r = i >> 6, c = i & 63;
+    if (c <= r) blk[int64_t(r) * C + c] = S[r * LD + c];
+  }
+  for (int e = tid; e < 32 * 32; e += 128) {  // T = L21 X11 (X11 lower: t >= j)
+    const int i = e >> 5, j = e & 31;
+    float acc = 0.0f;
+    for (int t = j; t < 32; ++t) acc = acc + S[(32 + i) * LD + t] * X[t * LD + j];
+    T[i * 33 + j] = acc;
+  }
+  __syncthreads();
+  for (int e = tid; e < 32 * 32; e += 128) {  // X21 = -X22 T (X22 lower: t <= i)
+    const int i = e >> 5, j = e & 31;
+    float acc = 0.0f;
+    for (int t = 0; t <= i; ++t) acc = acc + X[(32 + i) * LD + 32 + t] * T[t * 33 + j];
+    X[(32 + i) * LD + j] = -acc;
+  }
+  __syncthreads();
   float* D = Dinv + (b * (C / NB) + k) * NB * NB;
-  for (int i = tid; i < NB * NB; i += 256) D[i] = X[i >> 6][i & 63];
+  for (int i = tid; i < NB * NB; i += 128) {
+    const int r = i >> 6, c = i & 63;
+    D[i] = c <= r ? X[r * LD + c] : 0.0f;
+  }
 }
 
 // Panel solve: A[i][k] = A[i][k] * L_kk^-T for block rows i > k (in place, one CTA per block).
 __global__ void __launch_bounds__(256) trsm_panel_kernel(float* __restrict__ Hr, int64_t C, int k,
                                                          const float* __restrict__ Dinv, FactorState st) {
-  __shared__ __align__(16) float As[16][68];
-  __shared__ __align__(16) float Bs[16][68];
+  __shared__ __align__(16) float As[16][TS];
+  __shared__ __align__(16) float Bs[16][TS];
   const int64_t b = blockIdx.y;
   if (st.skip[b] || st.info[b]) return;
   const int i = k + 1 + blockIdx.x;
@@ -282,8 +364,8 @@ __global__ void __launch_bounds__(256) trsm_panel_kernel(float* __restrict__ Hr,
 
 // Trailing update on block tiles (i, j) with k < j <= i: A_ij -= A_ik A_jk^T.
 __global__ void __launch_bounds__(256) syrk_kernel(float* __restrict__ Hr, int64_t C, int k, FactorState st) {
-  __shared__ __align__(16) float As[16][68];
-  __shared__ __align__(16) float Bs[16][68];
+  __shared__ __align__(16) float As[16][TS];
+  __shared__ __align__(16) float Bs[16][TS];
   const int64_t b = blockIdx.y;
   if (st.skip[b] || st.info[b]) return;
   // linear tile index -> (ii, jj), 0 <= jj <= ii < m
@@ -492,7 +574,7 @@ extern "C" int gq_prepare_hinv(const float* H, int64_t B, int64_t C, float damp,
   for (int attempt = 0; attempt < 6; ++attempt) {
     build_reversed_kernel<<<dim3(ew_blocks, unsigned(B)), 256, 0, s>>>(H, C, Hr, st);
     for (int k = 0; k < nb; ++k) {
-      potrf_diag_kernel<<<unsigned(B), 256, 0, s>>>(Hr, C, k, Dinv, st);
+      potrf_diag_kernel<<<unsigned(B), 128, 0, s>>>(Hr, C, k, Dinv, st);
       const int m = nb - k - 1;
       if (m > 0) {
         trsm_panel_kernel<<<dim3(unsigned(m), unsigned(B)), 256, 0, s>>>(Hr, C, k, Dinv, st);
