@@ -1,0 +1,109 @@
+"""Golden artifacts of the REAL reference's layer-sequential Stage A on CPU.
+
+Runs mlx_gptq.sequential.Pipeline (the reference's own capture, Hessians,
+solve_gptq, artifact writer) over a tiny seeded Qwen3-MoE checkpoint and stores
+its per-tensor codes, scales, rel_err and token counts in stack_mxfp4.npz:
+
+    python tests/golden/make_stack_golden.py [--ref PATH_TO_REFERENCE_CHECKOUT]
+
+The checkpoint is not stored: write_checkpoint() regenerates it bit for bit from
+its seed (CPU generators), in this container and on a GPU box, so the tests run
+their own pipeline on the same weights and windows and compare with the fixture.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import tempfile
+import types
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(ROOT, "mlx-gptq-mxfp_b200"))
+
+STACK_CONFIG = dict(model_type="qwen3_moe", vocab_size=512, hidden_size=128, intermediate_size=256,
+                    moe_intermediate_size=64, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                    head_dim=32, num_experts=8, num_experts_per_tok=2, decoder_sparse_step=1, norm_topk_prob=True,
+                    max_position_embeddings=256)
+WINDOWS_SEED, N_WINDOWS, SEQLEN, BATCH = 1, 8, 64, 4
+
+
+def write_checkpoint(path: str, cfg: dict = STACK_CONFIG, seed: int = 0) -> str:
+    """config.json + model.safetensors (per-expert tensors, as Hugging Face ships them),
+    weights from mlx_gptq_b200.sequential.SyntheticWeights on the CPU, stored in bf16."""
+    from safetensors.torch import save_file
+
+    from mlx_gptq_b200 import sequential
+
+    os.makedirs(path, exist_ok=True)
+    with open(os.path.join(path, "config.json"), "w") as f:
+        json.dump(cfg, f)
+    model = sequential.build_model(dict(cfg))
+    src = sequential.SyntheticWeights(model, "cpu", seed=seed)
+    tensors = {}
+    for name in src.shapes:
+        t = src.get(name).to(torch.bfloat16)
+        if name.endswith(("experts.gate_up_proj", "experts.down_proj")):
+            base, kind = name.rsplit(".", 1)
+            for e in range(t.shape[0]):
+                if kind == "gate_up_proj":
+                    half = t.shape[1] // 2
+                    tensors[f"{base}.{e}.gate_proj.weight"] = t[e, :half].contiguous()
+                    tensors[f"{base}.{e}.up_proj.weight"] = t[e, half:].contiguous()
+                else:
+                    tensors[f"{base}.{e}.down_proj.weight"] = t[e].contiguous()
+        else:
+            tensors[name] = t.contiguous()
+    save_file(tensors, os.path.join(path, "model.safetensors"))
+    return path
+
+
+def windows() -> np.ndarray:
+    return np.random.default_rng(WINDOWS_SEED).integers(0, STACK_CONFIG["vocab_size"],
+                                                        (N_WINDOWS, SEQLEN)).astype(np.int64)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default=os.environ.get("MLX_GPTQ_REFERENCE", "/root/reference"))
+    a = ap.parse_args()
+    sys.path.insert(0, a.ref)
+    from mlx_gptq.artifacts import ArtifactReader, ArtifactWriter
+    from mlx_gptq.sequential import DEFAULT_EXCLUDE, Pipeline, RawShardIndex
+
+    from mlx_gptq_b200 import sequential
+
+    torch.manual_seed(0)
+    with tempfile.TemporaryDirectory(dir=os.path.join(ROOT, "_work") if os.path.isdir(os.path.join(ROOT, "_work"))
+                                     else None) as tmp:
+        model_dir = write_checkpoint(os.path.join(tmp, "model"))
+        out = os.path.join(tmp, "out")
+        args = types.SimpleNamespace(devices=["cpu"], dtype="bfloat16", layers_attr="model.layers",
+                                     checkpoint_model_prefix=None, artifact_layers_prefix=None, batch_size=BATCH,
+                                     exclude=DEFAULT_EXCLUDE, group_size=32, bits=4, mode="mxfp4",
+                                     mxfp_algorithm="safe-scale-search", damp=0.01, clip="mse", overrides=[],
+                                     vram_gb={"cpu": 16.0}, lazy_ple=False)
+        model = sequential.build_model(dict(STACK_CONFIG))  # meta skeleton, eager experts
+        writer = ArtifactWriter(out, {"mode": "mxfp4", "bits": 4, "group_size": 32, "storage_dtype": "bfloat16"})
+        with torch.no_grad():
+            Pipeline(model, RawShardIndex(model_dir), args).run(torch.from_numpy(windows()), writer)
+        reader = ArtifactReader(out)
+        fx, meta = {}, {}
+        for name, info in sorted(reader.tensors.items()):
+            q, s, b, info = reader.get(name)
+            fx[f"q:{name}"] = q.numpy().astype(np.uint8)
+            fx[f"s:{name}"] = s.numpy().astype(np.uint8)
+            meta[name] = {"rel_err": info["rel_err"], "tokens": info["tokens"], "kind": info["kind"]}
+        fx["meta"] = np.frombuffer(json.dumps(meta, sort_keys=True).encode(), dtype=np.uint8)
+        np.savez_compressed(os.path.join(HERE, "stack_mxfp4.npz"), **fx)
+        print(f"stack_mxfp4.npz: {len(meta)} tensors")
+
+
+if __name__ == "__main__":
+    main()

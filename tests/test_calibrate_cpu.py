@@ -103,30 +103,9 @@ def test_multimodal_checkpoint_prefixes_are_independent():
 
 
 def write_tiny_checkpoint(path, cfg=TINY, seed=0):
-    """config.json + model.safetensors with per-expert tensors, as Hugging Face ships them."""
-    from safetensors.torch import save_file
+    from golden.make_stack_golden import write_checkpoint
 
-    os.makedirs(path, exist_ok=True)
-    with open(os.path.join(path, "config.json"), "w") as f:
-        json.dump(cfg, f)
-    model = sequential.build_model(dict(cfg))
-    src = sequential.SyntheticWeights(model, "cpu", seed=seed)
-    tensors = {}
-    for name in src.shapes:
-        t = src.get(name).to(torch.bfloat16)
-        if name.endswith(("experts.gate_up_proj", "experts.down_proj")):
-            base, kind = name.rsplit(".", 1)
-            for e in range(t.shape[0]):
-                if kind == "gate_up_proj":
-                    half = t.shape[1] // 2
-                    tensors[f"{base}.{e}.gate_proj.weight"] = t[e, :half].contiguous()
-                    tensors[f"{base}.{e}.up_proj.weight"] = t[e, half:].contiguous()
-                else:
-                    tensors[f"{base}.{e}.down_proj.weight"] = t[e].contiguous()
-        else:
-            tensors[name] = t.contiguous()
-    save_file(tensors, os.path.join(path, "model.safetensors"))
-    return path
+    return write_checkpoint(path, cfg, seed)
 
 
 def test_cli_runs_and_resumes_on_cpu(tmp_path, monkeypatch):
