@@ -22,6 +22,11 @@ which the reference solves independently).
 
 Under torchrun each rank solves its own copy of the workload (weak scaling, no
 data-path collective); timing is the max over ranks.
+
+--config c5 instead calibrates a synthetic Qwen3-30B-A3B-shaped layer stack
+layer by layer through the package's Pipeline and
+prints per-layer stage times (--layers L, --c5-dp for data-parallel windows).
+--profile-case NAME runs one small kernel case for an ncu capture.
 """
 
 from __future__ import annotations

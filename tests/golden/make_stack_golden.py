@@ -80,8 +80,9 @@ def main():
     from mlx_gptq_b200 import sequential
 
     torch.manual_seed(0)
-    with tempfile.TemporaryDirectory(dir=os.path.join(ROOT, "_work") if os.path.isdir(os.path.join(ROOT, "_work"))
-                                     else None) as tmp:
+    scratch = os.path.join(ROOT, "_build")  # git-ignored build scratch
+    os.makedirs(scratch, exist_ok=True)
+    with tempfile.TemporaryDirectory(dir=scratch) as tmp:
         model_dir = write_checkpoint(os.path.join(tmp, "model"))
         out = os.path.join(tmp, "out")
         args = types.SimpleNamespace(devices=["cpu"], dtype="bfloat16", layers_attr="model.layers",
