@@ -248,9 +248,12 @@ def hessian_cases(capture):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("GQ_REFERENCE", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("GQ_REFERENCE"),
+                    help="reference checkout (or set GQ_REFERENCE)")
     ap.add_argument("--skip-exhaustive", action="store_true")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("--ref (or GQ_REFERENCE) must point at the reference checkout")
     sys.path.insert(0, os.path.join(HERE, "..", ".."))
     sys.path.insert(0, args.ref)
     torch.set_num_threads(max(1, os.cpu_count() or 1))

@@ -71,8 +71,11 @@ def windows() -> np.ndarray:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("MLX_GPTQ_REFERENCE", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("GQ_REFERENCE"),
+                    help="reference checkout (or set GQ_REFERENCE)")
     a = ap.parse_args()
+    if not a.ref:
+        ap.error("--ref (or GQ_REFERENCE) must point at the reference checkout")
     sys.path.insert(0, a.ref)
     from mlx_gptq.artifacts import ArtifactReader, ArtifactWriter
     from mlx_gptq.sequential import DEFAULT_EXCLUDE, Pipeline, RawShardIndex
