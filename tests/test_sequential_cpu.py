@@ -393,3 +393,29 @@ def test_dp_windows_stack_matches_single_process(tmp_path):
     assert len(hidden) == len(ref["hidden"])
     for a, b in zip(hidden, ref["hidden"]):
         assert torch.equal(a, b)
+
+
+def test_segment_store_grows_without_a_reservation():
+    """Buffers double when no token count is reserved; the rows stay in capture order."""
+    from mlx_gptq_b200.capture import SegmentStore
+
+    st = SegmentStore(num_experts=3)
+    g = torch.Generator().manual_seed(0)
+    ref_in, ref_act, ref_tok = [], [], []
+    for T in (5, 9, 17):
+        hidden = torch.randn(T, 4, generator=g)
+        counts = [T, 0, T]  # 2 slots per token
+        tok = torch.cat([torch.arange(T), torch.arange(T)])
+        out = st.acts_out(2 * T, T, 6, torch.float32, "cpu")
+        acts = torch.randn(2 * T, 6, generator=g)
+        out.copy_(acts)
+        st.add(hidden, tok, counts, out)
+        ref_in.append(hidden)
+        ref_act.append(acts)
+        ref_tok.append(tok + sum(h.shape[0] for h in ref_in[:-1]))
+    assert st.n_tok == 31 and st.n_slot == 62 and st.counts == [31, 0, 31]
+    assert torch.equal(st.inputs[:st.n_tok], torch.cat(ref_in))
+    assert torch.equal(st.acts[:st.n_slot], torch.cat(ref_act))
+    assert torch.equal(st.tok[:st.n_slot].long(), torch.cat(ref_tok))
+    assert torch.equal(st.slot_experts("cpu"), torch.cat([torch.tensor([0] * T + [2] * T) for T in (5, 9, 17)]))
+    assert st.nbytes() > 0
