@@ -164,8 +164,158 @@ __global__ void __launch_bounds__(256) gemm_kernel(GemmBatch p) {
   tile_store(Cm, p.ldc, p.M - m0, p.N - n0, acc, p.alpha, p.beta);
 }
 
+// ---------------------------------------------------------------------------
+// 128x128-tile GEMM on the tensor cores for the large products (the trailing
+// update W[:, i2:] -= Err U[i1:i2, i2:] and the inverse-doubling GEMMs): 8 warps as
+// 2 (M) x 4 (N), each 64 x 32 = 4 x 4 m16n8k8 fragments in 3xTF32; 32-deep K tiles
+// double-buffered in shared memory with cp.async (16-byte chunks, zero-filled past
+// the matrix edges). Each operand is staged in the orientation its global layout
+// copies contiguously, with row strides (36 or 136 floats) that make every
+// fragment load bank-conflict free. Used for deep products (K >= 256: the
+// inverse doubling) whose copied chunks are all 16-byte aligned (checked on the
+// host); the 64x64 tiles above, at several CTAs per SM, serve the rest, the
+// K = 128 trailing update among them (measured faster there).
+// ---------------------------------------------------------------------------
+namespace g128 {
+constexpr int BM = 128, BN = 128, BK = 32, THREADS = 256;
+constexpr int LDS_ROW = BK + 4;    // [128][36]: rows are M (or N), 32 k each
+constexpr int LDS_COL = BM + 8;    // [32][136]: rows are k, 128 M (or N) each
+constexpr int A_FLOATS = BM * LDS_ROW > BK * LDS_COL ? BM * LDS_ROW : BK * LDS_COL;
+constexpr int STAGE_FLOATS = 2 * A_FLOATS;
+constexpr size_t SMEM_BYTES = size_t(2) * STAGE_FLOATS * 4;
+
+__device__ __forceinline__ void cp_async16(float* dst, const float* src, int src_bytes) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(src), "r"(src_bytes));
+}
+
+// Stage a (rows x 32) or (32 x rows) block of one operand. ROWMAJOR_K: the global
+// layout has k contiguous (element (i, k) at p[i * ld + k]); else i is contiguous.
+template <bool K_CONTIG>
+__device__ __forceinline__ void stage(float* sm, const float* p, int64_t ld, int lim_i, int k0, int K) {
+  const int tid = threadIdx.x;
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int ch = tid + u * THREADS;  // 1024 chunks of 4 floats
+    if (K_CONTIG) {
+      const int i = ch >> 3, kc = (ch & 7) * 4, k = k0 + kc;
+      int bytes = 0;
+      if (i < lim_i && k < K) bytes = (K - k >= 4 ? 4 : K - k) * 4;
+      cp_async16(sm + i * LDS_ROW + kc, bytes ? p + int64_t(i) * ld + k : p, bytes);
+    } else {
+      const int kr = ch >> 5, ic = (ch & 31) * 4, k = k0 + kr;
+      int bytes = 0;
+      if (k < K && ic < lim_i) bytes = (lim_i - ic >= 4 ? 4 : lim_i - ic) * 4;
+      cp_async16(sm + kr * LDS_COL + ic, bytes ? p + int64_t(k) * ld + ic : p, bytes);
+    }
+  }
+}
+
+template <bool TRANS_A, bool TRANS_B>
+__global__ void __launch_bounds__(THREADS) gemm128_kernel(GemmBatch p) {
+  extern __shared__ __align__(16) float smem[];
+  const int64_t z = blockIdx.z;
+  const int64_t o = z / p.n_inner, in = z % p.n_inner;
+  if (p.skip && p.skip[o]) return;
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  // A(r, k): TRANS_A ? A[k * lda + r] : A[r * lda + k];  B(k, c): TRANS_B ? B[c * ldb + k] : B[k * ldb + c]
+  const float* A = p.A + o * p.sa_o + in * p.sa_i + (TRANS_A ? int64_t(m0) : int64_t(m0) * p.lda);
+  const float* Bm = p.Bm + o * p.sb_o + in * p.sb_i + (TRANS_B ? int64_t(n0) * p.ldb : int64_t(n0));
+  const int lim_m = p.M - m0, lim_n = p.N - n0, K = p.K;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, tq = lane & 3;
+  const int wm = 64 * (warp & 1), wn = 32 * (warp >> 1);
+  float acc[4][4][4] = {};
+  const int KT = (K + BK - 1) / BK;
+  auto issue = [&](int kt) {
+    float* st = smem + (kt & 1) * STAGE_FLOATS;
+    stage<!TRANS_A>(st, A, p.lda, lim_m, kt * BK, K);
+    stage<TRANS_B>(st + A_FLOATS, Bm, p.ldb, lim_n, kt * BK, K);
+    asm volatile("cp.async.commit_group;\n" ::);
+  };
+  issue(0);
+  for (int kt = 0; kt < KT; ++kt) {
+    if (kt + 1 < KT) {
+      issue(kt + 1);
+      asm volatile("cp.async.wait_group 1;\n" ::);
+    } else {
+      asm volatile("cp.async.wait_group 0;\n" ::);
+    }
+    __syncthreads();
+    const float* As = smem + (kt & 1) * STAGE_FLOATS;
+    const float* Bs = As + A_FLOATS;
+#pragma unroll
+    for (int kk = 0; kk < BK; kk += 8) {
+      uint32_t bh[4][2], bl[4][2];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int c = wn + 8 * j + g;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int k = kk + tq + 4 * h;
+          const float v = TRANS_B ? Bs[c * LDS_ROW + k] : Bs[k * LDS_COL + c];
+          split_tf32(v, bh[j][h], bl[j][h]);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint32_t ah[4], al[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int r = wm + 16 * i + g + 8 * (q & 1), k = kk + tq + 4 * (q >> 1);
+          const float v = TRANS_A ? As[k * LDS_COL + r] : As[r * LDS_ROW + k];
+          split_tf32(v, ah[q], al[q]);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          mma_tf32_acc(acc[i][j], al, bh[j][0], bh[j][1]);
+          mma_tf32_acc(acc[i][j], ah, bl[j][0], bl[j][1]);
+          mma_tf32_acc(acc[i][j], ah, bh[j][0], bh[j][1]);
+        }
+      }
+    }
+    __syncthreads();  // this stage is refilled by the next iteration's issue
+  }
+  float* Cm = p.Cm + o * p.sc_o + in * p.sc_i + int64_t(m0) * p.ldc + n0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int r = wm + 16 * i + g + 8 * (q >> 1), c = wn + 8 * j + 2 * tq + (q & 1);
+        if (r >= lim_m || c >= lim_n) continue;
+        float* ptr = Cm + int64_t(r) * p.ldc + c;
+        const float v = p.alpha * acc[i][j][q];
+        *ptr = p.beta == 0.0f ? v : p.beta * *ptr + v;
+      }
+}
+
+// Every cp.async source must be 16-byte aligned: bases, leading dimensions and
+// batch strides in whole 4-float units.
+static bool usable(const GemmBatch& p) {
+  auto al = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  return al(p.A) && al(p.Bm) && p.lda % 4 == 0 && p.ldb % 4 == 0 && p.sa_o % 4 == 0 && p.sa_i % 4 == 0 &&
+         p.sb_o % 4 == 0 && p.sb_i % 4 == 0 && (p.M >= BM || p.N >= BN) && p.K >= 8 * BK;
+}
+
+template <bool TA, bool TB>
+static int launch(const GemmBatch& p, int64_t batches, cudaStream_t s) {
+  GQ_CUDA_TRY(cudaFuncSetAttribute(gemm128_kernel<TA, TB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   int(SMEM_BYTES)));
+  const dim3 grid(unsigned((p.N + BN - 1) / BN), unsigned((p.M + BM - 1) / BM), unsigned(batches));
+  gemm128_kernel<TA, TB><<<grid, THREADS, SMEM_BYTES, s>>>(p);
+  return check_launch("gemm128_kernel");
+}
+}  // namespace g128
+
 static int launch_gemm(const GemmBatch& p, bool trans_a, bool trans_b, int64_t batches, cudaStream_t s) {
   if (batches <= 0 || p.M <= 0 || p.N <= 0) return GQ_OK;
+  if (g128::usable(p)) {
+    if (trans_a && trans_b) return g128::launch<true, true>(p, batches, s);
+    if (trans_a) return g128::launch<true, false>(p, batches, s);
+    if (trans_b) return g128::launch<false, true>(p, batches, s);
+    return g128::launch<false, false>(p, batches, s);
+  }
   const dim3 grid(unsigned((p.N + 63) / 64), unsigned((p.M + 63) / 64), unsigned(batches));
   if (trans_a && trans_b)
     gemm_kernel<true, true><<<grid, 256, 0, s>>>(p);
