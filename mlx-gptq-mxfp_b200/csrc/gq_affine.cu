@@ -15,6 +15,8 @@
 // start, the per-column quantize / error / in-block rank-1 update. Err [B, R, bs]
 // goes to the workspace and the trailing update W[:, :, i2:] -= Err * U[i1:i2, i2:]
 // is a batched float32 GEMM.
+#include <map>
+#include <mutex>
 #include <vector>
 
 #include "gq_affine_grid.cuh"
@@ -23,6 +25,26 @@ namespace gq {
 namespace aff {
 
 constexpr int NB = 64;  // factorization block
+
+// One non-blocking side stream per device for the factorization's lookahead,
+// created on first use and kept for the life of the process.
+static cudaError_t side_stream(cudaStream_t* out) {
+  static std::mutex mu;
+  static std::map<int, cudaStream_t> streams;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = streams.find(dev);
+  if (it == streams.end()) {
+    cudaStream_t st = nullptr;
+    e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return e;
+    it = streams.emplace(dev, st).first;
+  }
+  *out = it->second;
+  return cudaSuccess;
+}
 
 // ---------------------------------------------------------------------------
 // 64x64 float32 tile GEMM building block on the tensor cores (256 threads)
@@ -513,17 +535,32 @@ __global__ void __launch_bounds__(256) trsm_panel_kernel(float* __restrict__ Hr,
 }
 
 // Trailing update on block tiles (i, j) with k < j <= i: A_ij -= A_ik A_jk^T.
-__global__ void __launch_bounds__(256) syrk_kernel(float* __restrict__ Hr, int64_t C, int k, FactorState st) {
+// part 0: every such tile; part 1: the next block column only (j = k + 1), the
+// one the next diagonal factor and panel solve wait for; part 2: the rest
+// (j >= k + 2), which can run beside them.
+__global__ void __launch_bounds__(256) syrk_kernel(float* __restrict__ Hr, int64_t C, int k, int part,
+                                                   FactorState st) {
   __shared__ __align__(16) float As[16][TS];
   __shared__ __align__(16) float Bs[16][TS];
   const int64_t b = blockIdx.y;
   if (st.skip[b] || st.info[b]) return;
-  // linear tile index -> (ii, jj), 0 <= jj <= ii < m
-  const int t = blockIdx.x;
-  int ii = int((sqrtf(8.0f * float(t) + 1.0f) - 1.0f) * 0.5f);
-  while ((ii + 1) * (ii + 2) / 2 <= t) ++ii;
-  while (ii * (ii + 1) / 2 > t) --ii;
-  const int jj = t - ii * (ii + 1) / 2;
+  int ii, jj;
+  if (part == 1) {
+    ii = blockIdx.x;
+    jj = 0;
+  } else {
+    // linear tile index -> (ii, jj), 0 <= jj <= ii (over the triangle from column
+    // k + 1, or from k + 2 for part 2)
+    const int t = blockIdx.x;
+    ii = int((sqrtf(8.0f * float(t) + 1.0f) - 1.0f) * 0.5f);
+    while ((ii + 1) * (ii + 2) / 2 <= t) ++ii;
+    while (ii * (ii + 1) / 2 > t) --ii;
+    jj = t - ii * (ii + 1) / 2;
+    if (part == 2) {
+      ++ii;
+      ++jj;
+    }
+  }
   const int i = k + 1 + ii, j = k + 1 + jj;
   const float* Aik = Hr + (b * C + int64_t(i) * NB) * C + int64_t(k) * NB;
   const float* Ajk = Hr + (b * C + int64_t(j) * NB) * C + int64_t(k) * NB;
@@ -721,16 +758,45 @@ extern "C" int gq_prepare_hinv(const float* H, int64_t B, int64_t C, float damp,
   diag_mean_kernel<<<unsigned(B), 256, 0, s>>>(H, C, damp, st);
   std::vector<int32_t> hinfo(B);
   bool ok = false;
+  // Lookahead: the trailing update of step k is split; its next block column runs on
+  // the caller's stream (the next diagonal factor and panel solve need it), the rest
+  // on a side stream beside them. Events order the two: the rest of step k starts
+  // after the panel solve and next-column update of step k, and the next-column
+  // update of step k + 1 (which writes tiles the rest of step k also writes) waits
+  // for it. No tile is written by both streams at once.
+  cudaStream_t side = nullptr;
+  cudaEvent_t ev_main = nullptr, ev_side = nullptr;
+  GQ_CUDA_TRY(side_stream(&side));
+  GQ_CUDA_TRY(cudaEventCreateWithFlags(&ev_main, cudaEventDisableTiming));
+  GQ_CUDA_TRY(cudaEventCreateWithFlags(&ev_side, cudaEventDisableTiming));
+  struct EventGuard {
+    cudaEvent_t a, b;
+    ~EventGuard() {
+      cudaEventDestroy(a);
+      cudaEventDestroy(b);
+    }
+  } guard{ev_main, ev_side};
   for (int attempt = 0; attempt < 6; ++attempt) {
     build_reversed_kernel<<<dim3(ew_blocks, unsigned(B)), 256, 0, s>>>(H, C, Hr, st);
+    bool side_pending = false;
     for (int k = 0; k < nb; ++k) {
       potrf_diag_kernel<<<unsigned(B), 128, 0, s>>>(Hr, C, k, Dinv, st);
       const int m = nb - k - 1;
       if (m > 0) {
         trsm_panel_kernel<<<dim3(unsigned(m), unsigned(B)), 256, 0, s>>>(Hr, C, k, Dinv, st);
-        syrk_kernel<<<dim3(unsigned(m * (m + 1) / 2), unsigned(B)), 256, 0, s>>>(Hr, C, k, st);
+        if (side_pending) GQ_CUDA_TRY(cudaStreamWaitEvent(s, ev_side, 0));
+        syrk_kernel<<<dim3(unsigned(m), unsigned(B)), 256, 0, s>>>(Hr, C, k, 1, st);
+        side_pending = false;
+        if (m > 1) {
+          GQ_CUDA_TRY(cudaEventRecord(ev_main, s));
+          GQ_CUDA_TRY(cudaStreamWaitEvent(side, ev_main, 0));
+          syrk_kernel<<<dim3(unsigned((m - 1) * m / 2), unsigned(B)), 256, 0, side>>>(Hr, C, k, 2, st);
+          GQ_CUDA_TRY(cudaEventRecord(ev_side, side));
+          side_pending = true;
+        }
       }
     }
+    if (side_pending) GQ_CUDA_TRY(cudaStreamWaitEvent(s, ev_side, 0));
     int stl = check_launch("cholesky kernels");
     if (stl != GQ_OK) return stl;
     GQ_CUDA_TRY(cudaMemcpyAsync(hinfo.data(), st.info, size_t(B) * 4, cudaMemcpyDeviceToHost, s));

@@ -159,16 +159,17 @@ def _fake_solve(W, H, bits, args):
     return q, s, None, W_dq, rel
 
 
-def install_fakes(pipeline_mod, capture_mod):
-    """Replace the CUDA pieces the layer solve calls with CPU stand-ins."""
-    pipeline_mod._solve_batch = _fake_solve
-    pipeline_mod.dequantize_artifact = _fake_dequant
-    pipeline_mod.pack_nibbles = _fake_pack
-    pipeline_mod.unpack_nibbles = _fake_unpack
-    pipeline_mod.hessian_tile_count = _fake_tile_count
-    pipeline_mod.hessian_tiles_per_wave = _fake_tiles_per_wave
-    capture_mod.CaptureManager.expert_hessians = _fake_expert_hessians
-    capture_mod.Stash.hessian = _fake_stash_hessian
+def install_fakes(pipeline_mod, capture_mod, setattr_=setattr):
+    """Replace the CUDA pieces the layer solve calls with CPU stand-ins (pass
+    monkeypatch.setattr inside the test process, so they are undone afterwards)."""
+    for obj, name, fn in ((pipeline_mod, "_solve_batch", _fake_solve),
+                          (pipeline_mod, "dequantize_artifact", _fake_dequant),
+                          (pipeline_mod, "pack_nibbles", _fake_pack), (pipeline_mod, "unpack_nibbles", _fake_unpack),
+                          (pipeline_mod, "hessian_tile_count", _fake_tile_count),
+                          (pipeline_mod, "hessian_tiles_per_wave", _fake_tiles_per_wave),
+                          (capture_mod.CaptureManager, "expert_hessians", _fake_expert_hessians),
+                          (capture_mod.Stash, "hessian", _fake_stash_hessian)):
+        setattr_(obj, name, fn)
 
 
 def _fake_expert_hessians(self, task, device, experts=None, timer=None):
@@ -195,12 +196,12 @@ def _fake_tiles_per_wave(device=None):
     return 20  # a 32-feature stash (32 "tiles") is formed in two parts
 
 
-def _run_layer(rank, world, port, out_dir):
+def _run_layer(rank, world, port, out_dir, setattr_=setattr):
     import torch.distributed as dist
 
     from mlx_gptq_b200 import capture, pipeline
 
-    install_fakes(pipeline, capture)
+    install_fakes(pipeline, capture, setattr_)
     group = None
     if world > 1:
         dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
@@ -220,12 +221,12 @@ def _run_layer(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
-def test_sharded_layer_solve_matches_single_process(tmp_path):
+def test_sharded_layer_solve_matches_single_process(tmp_path, monkeypatch):
     import socket
 
     import torch.multiprocessing as mp
 
-    _run_layer(0, 1, 0, str(tmp_path))
+    _run_layer(0, 1, 0, str(tmp_path), monkeypatch.setattr)
     with socket.socket() as sk:
         sk.bind(("127.0.0.1", 0))
         port = sk.getsockname()[1]
@@ -268,3 +269,37 @@ def test_plan_layer_covers_every_item_once_and_balances(monkeypatch):
         assert sorted(k for p in plans for k in p["linears"]) == sorted(t.name for t in mgr.linear_tasks)
     # q/k share one stash: one linear item
     assert len(by_stash) == 1 and len(next(iter(by_stash.values()))) == 2
+
+
+def test_vram_budget_splits_expert_batches(monkeypatch):
+    """A budget smaller than one expert's working set solves experts in chunks of one;
+    the artifacts equal those of one batched solve (sequential.py:314-318)."""
+    from mlx_gptq_b200 import capture, pipeline
+
+    install_fakes(pipeline, capture, monkeypatch.setattr)
+    calls = []
+    real = pipeline._solve_batch
+
+    def counting(W, H, bits, args):
+        calls.append(W.shape[0])
+        return real(W, H, bits, args)
+
+    monkeypatch.setattr(pipeline, "_solve_batch", counting)
+    assert pipeline.expert_chunk_size(2048, 1536, 16.0) == int(16 * 2**30 // ((3 * 2048**2 + 3 * 1536 * 2048) * 4))
+    assert pipeline.expert_chunk_size(64, 64, 1e-9) == 1
+    out = {}
+    for budget in (None, 1e-9):
+        torch.manual_seed(0)
+        layer = ToyMoELayer(E=5, k=2)
+        mgr = CaptureManager(layer, exclude_regex=r"(^|\.)gate$", group_size=32)
+        with mgr:
+            mgr.begin_batch()
+            layer(torch.randn(40, 32))
+        calls.clear()
+        res = pipeline.solve_layer("model.layers.0", mgr, LayerSolveArgs(bits=4, group_size=32, mode="mxfp4",
+                                                                         vram_gb=budget), "cpu")
+        out[budget] = (res, list(calls))
+    assert max(out[1e-9][1]) == 1 and max(out[None][1]) == 5
+    for k, (q, s, b) in out[None][0].tensors.items():
+        q2, s2, _ = out[1e-9][0].tensors[k]
+        assert torch.equal(q, q2) and torch.equal(s, s2)

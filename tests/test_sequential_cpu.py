@@ -191,7 +191,7 @@ def test_tiny_qwen3_moe_stack_names_and_stats(monkeypatch):
     assert all(p.is_meta for p in model.model.layers[0].parameters())
 
 
-def _run_stack(rank, world, port, out_dir):
+def _run_stack(rank, world, port, out_dir, setattr_=setattr):
     import sys
 
     import torch.distributed as dist
@@ -201,7 +201,7 @@ def _run_stack(rank, world, port, out_dir):
 
     from mlx_gptq_b200 import capture, pipeline
 
-    install_fakes(pipeline, capture)
+    install_fakes(pipeline, capture, setattr_)
     group = None
     if world > 1:
         dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
@@ -216,12 +216,12 @@ def _run_stack(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
-def test_sharded_stack_matches_single_process(tmp_path):
+def test_sharded_stack_matches_single_process(tmp_path, monkeypatch):
     import socket
 
     import torch.multiprocessing as mp
 
-    _run_stack(0, 1, 0, str(tmp_path))
+    _run_stack(0, 1, 0, str(tmp_path), monkeypatch.setattr)
     with socket.socket() as sk:
         sk.bind(("127.0.0.1", 0))
         port = sk.getsockname()[1]
@@ -339,7 +339,7 @@ def _dp_fake_solve(W, H, bits, args):
     return q, s, None, W_dq, H.diagonal(dim1=-2, dim2=-1).sum(-1)
 
 
-def _run_dp(rank, world, port, out_dir):
+def _run_dp(rank, world, port, out_dir, setattr_=setattr):
     import sys
 
     import torch.distributed as dist
@@ -349,10 +349,10 @@ def _run_dp(rank, world, port, out_dir):
 
     from mlx_gptq_b200 import capture, pipeline
 
-    install_fakes(pipeline, capture)
-    pipeline._solve_batch = _dp_fake_solve
-    capture.CaptureManager.expert_hessians = _dp_expert_hessians
-    capture.Stash.hessian = _dp_stash_hessian
+    install_fakes(pipeline, capture, setattr_)
+    setattr_(pipeline, "_solve_batch", _dp_fake_solve)
+    setattr_(capture.CaptureManager, "expert_hessians", _dp_expert_hessians)
+    setattr_(capture.Stash, "hessian", _dp_stash_hessian)
     group = None
     if world > 1:
         dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
@@ -367,14 +367,14 @@ def _run_dp(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
-def test_dp_windows_stack_matches_single_process(tmp_path):
+def test_dp_windows_stack_matches_single_process(tmp_path, monkeypatch):
     """Each rank forwards half the windows; summed Hessians and token counts give the
     single-process artifacts and, across the two ranks, the same hidden states."""
     import socket
 
     import torch.multiprocessing as mp
 
-    _run_dp(0, 1, 0, str(tmp_path))
+    _run_dp(0, 1, 0, str(tmp_path), monkeypatch.setattr)
     with socket.socket() as sk:
         sk.bind(("127.0.0.1", 0))
         port = sk.getsockname()[1]
