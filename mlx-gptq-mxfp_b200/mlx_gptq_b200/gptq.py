@@ -36,6 +36,9 @@ def _not_pd_error(H: torch.Tensor, failed: torch.Tensor, B: int) -> RuntimeError
 
 
 @torch.no_grad()
+_FACTOR_BLOCK = 64  # column block of gq_prepare_hinv
+
+
 def _prepare_hinv(H: torch.Tensor, damp: float, max_attempts: int = 6) -> torch.Tensor:
     """gptq.py:27-66: upper Cholesky factor of (H + damp*mean(diag)*I)^-1, batched,
     damping escalated x10 for failing items (6 attempts)."""
@@ -44,11 +47,22 @@ def _prepare_hinv(H: torch.Tensor, damp: float, max_attempts: int = 6) -> torch.
     B, C, _ = H.shape
     dev = L.require_cuda(H)
     Hc = L.aligned(H.float())
-    U = torch.empty(B, C, C, dtype=torch.float32, device=dev)
+    Hf = Hc
+    if C % _FACTOR_BLOCK:
+        # The factorization works on 64-column blocks: embed H in a block-diagonal matrix
+        # whose extra diagonal is mean(diag H), so the damping mean (and lambda) is that
+        # of H and the upper factor of the inverse is block-diagonal, U = U'[:C, :C].
+        Cp = -(-C // _FACTOR_BLOCK) * _FACTOR_BLOCK
+        Hf = torch.zeros(B, Cp, Cp, dtype=torch.float32, device=dev)
+        Hf[:, :C, :C] = Hc
+        m = Hc.diagonal(dim1=-2, dim2=-1).mean(-1)
+        Hf[:, C:, C:].diagonal(dim1=-2, dim2=-1).copy_(m.unsqueeze(-1).expand(B, Cp - C))
+    Cf = Hf.shape[-1]
+    U = torch.empty(B, Cf, Cf, dtype=torch.float32, device=dev)
     info = torch.empty(B, dtype=torch.int32, device=dev)
     used = torch.empty(B, dtype=torch.float32, device=dev)
-    ws = torch.empty(L.lib().gq_prepare_hinv_workspace_size(B, C), dtype=torch.uint8, device=dev)
-    st = L.lib().gq_prepare_hinv(L.ptr(Hc), B, C, float(damp), L.ptr(U), L.ptr(info), L.ptr(used),
+    ws = torch.empty(L.lib().gq_prepare_hinv_workspace_size(B, Cf), dtype=torch.uint8, device=dev)
+    st = L.lib().gq_prepare_hinv(L.ptr(Hf), B, Cf, float(damp), L.ptr(U), L.ptr(info), L.ptr(used),
                                  L.ptr(ws), ws.numel(), L.stream_ptr(dev))
     if st == L.GQ_ERR_NOT_PD:
         raise _not_pd_error(Hc, info != 0, B)
@@ -56,7 +70,7 @@ def _prepare_hinv(H: torch.Tensor, damp: float, max_attempts: int = 6) -> torch.
     esc = used > damp
     if bool(esc.any()):
         log.warning("cholesky failed for %d/%d matrices, damp -> %.3g", int(esc.sum()), B, float(used.max()))
-    return U
+    return U if Cf == C else U[:, :C, :C].contiguous()
 
 
 def _dead_columns(H: torch.Tensor) -> torch.Tensor:

@@ -235,3 +235,17 @@ def test_rtn_grid_identity_on_oracle_random():
     oq, os_, ob, odq = ogrid.rtn_quantize(W, 4, 64)
     np.testing.assert_array_equal(q.cpu().numpy(), oq)
     np.testing.assert_array_equal(dq.cpu().numpy(), odq)
+
+
+@pytest.mark.parametrize("C", [96, 160])
+def test_affine_columns_not_a_multiple_of_64(C):
+    """group 32 allows C = 32 * odd (the reference takes any C the group divides): the
+    factor is padded to 64-column blocks; codes agree with the oracle like C % 64 == 0."""
+    from mlx_gptq_b200 import solve_gptq
+    from oracle import gptq as og
+
+    W, H = _correlated(2, 16, C, 2048, seed=C)
+    q, s, b, Wdq, rel = solve_gptq(_cuda(W), _cuda(H), 4, 32, mode="affine")
+    oq, os_, ob, oWdq, orel = og.solve_gptq(W, H.copy(), 4, 32, mode="affine")
+    assert (q.cpu().numpy() == oq).mean() >= 0.999
+    np.testing.assert_allclose(rel.cpu().numpy(), orel, rtol=1e-3)
