@@ -35,10 +35,10 @@ def _not_pd_error(H: torch.Tensor, failed: torch.Tensor, B: int) -> RuntimeError
     )
 
 
-@torch.no_grad()
 _FACTOR_BLOCK = 64  # column block of gq_prepare_hinv
 
 
+@torch.no_grad()
 def _prepare_hinv(H: torch.Tensor, damp: float, max_attempts: int = 6) -> torch.Tensor:
     """gptq.py:27-66: upper Cholesky factor of (H + damp*mean(diag)*I)^-1, batched,
     damping escalated x10 for failing items (6 attempts)."""
