@@ -148,3 +148,22 @@ def test_mxfp_range_guard(golden):
     assert np.isfinite(Wdq).all()
     assert np.abs(Wdq).max() <= np.abs(W).max() * 32.0
     assert int(s.max()) < 250
+
+
+def test_block_diagonal_padding_keeps_the_factor():
+    """The identity behind padding the affine factor to 64-column blocks: H embedded
+    block-diagonally with mean(diag H) on the extra diagonal has the same damping and
+    an inverse factor whose leading C x C block is U (gptq.py:27-66 restated)."""
+    from oracle.gptq import prepare_hinv
+
+    rng = np.random.default_rng(5)
+    C, Cp = 96, 128
+    X = rng.standard_normal((512, C)).astype(np.float32)
+    H = (X.T @ X)[None].astype(np.float32)
+    U, *_ = prepare_hinv(H.copy(), 0.01)
+    Hp = np.zeros((1, Cp, Cp), np.float32)
+    Hp[0, :C, :C] = H[0]
+    Hp[0, np.arange(C, Cp), np.arange(C, Cp)] = np.diagonal(H[0]).mean()
+    Up, *_ = prepare_hinv(Hp, 0.01)
+    np.testing.assert_allclose(Up[0, :C, :C], U[0], rtol=2e-4, atol=1e-6)
+    assert np.abs(Up[0, :C, C:]).max() == 0.0
