@@ -199,9 +199,10 @@ class SegmentStore:
     grow by doubling otherwise; the forward writes its activations straight into
     them."""
 
-    def __init__(self, num_experts: int, reserve_tokens: int | None = None):
+    def __init__(self, num_experts: int, reserve_tokens: int | None = None, device=None):
         self.E = num_experts
         self.reserve = reserve_tokens
+        self.device = None if device is None else torch.device(device)  # None: where the rows are produced
         self.inputs = self.acts = self.tok = None
         self.n_tok = self.n_slot = 0
         self.batch_counts: list[list[int]] = []
@@ -222,8 +223,11 @@ class SegmentStore:
         """Slots per layer expected from the reservation (tokens x slots per token)."""
         return None if self.reserve is None else self.reserve * max(1, -(-slots // max(1, tokens)))
 
-    def acts_out(self, slots: int, tokens: int, inter: int, dtype, device) -> torch.Tensor:
-        """Where the forward should write this batch's activation rows."""
+    def acts_out(self, slots: int, tokens: int, inter: int, dtype, device) -> torch.Tensor | None:
+        """Where the forward should write this batch's activation rows (None when the
+        store keeps its rows on another device: add() copies them there)."""
+        if self.device is not None and torch.device(device) != self.device:
+            return None
         self.acts = self._grow(self.acts, self.n_slot, self.n_slot + slots, (inter,), dtype, device,
                                self._slot_hint(slots, tokens))
         self._pending = self.acts[self.n_slot:self.n_slot + slots]
@@ -231,7 +235,7 @@ class SegmentStore:
 
     def add(self, hidden: torch.Tensor, tok: torch.Tensor, counts, acts: torch.Tensor):
         T, S = hidden.shape[0], tok.shape[0]
-        dev = hidden.device
+        dev = hidden.device if self.device is None else self.device
         self.inputs = self._grow(self.inputs, self.n_tok, self.n_tok + T, hidden.shape[1:], hidden.dtype, dev,
                                  self.reserve)
         self.inputs[self.n_tok:self.n_tok + T].copy_(hidden)
@@ -360,7 +364,7 @@ class CaptureManager:
     def _make_segment_sink(self, module_name: str):
         tasks = [t for t in self.fused_tasks if t.module_name == module_name]
         E = tasks[0].num_experts
-        store = self._segments.setdefault(module_name, SegmentStore(E, self.reserve_tokens))
+        store = self._segments.setdefault(module_name, SegmentStore(E, self.reserve_tokens, self.stash_device))
 
         def sink(hidden, tok, counts, acts):
             store.add(hidden.detach(), tok, counts, acts)
@@ -510,9 +514,9 @@ class CaptureManager:
         pos = torch.full((st.E,), len(experts), dtype=torch.int64, device=device)
         pos[torch.tensor(experts, dtype=torch.int64, device=device)] = torch.arange(len(experts), device=device)
         order = torch.argsort(pos[se] * S + torch.arange(S, device=device))[:sum(counts)]
-        if task.param_name == "down_proj":
-            return st.acts[:S], order.to(torch.int32), counts
-        return st.inputs[:st.n_tok], st.tok[:S][order], counts
+        if task.param_name == "down_proj":  # rows kept on another device move once, here
+            return st.acts[:S].to(device), order.to(torch.int32), counts
+        return st.inputs[:st.n_tok].to(device), st.tok[:S].to(device)[order], counts
 
     @torch.no_grad()
     def expert_rows(self, task: FusedExpertTask, expert: int, device) -> torch.Tensor:

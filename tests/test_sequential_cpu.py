@@ -419,3 +419,14 @@ def test_segment_store_grows_without_a_reservation():
     assert torch.equal(st.tok[:st.n_slot].long(), torch.cat(ref_tok))
     assert torch.equal(st.slot_experts("cpu"), torch.cat([torch.tensor([0] * T + [2] * T) for T in (5, 9, 17)]))
     assert st.nbytes() > 0
+
+
+def test_segment_store_keeps_rows_on_the_stash_device():
+    """A store pinned to another device than the forward's declines to lend its buffer
+    (the forward keeps its own activations) and receives copies."""
+    from mlx_gptq_b200.capture import SegmentStore
+
+    st = SegmentStore(num_experts=2, device="meta")
+    assert st.acts_out(4, 2, 3, torch.float32, "cpu") is None
+    st2 = SegmentStore(num_experts=2, device="cpu")
+    assert st2.acts_out(4, 2, 3, torch.float32, "cpu") is not None
