@@ -146,3 +146,45 @@ def test_cli_runs_and_resumes_on_cpu(tmp_path, monkeypatch):
     with pytest.raises(ValueError, match="exceed vocabulary"):
         calibrate.main(["--model", model_dir, "--output", str(tmp_path / "o2"), "--calibration-tokens", str(bad),
                         "--devices", "cpu"])
+
+
+def _write_tokenizer(model_dir, vocab_size=300):
+    """A word-level tokenizer (w2 .. w{n-1}, [UNK] = 0, </s> = 1) saved the Hugging Face way."""
+    from tokenizers import Tokenizer, models, pre_tokenizers
+
+    vocab = {"[UNK]": 0, "</s>": 1, **{f"w{i}": i for i in range(2, vocab_size)}}
+    tok = Tokenizer(models.WordLevel(vocab=vocab, unk_token="[UNK]"))
+    tok.pre_tokenizer = pre_tokenizers.Whitespace()
+    tok.save(os.path.join(model_dir, "tokenizer.json"))
+    with open(os.path.join(model_dir, "tokenizer_config.json"), "w") as f:
+        json.dump({"tokenizer_class": "PreTrainedTokenizerFast", "eos_token": "</s>", "unk_token": "[UNK]"}, f)
+
+
+def test_cli_dataset_path_with_the_model_tokenizer(tmp_path, monkeypatch):
+    """--dataset: documents tokenized by the model's own tokenizer, joined with EOS and cut
+    into windows (data.py:load_calibration), saved as calib_tokens.npy and hashed into the
+    manifest; token ids are checked against the tokenizer's vocabulary."""
+    import test_pipeline_cpu as fakes
+
+    from mlx_gptq_b200 import artifacts, capture, grid, pipeline
+
+    fakes.install_fakes(pipeline, capture, monkeypatch.setattr)
+    for mod, name, fn in ((artifacts, "pack_nibbles", fakes._fake_pack), (artifacts, "unpack_nibbles", fakes._fake_unpack),
+                          (grid, "dequantize_artifact", fakes._fake_dequant)):
+        monkeypatch.setattr(mod, name, fn)
+    model_dir = write_tiny_checkpoint(str(tmp_path / "model"))
+    _write_tokenizer(model_dir)
+    text = tmp_path / "corpus.txt"
+    rng = np.random.default_rng(0)
+    text.write_text(" ".join(f"w{i}" for i in rng.integers(2, 300, 4000)))
+    out = str(tmp_path / "out")
+    calibrate.main(["--model", model_dir, "--output", out, "--dataset", str(text), "--nsamples", "4",
+                    "--seqlen", "32", "--mode", "mxfp4", "--devices", "cpu", "--batch-size", "2", "--seed", "3"])
+    toks = np.load(os.path.join(out, "calib_tokens.npy"))
+    assert toks.shape == (4, 32) and toks.min() >= 1 and toks.max() < 300
+    man = json.load(open(os.path.join(out, "manifest.json")))
+    assert man["dataset"] == str(text) and man["nsamples"] == 4 and man["layers_done"] == [0, 1]
+    import hashlib
+
+    assert man["calibration_tokens_sha256"] == hashlib.sha256(open(os.path.join(out, "calib_tokens.npy"),
+                                                                   "rb").read()).hexdigest()
