@@ -188,3 +188,46 @@ def test_cli_dataset_path_with_the_model_tokenizer(tmp_path, monkeypatch):
 
     assert man["calibration_tokens_sha256"] == hashlib.sha256(open(os.path.join(out, "calib_tokens.npy"),
                                                                    "rb").read()).hexdigest()
+
+
+def test_validate_artifacts_report(tmp_path, monkeypatch):
+    """validate_artifacts.py:21-76: a clean run verifies; a corrupted scale (range blow-up),
+    a tensor missing from the checkpoint and a shape mismatch are reported as failures."""
+    import safetensors.torch as st
+
+    import test_pipeline_cpu as fakes
+
+    from mlx_gptq_b200 import artifacts, capture, grid, pipeline, validate
+
+    fakes.install_fakes(pipeline, capture, monkeypatch.setattr)
+    for mod, name, fn in ((artifacts, "pack_nibbles", fakes._fake_pack), (artifacts, "unpack_nibbles", fakes._fake_unpack),
+                          (grid, "dequantize_artifact", fakes._fake_dequant),
+                          (validate, "dequantize_artifact", fakes._fake_dequant)):
+        monkeypatch.setattr(mod, name, fn)
+    model_dir = write_tiny_checkpoint(str(tmp_path / "model"))
+    toks = tmp_path / "t.npy"
+    np.save(toks, np.random.default_rng(1).integers(0, 512, (4, 32)).astype(np.int64))
+    out = str(tmp_path / "out")
+    calibrate.main(["--model", model_dir, "--output", out, "--calibration-tokens", str(toks), "--mode", "mxfp4",
+                    "--devices", "cpu", "--batch-size", "2"])
+    # the fake dequantization is 0.03 * code: scale the source so that is within range
+    src = st.load_file(f"{model_dir}/model.safetensors")
+    src = {k: (v.float() * 100).to(torch.bfloat16) for k, v in src.items()}
+    st.save_file(src, f"{model_dir}/model.safetensors")
+    r = validate.validate(model_dir, out, device="cpu")
+    assert r["status"] == "verified" and r["tensors"] == 2 * (4 + 3 * 8) and not r["failures"]
+    assert len(r["worst"]) == 20 and r["worst"][0]["ratio"] >= r["worst"][-1]["ratio"]
+
+    name = "model.layers.0.self_attn.q_proj.weight"  # artifact far outside its source's range
+    src[name] = (src[name].float() * 1e-4).to(torch.bfloat16)
+    del src["model.layers.1.self_attn.k_proj.weight"]
+    src["model.layers.1.self_attn.v_proj.weight"] = src["model.layers.1.self_attn.v_proj.weight"][:, :32].contiguous()
+    st.save_file(src, f"{model_dir}/model.safetensors")
+    r = validate.validate(model_dir, out, device="cpu")
+    errors = {f["name"]: f["error"] for f in r["failures"]}
+    assert r["status"] == "failed"
+    assert errors[name].startswith("group range ratio")
+    assert errors["model.layers.1.self_attn.k_proj.weight"] == "missing source tensor"
+    assert errors["model.layers.1.self_attn.v_proj.weight"].startswith("shape")
+    assert validate.main(["--model", model_dir, "--calib", out, "--device", "cpu",
+                          "--output", str(tmp_path / "report.json")]) == 1
