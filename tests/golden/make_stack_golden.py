@@ -2,7 +2,11 @@
 
 Runs mlx_gptq.sequential.Pipeline (the reference's own capture, Hessians,
 solve_gptq, artifact writer) over a tiny seeded Qwen3-MoE checkpoint and stores
-its per-tensor codes, scales, rel_err and token counts in stack_mxfp4.npz:
+its per-tensor codes, scales, rel_err and token counts in stack_mxfp4.npz; then runs
+the reference's Stage B streaming packer (mlx_gptq/stream_pack.py) on those
+artifacts, as they are and without one stacked projection's artifacts (RTN fallback), and
+stores a summary of each MLX output (dtype, shape and sha256 of every tensor, the
+index's weight map, the config's quantization entry):
 
     python tests/golden/make_stack_golden.py [--ref PATH_TO_REFERENCE_CHECKOUT]
 
@@ -16,6 +20,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import shutil
 import sys
 import tempfile
 import types
@@ -69,6 +74,37 @@ def windows() -> np.ndarray:
                                                         (N_WINDOWS, SEQLEN)).astype(np.int64)
 
 
+def _json_bytes(obj) -> np.ndarray:
+    return np.frombuffer(json.dumps(obj, sort_keys=True).encode(), dtype=np.uint8)
+
+
+def packed_summary(mlx_dir: str) -> dict:
+    """Every tensor of an MLX output directory as [dtype, shape, sha256 of its bytes], plus
+    its index's weight map (file per key) and the quantization entry of its config."""
+    import hashlib
+
+    from safetensors import safe_open
+
+    tensors = {}
+    index = json.load(open(os.path.join(mlx_dir, "model.safetensors.index.json")))
+    for fname in sorted(set(index["weight_map"].values())):
+        with safe_open(os.path.join(mlx_dir, fname), framework="pt") as f:
+            for k in f.keys():
+                t = f.get_tensor(k).contiguous()
+                raw = t.view(torch.uint8).numpy().tobytes() if t.numel() else b""
+                tensors[k] = [str(t.dtype), list(t.shape), hashlib.sha256(raw).hexdigest()]
+    cfg = json.load(open(os.path.join(mlx_dir, "config.json")))
+    return {"tensors": tensors, "weight_map": index["weight_map"], "quantization": cfg["quantization"]}
+
+
+def run_reference_packer(model_dir: str, calib: str, mlx_dir: str) -> dict:
+    from mlx_gptq.stream_pack import StreamingPacker
+
+    StreamingPacker(model_dir, calib, mlx_dir, "mxfp4", 4, 32,
+                    r"(^|\.)(gate|router)$|shared_expert_gate|e_score|(^|\.)ple($|\.)").run()
+    return packed_summary(mlx_dir)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("GQ_REFERENCE"),
@@ -99,6 +135,19 @@ def main():
             Pipeline(model, RawShardIndex(model_dir), args).run(torch.from_numpy(windows()), writer)
         reader = ArtifactReader(out)
         fx, meta = {}, {}
+        fx["packed"] = _json_bytes(run_reference_packer(model_dir, out, os.path.join(tmp, "mlx")))
+        # the same without layer 1's down_proj artifacts: that stacked switch_mlp tensor
+        # falls back to RTN (the packer requires every remaining artifact to be used)
+        drop = [n for n in reader.tensors if n.startswith("model.layers.1.mlp.experts.") and
+                n.endswith(".down_proj.weight")]
+        out_rtn = os.path.join(tmp, "out_rtn")
+        shutil.copytree(out, out_rtn)
+        man = json.load(open(os.path.join(out_rtn, "manifest.json")))
+        for n in drop:
+            del man["tensors"][n]
+        json.dump(man, open(os.path.join(out_rtn, "manifest.json"), "w"))
+        fx["packed_rtn"] = _json_bytes(run_reference_packer(model_dir, out_rtn, os.path.join(tmp, "mlx_rtn")))
+        fx["packed_rtn_dropped"] = _json_bytes(sorted(drop))
         for name, info in sorted(reader.tensors.items()):
             q, s, b, info = reader.get(name)
             fx[f"q:{name}"] = q.numpy().astype(np.uint8)
