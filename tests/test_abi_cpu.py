@@ -86,3 +86,30 @@ def test_cpu_tensors_are_rejected_not_computed():
     H = torch.eye(64).unsqueeze(0)
     with pytest.raises(RuntimeError, match="CUDA"):
         solve_gptq(W, H, bits=4, group_size=32)
+
+
+def test_hessian_tile_schedule_queries(lib, monkeypatch):
+    """Host-only queries of the Hessian tile schedule: 256x256 tiles on or above the
+    diagonal for the CTA-pair kernel (one per pair in a wave), 128x256 ones for the
+    one-CTA kernel (one per CTA)."""
+    for c in (64, 1088, 2048, 4096, 11008):
+        t = -(-c // 256)
+        monkeypatch.setenv("GQ_HESSIAN_KERNEL", "2sm")
+        assert lib.gq_hessian_tile_count(c) == t * (t + 1) // 2
+        assert lib.gq_hessian_concurrent_tiles(148) == 74
+        monkeypatch.setenv("GQ_HESSIAN_KERNEL", "1sm")
+        mt = -(-c // 128)
+        assert lib.gq_hessian_tile_count(c) == sum(min(2 * tn + 2, mt) for tn in range(t))
+        assert lib.gq_hessian_concurrent_tiles(148) == 148
+    assert lib.gq_hessian_tile_count(0) == 0 and lib.gq_hessian_concurrent_tiles(0) == 0
+    # the range form validates its range before touching the device
+    import ctypes
+
+    import numpy as np
+
+    monkeypatch.setenv("GQ_HESSIAN_KERNEL", "2sm")
+    h = np.zeros(64, np.float32)
+    assert h.ctypes.data % 16 == 0
+    st = lib.gq_hessian_bf16_range(None, 0, 4, 8, h.ctypes.data, 4, 1.0, 0.0, 0, 5, None, None)
+    assert st == 1 and b"tile range" in lib.gq_last_error()  # GQ_ERR_ARG before any launch
+    assert lib.gq_hessian_bf16_range(None, 0, 4, 8, h.ctypes.data, 4, 1.0, 0.0, 1, 1, None, None) == 0  # empty
