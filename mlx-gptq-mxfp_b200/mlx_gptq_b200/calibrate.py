@@ -83,6 +83,10 @@ def build_parser() -> argparse.ArgumentParser:
     ap.add_argument("--seed", type=int, default=17)
     ap.add_argument("--experts-forward", default="grouped", choices=("grouped", "eager"),
                     help="sort-based expert forward (bit-identical to the eager loop) or the eager loop")
+    ap.add_argument("--dp-windows", action="store_true",
+                    help="with several processes: each forwards its share of the windows and Hessians are "
+                         "summed over processes (the forward scales; results match one process within the "
+                         "Hessian tolerance instead of bit for bit)")
     return ap
 
 
@@ -118,7 +122,7 @@ def resolve_args(ap: argparse.ArgumentParser, argv=None):
         args.vram_gb = parse_vram_budgets(args.vram_gb, args.devices)
     except ValueError as exc:
         ap.error(str(exc))
-    if local >= 0:  # one process per GPU under torchrun
+    if local >= 0 and args.devices[0].startswith("cuda"):  # one process per GPU under torchrun
         dev = f"cuda:{local}"
         args.vram_gb = {dev: args.vram_gb.get(dev, next(iter(args.vram_gb.values())))}
         args.devices = [dev]
@@ -207,8 +211,11 @@ def main(argv=None):
         import torch.distributed as dist
 
         dev = torch.device(args.devices[0])
-        torch.cuda.set_device(dev)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=1800), device_id=dev)
+        if dev.type == "cuda":
+            torch.cuda.set_device(dev)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=1800), device_id=dev)
+        else:  # host-only runs (tests): gloo
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
         group, rank = dist.group.WORLD, dist.get_rank()
     log.info("device %s (rank %d), expert-solve VRAM budget %s GiB", args.devices[0], rank, args.vram_gb)
 
@@ -253,7 +260,7 @@ def main(argv=None):
               "artifact_layers_prefix": args.artifact_layers_prefix}
     writer = ArtifactWriter(args.output, header) if rank == 0 else _ReadOnlyWriter(args.output)
     reader = ArtifactReader(args.output) if writer.manifest["layers_done"] else None
-    pipe = Pipeline(model, RawShardIndex(args.model), args, group=group)
+    pipe = Pipeline(model, RawShardIndex(args.model), args, group=group, dp=args.dp_windows)
     with torch.no_grad():
         pipe.run(samples, writer, reader_for_resume=reader)
     if group is not None:

@@ -231,3 +231,61 @@ def test_validate_artifacts_report(tmp_path, monkeypatch):
     assert errors["model.layers.1.self_attn.v_proj.weight"].startswith("shape")
     assert validate.main(["--model", model_dir, "--calib", out, "--device", "cpu",
                           "--output", str(tmp_path / "report.json")]) == 1
+
+
+def _cli_rank(rank, world, port, out_dir, model_dir, toks, dp):
+    import os
+    import sys
+
+    sys.path.insert(0, os.path.dirname(__file__))
+    import test_pipeline_cpu as fakes
+
+    from mlx_gptq_b200 import artifacts, capture, grid, pipeline
+
+    fakes.install_fakes(pipeline, capture)
+    artifacts.pack_nibbles, artifacts.unpack_nibbles = fakes._fake_pack, fakes._fake_unpack
+    grid.dequantize_artifact = fakes._fake_dequant
+    os.environ.update(RANK=str(rank), LOCAL_RANK=str(rank), WORLD_SIZE=str(world), MASTER_ADDR="127.0.0.1",
+                      MASTER_PORT=str(port))
+    argv = ["--model", model_dir, "--output", out_dir, "--calibration-tokens", toks, "--mode", "mxfp4",
+            "--devices", "cpu", "--batch-size", "2"] + (["--dp-windows"] if dp else [])
+    calibrate.main(argv)
+
+
+@pytest.mark.parametrize("dp", [False, True])
+def test_cli_two_processes(tmp_path, dp):
+    """The command line under two gloo processes writes one artifact set: identical to one
+    process by default; with --dp-windows the same names and layer-0 token counts summed
+    over the processes."""
+    import socket
+
+    import torch.multiprocessing as mp
+
+    model_dir = write_tiny_checkpoint(str(tmp_path / "model"))
+    toks = str(tmp_path / "t.npy")
+    np.save(toks, np.random.default_rng(1).integers(0, 512, (4, 32)).astype(np.int64))
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    out2 = str(tmp_path / "out2")
+    mp.start_processes(_cli_rank, args=(2, port, out2, model_dir, toks, dp), nprocs=2, start_method="spawn")
+    # one process, same fakes, in a fresh child (the fakes stay out of this test process)
+    out1 = str(tmp_path / "out1")
+    mp.start_processes(_cli_rank, args=(1, port + 1, out1, model_dir, toks, False), nprocs=1,
+                       start_method="spawn")
+    m1 = json.load(open(os.path.join(out1, "manifest.json")))
+    m2 = json.load(open(os.path.join(out2, "manifest.json")))
+    assert m1["layers_done"] == m2["layers_done"] == [0, 1]
+    assert sorted(m1["tensors"]) == sorted(m2["tensors"])
+    # with --dp-windows layer 0's counts are sums over the processes; later layers see
+    # weights solved from these stand-in Hessians, which are not sums over processes
+    layers = ("model.layers.0.",) if dp else ("model.layers.",)
+    assert ({k: v["tokens"] for k, v in m1["tensors"].items() if k.startswith(layers)}
+            == {k: v["tokens"] for k, v in m2["tensors"].items() if k.startswith(layers)})
+    if not dp:
+        import safetensors.torch as st
+
+        for li in (0, 1):
+            a = st.load_file(os.path.join(out1, f"layer_{li:04d}.safetensors"))
+            b = st.load_file(os.path.join(out2, f"layer_{li:04d}.safetensors"))
+            assert a.keys() == b.keys() and all(torch.equal(a[k], b[k]) for k in a)
