@@ -441,8 +441,8 @@ class Pipeline:
             world = dist.get_world_size(self.group)
             if samples.shape[0] < world:
                 raise ValueError(f"dp needs at least one calibration window per rank ({samples.shape[0]} < {world})")
-            per = -(-samples.shape[0] // world)
-            samples = samples[self.rank * per:(self.rank + 1) * per]
+            n = samples.shape[0]  # balanced contiguous shares: every rank gets >= 1 window
+            samples = samples[self.rank * n // world:(self.rank + 1) * n // world]
         batches = self.catch_layer0_inputs(samples, self.args.batch_size)
         log.info("caught %d forward batches for layer 0", len(batches))
         n_layers = len(self.layers) if layers is None else min(int(layers), len(self.layers))
