@@ -10,8 +10,7 @@ Several GPUs are several processes (one per GPU):
 Differences from the reference, all on the device side: one process per GPU
 instead of one thread per entry of --devices (under torchrun the process's GPU is
 LOCAL_RANK; without it the first --devices entry); Hugging Face dataset sources
-(hf:, hfchat:) need a network and are refused; --lazy-ple (Gemma-4 per-layer
-embeddings) and Flint models are not supported.
+(hf:, hfchat:) need a network and are refused; Flint models are not supported.
 """
 
 from __future__ import annotations
@@ -77,7 +76,8 @@ def build_parser() -> argparse.ArgumentParser:
     ap.add_argument("--checkpoint-model-prefix", default=None)
     ap.add_argument("--artifact-layers-prefix", default=None)
     ap.add_argument("--exclude", default=DEFAULT_EXCLUDE, help="regex of layer-relative names to leave unquantized")
-    ap.add_argument("--lazy-ple", action="store_true", help="not supported here")
+    ap.add_argument("--lazy-ple", action="store_true",
+                    help="read per-layer embedding rows from the source shards instead of materializing them")
     ap.add_argument("--override", action="append", metavar="REGEX=BITS", help="per-tensor bit override")
     ap.add_argument("--trust-remote-code", action="store_true")
     ap.add_argument("--seed", type=int, default=17)
@@ -109,8 +109,6 @@ def resolve_args(ap: argparse.ArgumentParser, argv=None):
         args.mxfp_algorithm = "none"
     if args.dataset is None and args.calibration_tokens is None:
         ap.error("one of --dataset or --calibration-tokens is required")
-    if args.lazy_ple:
-        ap.error("--lazy-ple is not supported by this build")
     local = int(os.environ.get("LOCAL_RANK", "-1"))
     if args.devices:
         args.devices = [d.strip() for d in args.devices.split(",")]

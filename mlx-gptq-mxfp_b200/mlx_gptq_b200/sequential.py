@@ -205,6 +205,53 @@ def free_module(module: torch.nn.Module):
     module.to_empty(device="meta")
 
 
+class LazyShardedEmbedding(torch.nn.Module):
+    """An embedding table stored as row shards in the checkpoint, read row by row on
+    demand instead of materialized (sequential.py:153-190, Gemma-4 per-layer embeddings):
+    each forward reads only the distinct rows its ids select, once, then places them on
+    the device."""
+
+    def __init__(self, prefix: str, shards, n_shards: int, rows_per_shard: int, dim: int, device, dtype):
+        super().__init__()
+        self.prefix = prefix
+        self.shards = shards
+        self.n_shards = n_shards
+        self.rows_per_shard = rows_per_shard
+        self.dim = dim
+        self.device = torch.device(device)
+        self.dtype = dtype
+        self.weight = torch.empty(0, device=device, dtype=dtype)  # callers check its device
+
+    def forward(self, ids: torch.Tensor) -> torch.Tensor:
+        flat = ids.detach().reshape(-1).to("cpu", torch.long)
+        uniq, inverse = torch.unique(flat, return_inverse=True)
+        rows = torch.empty(uniq.numel(), self.dim, dtype=self.dtype)
+        shard_of = uniq // self.rows_per_shard
+        for shard in torch.unique(shard_of).tolist():
+            sel = (shard_of == shard).nonzero().flatten()
+            local = (uniq[sel] % self.rows_per_shard).tolist()
+            rows[sel] = self.shards.get_rows(f"{self.prefix}.shard_{shard}.weight", local).to(self.dtype)
+        return rows.to(self.device)[inverse.to(self.device)].reshape(*ids.shape, self.dim)
+
+
+def install_lazy_ple(module: torch.nn.Module, prefix: str, shards, device, dtype):
+    """Replace every fused per-layer embedding table (`...ple.ple_embedding.ngram_embedding`)
+    under `module` by a LazyShardedEmbedding over its checkpoint shards (sequential.py:193-229)."""
+    for name, child in list(module.named_modules()):
+        if not name.endswith("ple.ple_embedding.ngram_embedding"):
+            continue
+        parent_name, attr = name.rsplit(".", 1)
+        total_rows, dim = child.weight.shape
+        shard_names = shards.names_with_prefix(f"{prefix}.{name}.shard_")
+        if not shard_names:
+            raise KeyError(f"no PLE shards found for {prefix}.{name}")
+        n = len(shard_names)
+        if total_rows % n:
+            raise ValueError(f"PLE rows {total_rows} are not divisible by {n} shards")
+        setattr(module.get_submodule(parent_name), attr,
+                LazyShardedEmbedding(f"{prefix}.{name}", shards, n, total_rows // n, dim, device, dtype))
+
+
 # ---------------------------------------------------------------------------
 # layer-0 inputs and per-layer call contexts
 # ---------------------------------------------------------------------------
@@ -450,6 +497,8 @@ class Pipeline:
             layer = self.layers[li]
             prefix = self.checkpoint_layers_prefix_fmt.format(li)
             t0 = time.time()
+            if getattr(self.args, "lazy_ple", False):
+                install_lazy_ple(layer, prefix, self.shards, self.dev0, self.dtype)
             materialize_module(layer, prefix, self.shards, self.dev0, self.dtype)
             if writer is not None and writer.layer_done(li):
                 self.apply_precomputed(layer, li, reader_for_resume)

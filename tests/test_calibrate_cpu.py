@@ -48,8 +48,9 @@ def test_mode_rules():
     assert (a.group_size, a.bits, a.mxfp_algorithm) == (64, 4, "none")
     assert a.overrides[0][0].search("mlp.down_proj.weight") and a.overrides[0][1] == 8
     assert a.vram_gb == {"cpu": 16.0}
+    assert _resolve(base + ["--lazy-ple"]).lazy_ple
     for bad in (["--mode", "mxfp4", "--bits", "8"], ["--mode", "mxfp8", "--group-size", "64"],
-                ["--mode", "mxfp4", "--override", "x=8"], ["--lazy-ple"]):
+                ["--mode", "mxfp4", "--override", "x=8"]):
         with pytest.raises(SystemExit):
             _resolve(base + bad)
     with pytest.raises(SystemExit):

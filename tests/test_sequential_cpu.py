@@ -430,3 +430,46 @@ def test_segment_store_keeps_rows_on_the_stash_device():
     assert st.acts_out(4, 2, 3, torch.float32, "cpu") is None
     st2 = SegmentStore(num_experts=2, device="cpu")
     assert st2.acts_out(4, 2, 3, torch.float32, "cpu") is not None
+
+
+def _ple_checkpoint(tmp_path):
+    from safetensors.torch import save_file
+
+    shard_0 = torch.arange(12, dtype=torch.float32).reshape(4, 3)
+    shard_1 = shard_0 + 100
+    name = "layer.ple.ple_embedding.ngram_embedding.shard_{i}.weight"
+    save_file({name.format(i=0): shard_0, name.format(i=1): shard_1}, str(tmp_path / "model.safetensors"))
+    wm = {name.format(i=i): "model.safetensors" for i in range(2)}
+    (tmp_path / "model.safetensors.index.json").write_text(__import__("json").dumps({"weight_map": wm}))
+    return sequential.RawShardIndex(str(tmp_path)), torch.cat([shard_0, shard_1])
+
+
+def test_lazy_sharded_embedding_reads_selected_rows(tmp_path):
+    """tests/test_lazy_ple.py: rows come from the shard that holds them, repeats included."""
+    index, table = _ple_checkpoint(tmp_path)
+    emb = sequential.LazyShardedEmbedding("layer.ple.ple_embedding.ngram_embedding", index, 2, 4, 3,
+                                          torch.device("cpu"), torch.float32)
+    ids = torch.tensor([[0, 4, 7], [5, 1, 3], [7, 7, 0]])
+    assert torch.equal(emb(ids), table[ids.reshape(-1)].reshape(3, 3, 3))
+
+
+def test_install_lazy_ple_replaces_the_fused_table(tmp_path):
+    index, table = _ple_checkpoint(tmp_path)
+
+    class Ple(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.ple_embedding = torch.nn.Module()
+            self.ple_embedding.ngram_embedding = torch.nn.Embedding(8, 3, device="meta")
+
+    layer = torch.nn.Module()
+    layer.ple = Ple()
+    sequential.install_lazy_ple(layer, "layer", index, "cpu", torch.float32)
+    emb = layer.ple.ple_embedding.ngram_embedding
+    assert isinstance(emb, sequential.LazyShardedEmbedding) and emb.n_shards == 2 and emb.rows_per_shard == 4
+    assert torch.equal(emb(torch.tensor([6, 2])), table[[6, 2]])
+    bad = torch.nn.Module()
+    bad.ple = Ple()
+    bad.ple.ple_embedding.ngram_embedding = torch.nn.Embedding(9, 3, device="meta")
+    with pytest.raises(ValueError):
+        sequential.install_lazy_ple(bad, "layer", index, "cpu", torch.float32)
