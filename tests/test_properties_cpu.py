@@ -1,0 +1,70 @@
+"""Property tests (hypothesis) of the host-side scheduling and routing logic."""
+
+import torch
+from hypothesis import given, settings
+from hypothesis import strategies as st
+
+from mlx_gptq_b200.experts import _token_ranks, route
+from mlx_gptq_b200.pipeline import _wave_parts, lpt_partition
+
+
+@st.composite
+def routings(draw):
+    T = draw(st.integers(1, 40))
+    E = draw(st.integers(1, 9))
+    k = draw(st.integers(1, min(E, 4)))
+    rows = []
+    for _ in range(T):
+        experts = draw(st.permutations(list(range(E))))[:k]
+        # occasionally a dropped slot (index E), as capacity-limited routers emit
+        rows.append([E if draw(st.integers(0, 9)) == 0 else e for e in experts])
+    return torch.tensor(rows, dtype=torch.long), E
+
+
+@settings(max_examples=200, deadline=None)
+@given(routings())
+def test_route_orders_slots_like_the_eager_loop(r):
+    idx, E = r
+    tok, pos, counts, counts_dev = route(idx, E)
+    assert counts == counts_dev.tolist() == [int((idx == e).sum()) for e in range(E)]
+    off = 0
+    for e in range(E):  # eager: torch.where over the [top_k, tokens] mask of expert e
+        j_ref, t_ref = torch.where((idx == e).T)
+        assert torch.equal(tok[off:off + counts[e]], t_ref) and torch.equal(pos[off:off + counts[e]], j_ref)
+        off += counts[e]
+    assert off == tok.numel()
+    # each token's slots ranked by ascending expert
+    ranks = _token_ranks(tok, idx.shape[0])
+    expert_of = torch.repeat_interleave(torch.arange(E), torch.tensor(counts))
+    for t in range(idx.shape[0]):
+        sel = (tok == t).nonzero().flatten()
+        order = torch.argsort(expert_of[sel])
+        assert torch.equal(ranks[sel][order], torch.arange(sel.numel()))
+
+
+@settings(max_examples=200, deadline=None)
+@given(st.lists(st.one_of(st.floats(0, 1e6, allow_nan=False), st.integers(0, 3).map(float)), max_size=60),
+       st.integers(1, 9))
+def test_lpt_partition_is_a_partition_within_the_lpt_bound(costs, parts):
+    bins = lpt_partition(costs, parts)
+    assert len(bins) == parts
+    assert sorted(i for b in bins for i in b) == list(range(len(costs)))
+    if costs:
+        loads = [sum(costs[i] for i in b) for b in bins]
+        # any list schedule (LPT included) ends by mean load + (1 - 1/m) * largest item
+        bound = sum(costs) / parts + (1.0 - 1.0 / parts) * max(costs)
+        assert max(loads) <= bound * (1 + 1e-9) + 1e-9
+    assert lpt_partition(costs, parts) == bins  # deterministic
+
+
+@settings(max_examples=300, deadline=None)
+@given(st.integers(1, 5000), st.integers(1, 200), st.integers(1, 16))
+def test_wave_parts_cover_the_tiles_in_at_most_one_wave_each(tiles, per_wave, world):
+    parts = _wave_parts(tiles, per_wave, world)
+    assert parts[0][0] == 0 and parts[-1][1] == tiles
+    assert all(a[1] == b[0] for a, b in zip(parts, parts[1:]))
+    assert all(e > b for b, e in parts) and len(parts) <= world
+    if world > 1 and -(-tiles // per_wave) <= world:
+        assert all(e - b <= per_wave for b, e in parts)
+    if world == 1:
+        assert parts == [(0, tiles)]
