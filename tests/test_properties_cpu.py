@@ -68,3 +68,51 @@ def test_wave_parts_cover_the_tiles_in_at_most_one_wave_each(tiles, per_wave, wo
         assert all(e - b <= per_wave for b, e in parts)
     if world == 1:
         assert parts == [(0, tiles)]
+
+
+@settings(max_examples=100, deadline=None)
+@given(st.lists(st.tuples(st.integers(1, 12), st.integers(1, 3)), min_size=1, max_size=6),
+       st.one_of(st.none(), st.integers(1, 30)), st.integers(1, 4))
+def test_segment_store_equals_concatenation(batches, reserve, E):
+    """Any sequence of batches, with or without a (possibly too small) reservation, leaves
+    the store equal to the concatenation of what it was given."""
+    from mlx_gptq_b200.capture import SegmentStore
+
+    g = torch.Generator().manual_seed(len(batches) * 31 + E)
+    st_ = SegmentStore(E, reserve)
+    ins, acts, toks, counts_all = [], [], [], []
+    base = 0
+    for T, k in batches:
+        hidden = torch.randn(T, 4, generator=g)
+        e = torch.randint(0, E, (T * k,), generator=g)
+        counts = torch.bincount(e, minlength=E).tolist()
+        tok = torch.randint(0, T, (T * k,), generator=g)
+        out = st_.acts_out(T * k, T, 3, torch.float32, "cpu")
+        a = torch.randn(T * k, 3, generator=g)
+        out.copy_(a)
+        st_.add(hidden, tok, counts, out)
+        ins.append(hidden)
+        acts.append(a)
+        toks.append(tok + base)
+        counts_all.append(counts)
+        base += T
+    assert torch.equal(st_.inputs[:st_.n_tok], torch.cat(ins))
+    assert torch.equal(st_.acts[:st_.n_slot], torch.cat(acts))
+    assert torch.equal(st_.tok[:st_.n_slot].long(), torch.cat(toks))
+    assert st_.counts == [sum(c[e] for c in counts_all) for e in range(E)]
+
+
+@settings(max_examples=100, deadline=None)
+@given(st.sampled_from([2, 4, 8]), st.integers(1, 5), st.integers(1, 6), st.integers(0, 2**31 - 1))
+def test_oracle_packing_round_trip(bits, rows, words, seed):
+    import numpy as np
+
+    from oracle.packing import pack_q, unpack_q
+
+    per = 32 // bits
+    q = np.random.default_rng(seed).integers(0, 1 << bits, (rows, words * per)).astype(np.uint8)
+    w = pack_q(q, bits)
+    assert w.dtype == np.uint32 and w.shape == (rows, words)
+    assert np.array_equal(unpack_q(w, bits, words * per), q)
+    # LSB first: the first code sits in the lowest bits of the first word
+    assert np.array_equal(w[:, 0] & ((1 << bits) - 1), q[:, 0].astype(np.uint32))
