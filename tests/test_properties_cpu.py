@@ -116,3 +116,67 @@ def test_oracle_packing_round_trip(bits, rows, words, seed):
     assert np.array_equal(unpack_q(w, bits, words * per), q)
     # LSB first: the first code sits in the lowest bits of the first word
     assert np.array_equal(w[:, 0] & ((1 << bits) - 1), q[:, 0].astype(np.uint32))
+
+
+class _FakeMgr:
+    """The parts of a CaptureManager that plan_layer reads."""
+
+    def __init__(self, expert_tokens, linear_specs):
+        import types
+
+        self.stashes, self.fused_tasks, self.linear_tasks = {}, [], []
+        for ti, (E, R, C, toks) in enumerate(expert_tokens):
+            keys = []
+            for e in range(E):
+                k = f"m{ti}.p::e{e}"
+                self.stashes[k] = types.SimpleNamespace(tokens=toks[e], in_features=C)
+                keys.append(k)
+            self.fused_tasks.append(types.SimpleNamespace(param=torch.empty(E, R, C, device="meta"),
+                                                          stash_keys=keys, num_experts=E))
+        for si, (C, toks, outs) in enumerate(linear_specs):
+            key = f"lin{si}"
+            self.stashes[key] = types.SimpleNamespace(tokens=toks, in_features=C)
+            for j, R in enumerate(outs):
+                self.linear_tasks.append(types.SimpleNamespace(
+                    name=f"lin{si}_{j}", stash_key=key, module=types.SimpleNamespace(out_features=R)))
+
+    def tokens(self, key):
+        return self.stashes[key].tokens
+
+
+@st.composite
+def layers(draw):
+    fused = []
+    for _ in range(draw(st.integers(0, 2))):
+        E = draw(st.integers(1, 12))
+        fused.append((E, 64, draw(st.sampled_from([64, 128, 2048])),
+                      draw(st.lists(st.integers(0, 5000), min_size=E, max_size=E))))
+    linears = [(draw(st.sampled_from([256, 2048, 4096])), draw(st.integers(0, 10**6)),
+                draw(st.lists(st.integers(32, 4096), min_size=1, max_size=3)))
+               for _ in range(draw(st.integers(0, 3)))]
+    return fused, linears
+
+
+@settings(max_examples=150, deadline=None)
+@given(layers(), st.integers(1, 8), st.integers(1, 148), st.booleans())
+def test_plan_layer_assigns_every_item_once(layer, world, per_wave, dp):
+    from mlx_gptq_b200 import pipeline
+
+    fused, linears = layer
+    mgr = _FakeMgr(fused, linears)
+    orig = pipeline.hessian_tile_count
+    pipeline.hessian_tile_count = lambda c: (-(-c // 256)) * (-(-c // 256) + 1) // 2
+    try:
+        plans, by_stash, ranges = pipeline.plan_layer(mgr, world, per_wave=per_wave, dp=dp)
+    finally:
+        pipeline.hessian_tile_count = orig
+    assert len(plans) == world
+    for ti, (E, _, _, _) in enumerate(fused):
+        assert sorted(e for p in plans for e in p["experts"][ti]) == list(range(E))
+    assert sorted(n for p in plans for n in p["linears"]) == sorted(t.name for t in mgr.linear_tasks)
+    if dp:
+        assert all(not p["hessian_parts"] for p in plans) and ranges == {}
+    else:
+        for key, rs in ranges.items():
+            held = sorted((b, e) for p in plans for k, b, e in p["hessian_parts"] if k == key)
+            assert held == rs and rs[0][0] == 0
