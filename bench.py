@@ -502,9 +502,11 @@ QWEN3_30B_A3B = dict(model_type="qwen3_moe", vocab_size=151936, hidden_size=2048
 def run_c5(args, ws, rank, local):
     """Synthetic Qwen3-30B-A3B stack (random init, seed 0; 256 x 2048 uniform tokens,
     seed 1) calibrated layer by layer to MXFP4 (safe-scale-search) through the
-    package's Pipeline. Every rank runs the layer forwards; experts and linears are
-    split across ranks; one all-gather per task. Reports the solve stage (Hessians,
-    factors, column loops, all-gather) and the whole layer time, max over ranks."""
+    package's Pipeline. By default every rank runs the layer forwards and the solves are
+    split across ranks (one exchange of packed codes per task); with --c5-dp each rank
+    forwards its share of the windows and Hessians are summed over ranks. Reports the
+    solve stage (Hessians, factors, column loops, exchange) and the whole layer time, max
+    over ranks."""
     import types
 
     from mlx_gptq_b200 import sequential
