@@ -175,13 +175,18 @@ int gq_gptq_mxfp(const void* W, int w_dtype, const float* H, const float* U, con
  * whose binding layer has no CUDA allocator to reach (a JNI, cgo or ctypes shim
  * given only the tensors it must read and write). Inputs and outputs are still
  * the caller's.
- * Limit: B * ceil(R/128) * (C/32) <= 524288 (row tile, group) pairs, else
- * GQ_ERR_ARG; e.g. [1, 11008, 4096] uses 11008 and [128, 1536, 2048] uses 98304.
- * The first call on a device looks up the array's device address (once per
- * device, with that device current); make that first call before any stream
- * capture. The array is shared by all calls and keeps the last call's contents;
- * each call rewrites every entry it reads, so nothing needs clearing, but calls
- * that overlap on the GPU (other streams, other host threads) race on it.
+ * Limit (only when rel_err is requested): B * ceil(R/128) * (C/32) <= 524288
+ * (row tile, group) pairs, else GQ_ERR_ARG; e.g. [1, 11008, 4096] uses 11008 and
+ * [128, 1536, 2048] uses 98304. With rel_err == NULL the column loop needs no
+ * scratch at all: any size is accepted and the array is not touched.
+ * The first call on a device that asks for rel_err looks up the array's device
+ * address (once per device, with that device current) and caches it; make that
+ * first call before any stream capture, and do not reset the device
+ * (cudaDeviceReset) between calls, which would leave the cached address stale.
+ * The array is shared by all calls and keeps the last call's contents; each call
+ * rewrites every entry it reads (groups whose factor failed, info != 0, write
+ * zeros and so drop out of rel_err), so nothing needs clearing, but calls that
+ * overlap on the GPU (other streams, other host threads) race on it.
  * This entry point has no counterpart in the reference. */
 int gq_gptq_mxfp_noalloc(const void* W, int w_dtype, const float* H, const float* U, const uint8_t* dead,
                          const int32_t* info, int64_t B, int64_t R, int64_t C, int mode, int algorithm, uint8_t* q,

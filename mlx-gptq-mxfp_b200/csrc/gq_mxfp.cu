@@ -298,7 +298,7 @@ __global__ void __launch_bounds__(128, 3) mx_gptq_kernel(const Tin* __restrict__
                                                       const int32_t* __restrict__ info, int64_t R, int64_t C,
                                                       uint8_t* __restrict__ q, uint8_t* __restrict__ qp,
                                                       uint8_t* __restrict__ scales, Tout* __restrict__ wdq,
-                                                      float* __restrict__ partials) {
+                                                      float* __restrict__ partials, int64_t partials_cap) {
   __shared__ __align__(16) uint32_t Hhi[32 * kES], Hlo[32 * kES];  // tf32 split of H_g
   __shared__ __align__(16) float Us[32][32];
   __shared__ __align__(16) float Sst[4][32 * kES];  // per-warp staging for quad32
@@ -307,7 +307,14 @@ __global__ void __launch_bounds__(128, 3) mx_gptq_kernel(const Tin* __restrict__
   const int64_t G = C / 32;
   const int64_t g = blockIdx.x, tile = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x;
-  if (info && info[b * G + g] != 0) return;  // factorization failed: host raises
+  // (num, den) slot of this CTA; slots past partials_cap (the caller's workspace)
+  // are never written, whatever the grid
+  const int64_t pslot = (b * gridDim.y + tile) * G + g;
+  float* p_out = partials && pslot < partials_cap ? partials + pslot * 2 : nullptr;
+  if (info && info[b * G + g] != 0) {  // factorization failed: host raises
+    if (p_out && tid == 0) p_out[0] = p_out[1] = 0.0f;  // rel_err then ignores this group
+    return;
+  }
   const float* Hg = H + (b * C + g * 32) * C + g * 32;
   const float* Ug = U + (b * G + g) * 1024;
   for (int i = tid; i < 1024; i += 128) {
@@ -456,10 +463,9 @@ __global__ void __launch_bounds__(128, 3) mx_gptq_kernel(const Tin* __restrict__
       red[1][tid >> 5] = den;
     }
     __syncthreads();
-    if (tid == 0) {
-      float* p = partials + ((b * gridDim.y + tile) * G + g) * 2;
-      p[0] = (red[0][0] + red[0][1]) + (red[0][2] + red[0][3]);
-      p[1] = (red[1][0] + red[1][1]) + (red[1][2] + red[1][3]);
+    if (tid == 0 && p_out) {
+      p_out[0] = (red[0][0] + red[0][1]) + (red[0][2] + red[0][3]);
+      p_out[1] = (red[1][0] + red[1][1]) + (red[1][2] + red[1][3]);
     }
   }
 }
@@ -556,11 +562,12 @@ extern "C" int gq_gptq_mxfp(const void* W, int w_dtype, const float* H, const fl
   if (B * R * C == 0) return GQ_OK;
   cudaStream_t s = (cudaStream_t)stream;
   float* partials = rel_err ? reinterpret_cast<float*>(workspace) : nullptr;
+  const int64_t partials_cap = rel_err ? int64_t(workspace_bytes / (2 * sizeof(float))) : 0;
   const dim3 grid(unsigned(C / 32), unsigned((R + 127) / 128), unsigned(B));
   const bool safe = algorithm == GQ_MX_SAFE_SCALE_SEARCH;
 #define MXL(MODE, SAFE, TIN, TOUT)                                                                              \
   mx_gptq_kernel<MODE, SAFE, TIN, TOUT><<<grid, 128, 0, s>>>((const TIN*)W, H, U, dead, info, R, C, q, q_packed, \
-                                                             scales, (TOUT*)w_dq, partials)
+                                                             scales, (TOUT*)w_dq, partials, partials_cap)
 #define MXL_OUT(MODE, SAFE, TIN)                  \
   do {                                            \
     if (wdq_dtype == GQ_BF16)                     \
@@ -629,6 +636,10 @@ extern "C" int gq_gptq_mxfp_noalloc(const void* W, int w_dtype, const float* H, 
                                     const int32_t* info, int64_t B, int64_t R, int64_t C, int mode, int algorithm,
                                     uint8_t* q, uint8_t* q_packed, uint8_t* scales, void* w_dq, int wdq_dtype,
                                     float* rel_err, void* stream) {
+  // Without rel_err the column loop needs no scratch at all: no limit, no lookup.
+  if (!rel_err)
+    return gq_gptq_mxfp(W, w_dtype, H, U, dead, info, B, R, C, mode, algorithm, q, q_packed, scales, w_dq,
+                        wdq_dtype, nullptr, nullptr, 0, stream);
   const size_t need = gq_gptq_mxfp_workspace_size(B, R, C);
   GQ_REQUIRE(need <= kNoAllocScratchBytes,
              "gq_gptq_mxfp_noalloc: B*ceil(R/128)*(C/32) = %zu (row tile, group) pairs exceed the fixed scratch "

@@ -125,6 +125,38 @@ def require_cuda(*tensors: torch.Tensor) -> torch.device:
     return dev
 
 
+_status_words: dict[int, torch.Tensor] = {}
+
+
+def status_word(device: torch.device | int | None = None) -> torch.Tensor:
+    """The device's int32 status word (zero at creation). Kernels with bounded waits
+    (the Hessians) write GQ_ERR_TIMEOUT into it when a wait gives up, instead of
+    hanging; the product path passes it to every such launch and reads it with
+    raise_on_device_timeout before results are used."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    w = _status_words.get(idx)
+    if w is None:
+        with _lock:
+            w = _status_words.get(idx)
+            if w is None:
+                w = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+                _status_words[idx] = w
+    return w
+
+
+def raise_on_device_timeout(device: torch.device | int | None = None) -> None:
+    """Read the device's status word (a synchronizing copy on the current stream) and
+    raise GQError(GQ_ERR_TIMEOUT) if a bounded device wait gave up since the last
+    check; a reported failure is cleared from the word."""
+    w = status_word(device)
+    v = int(w.item())
+    if v != GQ_OK:
+        w.zero_()
+        raise GQError(v, f"a device-side wait gave up (status {v}: "
+                         f"{lib().gq_status_string(v).decode()}); the results of the launch are incomplete")
+
+
 def aligned(t: torch.Tensor) -> torch.Tensor:
     """Contiguous and 16-byte aligned (copies otherwise)."""
     if not t.is_contiguous() or t.data_ptr() % 16:

@@ -256,11 +256,15 @@ def main(argv=None):
               "calibration_tokens": args.calibration_tokens, "calibration_tokens_sha256": tokens_sha256,
               "layers_attr": args.layers_attr, "checkpoint_model_prefix": args.checkpoint_model_prefix,
               "artifact_layers_prefix": args.artifact_layers_prefix}
-    writer = ArtifactWriter(args.output, header) if rank == 0 else _ReadOnlyWriter(args.output)
+    # rank 0 writes; layer L's file goes to disk while layer L+1 is calibrated
+    writer = ArtifactWriter(args.output, header, overlap=True) if rank == 0 else _ReadOnlyWriter(args.output)
     reader = ArtifactReader(args.output) if writer.manifest["layers_done"] else None
     pipe = Pipeline(model, RawShardIndex(args.model), args, group=group, dp=args.dp_windows)
-    with torch.no_grad():
-        pipe.run(samples, writer, reader_for_resume=reader)
+    try:
+        with torch.no_grad():
+            pipe.run(samples, writer, reader_for_resume=reader)
+    finally:
+        writer.close()  # the last layer's file and manifest entry are on disk
     if group is not None:
         import torch.distributed as dist
 
@@ -283,6 +287,9 @@ class _ReadOnlyWriter:
         return layer_idx in self.manifest["layers_done"]
 
     def write_layer(self, *a, **k):
+        pass
+
+    def close(self):
         pass
 
 

@@ -17,6 +17,7 @@ the B200 side of the boundary:
 
 from __future__ import annotations
 
+import contextlib
 import logging
 import re
 from dataclasses import dataclass, field
@@ -49,7 +50,9 @@ def hessian_accumulate(X: torch.Tensor, H: torch.Tensor, alpha: float = 1.0, bet
                        status: torch.Tensor | None = None, tiles: tuple[int, int] | None = None) -> torch.Tensor:
     """H = beta * H + alpha * X^T X for bf16 rows X [n, c] and float32 H [c, c], both on
     the same CUDA device. Returns H. With tiles=(begin, end) only the blocks of those
-    output tiles (of hessian_tile_count(c)) are written, bit-identical to a full call."""
+    output tiles (of hessian_tile_count(c)) are written, bit-identical to a full call.
+    status: int32 device word for the kernel's bounded waits; default: the device's
+    library status word, read by the solvers (and Stash.hessian) before H is used."""
     L.require_cuda(X, H)
     if X.dtype != torch.bfloat16:
         raise ValueError("X must be bfloat16 (the capture dtype)")
@@ -62,6 +65,8 @@ def hessian_accumulate(X: torch.Tensor, H: torch.Tensor, alpha: float = 1.0, bet
     if H.stride(1) != 1 or H.stride(0) % 4 or H.data_ptr() % 16:
         raise ValueError("H must be row-major, 16-byte aligned, row stride % 4 == 0")
     n, c = X.shape
+    if status is None:
+        status = L.status_word(X.device)
     if tiles is None:
         L.check(L.lib().gq_hessian_bf16(L.ptr(X), n, c, X.stride(0), L.ptr(H), H.stride(0), float(alpha),
                                         float(beta), L.ptr(status), L.stream_ptr(X.device)), "hessian")
@@ -77,7 +82,9 @@ def hessian_from_rows(X: torch.Tensor) -> torch.Tensor:
     """H = X^T X (float32) for device-resident bf16 rows X [n, c]."""
     c = X.shape[1]
     H = torch.empty(c, c, dtype=torch.float32, device=X.device)
-    return hessian_accumulate(X, H, 1.0, 0.0)
+    hessian_accumulate(X, H, 1.0, 0.0)
+    L.raise_on_device_timeout(X.device)
+    return H
 
 
 @torch.no_grad()
@@ -105,7 +112,8 @@ def hessian_grouped(X: torch.Tensor, token_idx: torch.Tensor, offsets: torch.Ten
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=X.device)
     L.check(lib.gq_hessian_grouped_bf16(L.ptr(X), n, c, X.stride(0), L.ptr(idx), L.ptr(off_dev),
                                         off_host.data_ptr(), num_experts, L.ptr(H), float(alpha), float(beta),
-                                        L.ptr(ws), ws.numel(), None, L.stream_ptr(X.device)), "hessian_grouped")
+                                        L.ptr(ws), ws.numel(), L.ptr(L.status_word(X.device)),
+                                        L.stream_ptr(X.device)), "hessian_grouped")
     return H
 
 
@@ -167,6 +175,7 @@ class Stash:
                 beta = 1.0
         if beta == 0.0 and tiles is None:
             H.zero_()
+        L.raise_on_device_timeout(device)
         return H
 
     def clear(self):
@@ -260,6 +269,65 @@ class SegmentStore:
         return sum(x.numel() * x.element_size() for x in (self.inputs, self.acts, self.tok) if x is not None)
 
 
+class _BatchInputs:
+    """Tensors stashed during the current forward batch, by identity: a module that
+    reads a tensor a sibling already stashed shares the sibling's stash. The tensors
+    are held until the batch ends, so an id() cannot be reused meanwhile."""
+
+    def __init__(self):
+        self._owner: dict[int, tuple[torch.Tensor, str]] = {}
+
+    def claim(self, x: torch.Tensor, key: str) -> str | None:
+        """None if x is new in this batch (it is now `key`'s); otherwise the key of
+        the stash that already holds x."""
+        hit = self._owner.get(id(x))
+        if hit is not None and hit[0] is x:
+            return hit[1]
+        self._owner[id(x)] = (x, key)
+        return None
+
+    def clear(self) -> None:
+        self._owner.clear()
+
+
+class _ExpertRouter(TorchFunctionMode):
+    """Active during capture: every F.linear whose weight is one registered expert
+    slice (matched by data pointer, capture.py:192-207) adds its input rows to that
+    expert's stash before the call runs."""
+
+    def __init__(self, table: dict[int, "Stash"]):
+        super().__init__()
+        self.table = table
+
+    def _stash_for(self, w):
+        if not isinstance(w, torch.Tensor) or w.dim() != 2:
+            return None
+        st = self.table.get(w.data_ptr())
+        return st if st is not None and w.shape[-1] == st.in_features else None
+
+    def __torch_function__(self, func, types, args=(), kwargs=None):
+        if func is F.linear and len(args) >= 2:
+            st = self._stash_for(args[1])
+            if st is not None:
+                st.add(args[0])
+        return func(*args, **(kwargs or {}))
+
+
+def _expert_activation(tasks: dict, e: int, rows: torch.Tensor) -> torch.Tensor | None:
+    """silu(x W_gate^T) * (x W_up^T) for expert e, from a fused gate_up parameter or
+    separate gate / up parameters; None if the module has neither."""
+    if "gate_up_proj" in tasks:
+        w = tasks["gate_up_proj"].param[e]
+        gate, up = F.linear(rows.to(w.device, w.dtype), w).chunk(2, dim=-1)
+    elif "gate_proj" in tasks and "up_proj" in tasks:
+        wg, wu = tasks["gate_proj"].param[e], tasks["up_proj"].param[e]
+        x = rows.to(wg.device, wg.dtype)
+        gate, up = F.linear(x, wg), F.linear(x, wu)
+    else:
+        return None
+    return F.silu(gate) * up
+
+
 class CaptureManager:
     """Owns all stashes and hooks for one decoder layer (capture.py:100-343).
 
@@ -279,7 +347,7 @@ class CaptureManager:
         self.fused_tasks: list[FusedExpertTask] = []
         self._hooks = []
         self._ptr_registry: dict[int, str] = {}
-        self._batch_seen: dict[int, tuple] = {}
+        self._batch = _BatchInputs()
         self._fused_modules: dict[str, torch.nn.Module] = {}
         self._fused_input_stashes: dict[str, Stash] = {}
         self.fallback_experts: dict[str, str] = {}
@@ -287,9 +355,8 @@ class CaptureManager:
         self.reserve_tokens = reserve_tokens
         self._segment_modules: set[str] = set()
         self._slot_experts: dict[str, torch.Tensor] = {}
-        self._mode_registry: dict[int, str] = {}
         self.global_tokens: dict[str, int] | None = None  # summed over data-parallel ranks
-        self._mode = None
+        self._exit_stack: contextlib.ExitStack | None = None
         excl = re.compile(exclude_regex) if exclude_regex else None
         seen = set()
         for name, mod in layer.named_modules():
@@ -324,42 +391,28 @@ class CaptureManager:
         for t in self.linear_tasks:
             self.stashes.setdefault(t.name, Stash(t.name, t.module.in_features, stash_device))
 
-    # ---- nn.Linear pre-hooks with same-input dedup (capture.py:167-178) ----
-    def _make_hook(self, task: LinearTask):
-        def hook(mod, args, kwargs=None):
+    # ---- capture taps (the reference's hooks: capture.py:167-207) ----
+    def _linear_tap(self, task: LinearTask):
+        """Forward pre-hook of one nn.Linear: stash its input, unless a sibling read the
+        very same tensor earlier in this batch (q/k/v, gate/up), in which case the task
+        adopts the sibling's stash and nothing is copied."""
+        def tap(mod, args, kwargs):
             x = args[0] if args else kwargs["input"]
-            seen = self._batch_seen.get(id(x))
-            if seen is not None and seen[0] is x:
-                task.stash_key = seen[1]
-                return
-            self._batch_seen[id(x)] = (x, task.stash_key)
-            self.stashes[task.stash_key].add(x)
-        return hook
+            owner = self._batch.claim(x, task.stash_key)
+            if owner is None:
+                self.stashes[task.stash_key].add(x)
+            else:
+                task.stash_key = owner
+        return tap
 
-    def _make_fused_input_hook(self, module_name: str):
-        def hook(mod, args, kwargs=None):
-            x = args[0] if args else kwargs["hidden_states"]
-            self._fused_input_stashes[module_name].add_sampled(x, 64)
-        return hook
+    def _fused_sample_tap(self, module_name: str):
+        """Forward pre-hook of a fused-expert module: keep 64 evenly spaced rows of its
+        input per batch, the activation-aware fallback for experts no token reaches."""
+        sample = self._fused_input_stashes[module_name]
 
-    class _ExpertMode(TorchFunctionMode):
-        """Routes F.linear inputs to the stash of the expert slice used as weight (capture.py:192-207)."""
-
-        def __init__(self, mgr):
-            super().__init__()
-            self.mgr = mgr
-
-        def __torch_function__(self, func, types, args=(), kwargs=None):
-            kwargs = kwargs or {}
-            if func is F.linear and len(args) >= 2:
-                w = args[1]
-                if isinstance(w, torch.Tensor) and w.dim() == 2:
-                    key = self.mgr._mode_registry.get(w.data_ptr())
-                    if key is not None:
-                        st = self.mgr.stashes[key]
-                        if w.shape[-1] == st.in_features:
-                            st.add(args[0])
-            return func(*args, **kwargs)
+        def tap(mod, args, kwargs):
+            sample.add_sampled(args[0] if args else kwargs["hidden_states"], 64)
+        return tap
 
     def _make_segment_sink(self, module_name: str):
         tasks = [t for t in self.fused_tasks if t.module_name == module_name]
@@ -377,36 +430,35 @@ class CaptureManager:
     def __enter__(self):
         from .experts import uses_grouped
 
+        stack = contextlib.ExitStack()
         for t in self.linear_tasks:
-            self._hooks.append(t.module.register_forward_pre_hook(self._make_hook(t)))
+            stack.callback(t.module.register_forward_pre_hook(self._linear_tap(t), with_kwargs=True).remove)
+        routed = set()  # experts whose rows arrive through a sort-based forward, not F.linear
         for name, module in self._fused_modules.items():
             if name in self._fused_input_stashes:
-                self._hooks.append(module.register_forward_pre_hook(self._make_fused_input_hook(name)))
+                stack.callback(module.register_forward_pre_hook(self._fused_sample_tap(name),
+                                                                with_kwargs=True).remove)
             if uses_grouped(module):
-                # sort-based forward: rows arrive as token indices + activation segments
                 module._gq_sink = self._make_segment_sink(name)
                 self._segment_modules.add(name)
-        skip = {k for t in self.fused_tasks if t.module_name in self._segment_modules for k in t.stash_keys}
-        self._mode_registry = {p: k for p, k in self._ptr_registry.items() if k not in skip}
-        if self._mode_registry:
-            self._mode = self._ExpertMode(self)
-            self._mode.__enter__()
+                stack.callback(module.__dict__.pop, "_gq_sink", None)
+                routed.update(k for t in self.fused_tasks if t.module_name == name for k in t.stash_keys)
+        table = {ptr: self.stashes[k] for ptr, k in self._ptr_registry.items() if k not in routed}
+        if table:
+            stack.enter_context(_ExpertRouter(table))
+        stack.callback(self._batch.clear)
+        self._exit_stack = stack
         return self
 
     def __exit__(self, *exc):
-        if self._mode is not None:
-            self._mode.__exit__(*exc)
-            self._mode = None
-        for name in self._segment_modules:
-            self._fused_modules[name].__dict__.pop("_gq_sink", None)
-        for h in self._hooks:
-            h.remove()
-        self._hooks.clear()
-        self._batch_seen.clear()
+        stack, self._exit_stack = self._exit_stack, None
+        if stack is not None:
+            stack.close()
         return False
 
     def begin_batch(self):
-        self._batch_seen.clear()
+        """A new forward batch: input identities from the previous one no longer dedup."""
+        self._batch.clear()
 
     def tokens(self, key: str) -> int:
         """Rows captured for a stash: this process's, or the sum over data-parallel
@@ -441,45 +493,48 @@ class CaptureManager:
 
     @torch.no_grad()
     def backfill_unrouted_experts(self):
-        """Give never-routed experts a bounded sample of the block's real inputs
-        (capture.py:253-326); down-proj inputs come from that expert's own gate/up."""
-        by_module: dict[str, dict[str, FusedExpertTask]] = {}
-        for task in self.fused_tasks:
-            by_module.setdefault(task.module_name, {})[task.param_name] = task
-        backfilled = {}
-        for module_name, tasks in by_module.items():
-            source = self._fused_input_stashes.get(module_name)
-            if source is None or source.tokens == 0:
+        """Experts that no calibration token reached get real inputs instead of a zero
+        Hessian (capture.py:253-326): their input-side stashes receive the module's
+        sampled input rows, and their down_proj stash the activations those rows
+        produce through the expert's own gate/up weights. Returns module -> experts."""
+        done = {}
+        for module_name, tasks in self._fused_tasks_by_module().items():
+            sample = self._fused_input_stashes.get(module_name)
+            feeder = next((tasks[n] for n in ("gate_up_proj", "gate_proj", "up_proj") if n in tasks), None)
+            if sample is None or sample.tokens == 0 or feeder is None:
                 continue
-            input_task = next((tasks[n] for n in ("gate_up_proj", "gate_proj", "up_proj") if n in tasks), None)
-            if input_task is None:
+            missing = [e for e, key in enumerate(feeder.stash_keys) if self.tokens(key) == 0]
+            for e in missing:
+                self._backfill_expert(tasks, e, sample)
+            if missing:
+                done[module_name] = missing
+        return done
+
+    def _fused_tasks_by_module(self) -> dict[str, dict[str, FusedExpertTask]]:
+        out: dict[str, dict[str, FusedExpertTask]] = {}
+        for t in self.fused_tasks:
+            out.setdefault(t.module_name, {})[t.param_name] = t
+        return out
+
+    def _backfill_expert(self, tasks: dict[str, FusedExpertTask], e: int, sample: Stash) -> None:
+        for pname, task in tasks.items():
+            if pname == "down_proj":
                 continue
-            missing = [e for e, key in enumerate(input_task.stash_keys) if self.tokens(key) == 0]
-            for expert in missing:
-                for task in tasks.values():
-                    if task.param_name == "down_proj":
-                        continue
-                    stash = self.stashes[task.stash_keys[expert]]
-                    for chunk in source.chunks:
-                        stash.add(chunk)
-                    self.fallback_experts[task.stash_keys[expert]] = "all_expert_inputs"
-                down_task = tasks.get("down_proj")
-                if down_task is not None:
-                    down_stash = self.stashes[down_task.stash_keys[expert]]
-                    if "gate_up_proj" in tasks:
-                        gate_up = tasks["gate_up_proj"].param[expert]
-                        for chunk in source.chunks:
-                            gate, up = F.linear(chunk.to(gate_up.device, gate_up.dtype), gate_up).chunk(2, dim=-1)
-                            down_stash.add(F.silu(gate) * up)
-                    elif "gate_proj" in tasks and "up_proj" in tasks:
-                        gw, uw = tasks["gate_proj"].param[expert], tasks["up_proj"].param[expert]
-                        for chunk in source.chunks:
-                            x = chunk.to(gw.device, gw.dtype)
-                            down_stash.add(F.silu(F.linear(x, gw)) * F.linear(x, uw))
-                    if down_stash.tokens:
-                        self.fallback_experts[down_task.stash_keys[expert]] = "all_expert_inputs"
-                backfilled.setdefault(module_name, []).append(expert)
-        return backfilled
+            key = task.stash_keys[e]
+            for rows in sample.chunks:
+                self.stashes[key].add(rows)
+            self.fallback_experts[key] = "all_expert_inputs"
+        down = tasks.get("down_proj")
+        if down is None:
+            return
+        key = down.stash_keys[e]
+        for rows in sample.chunks:
+            act = _expert_activation(tasks, e, rows)
+            if act is None:
+                break
+            self.stashes[key].add(act)
+        if self.stashes[key].tokens:
+            self.fallback_experts[key] = "all_expert_inputs"
 
     def check_capture_happened(self):
         """capture.py:328-337: fused experts must have gone through F.linear."""

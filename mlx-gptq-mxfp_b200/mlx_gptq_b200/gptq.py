@@ -62,6 +62,7 @@ def _prepare_hinv(H: torch.Tensor, damp: float, max_attempts: int = 6) -> torch.
     info = torch.empty(B, dtype=torch.int32, device=dev)
     used = torch.empty(B, dtype=torch.float32, device=dev)
     ws = torch.empty(L.lib().gq_prepare_hinv_workspace_size(B, Cf), dtype=torch.uint8, device=dev)
+    L.raise_on_device_timeout(dev)  # a Hessian formed on this device finished every wait
     st = L.lib().gq_prepare_hinv(L.ptr(Hf), B, Cf, float(damp), L.ptr(U), L.ptr(info), L.ptr(used),
                                  L.ptr(ws), ws.numel(), L.stream_ptr(dev))
     if st == L.GQ_ERR_NOT_PD:
@@ -106,6 +107,7 @@ def _solve_mxfp(W_src: torch.Tensor, H: torch.Tensor, mode: str, damp: float, al
                              L.GQ_MX_SAFE_SCALE_SEARCH if algorithm == "safe-scale-search" else L.GQ_MX_GROUPWISE,
                              L.ptr(q), L.ptr(q_packed), L.ptr(scales), L.ptr(W_out), L.DTYPE_CODE[W_out.dtype],
                              L.ptr(rel), L.ptr(ws), ws.numel(), stream), "gptq mxfp")
+    L.raise_on_device_timeout(dev)  # a Hessian formed on this device finished every wait
     failed_groups = info != 0
     if bool(failed_groups.any()):
         raise _not_pd_error(H, failed_groups.any(dim=1), B)

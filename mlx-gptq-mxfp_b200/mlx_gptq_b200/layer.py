@@ -89,6 +89,7 @@ def solve_mxfp_packed(W: torch.Tensor, f: MxfpFactors, mode: str = "mxfp4", algo
                              q_ptr, qp_ptr, L.ptr(scales), L.ptr(w_dq), L.DTYPE_CODE[wdq_dtype], L.ptr(rel),
                              L.ptr(ws), ws.numel(), stream), "gptq mxfp")
     if check_info:
+        L.raise_on_device_timeout(dev)  # the Hessian behind f finished every wait
         failed = f.info != 0
         if bool(failed.any()):
             raise _not_pd_error(f.H, failed.any(dim=1), B)

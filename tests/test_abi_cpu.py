@@ -113,3 +113,20 @@ def test_hessian_tile_schedule_queries(lib, monkeypatch):
     st = lib.gq_hessian_bf16_range(None, 0, 4, 8, h.ctypes.data, 4, 1.0, 0.0, 0, 5, None, None)
     assert st == 1 and b"tile range" in lib.gq_last_error()  # GQ_ERR_ARG before any launch
     assert lib.gq_hessian_bf16_range(None, 0, 4, 8, h.ctypes.data, 4, 1.0, 0.0, 1, 1, None, None) == 0  # empty
+
+
+def test_timed_out_status_word_raises(monkeypatch):
+    """A bounded device wait that gave up leaves GQ_ERR_TIMEOUT in the device's status
+    word; the solver entry points read it and raise instead of using a partial H.
+    Host-side check with a CPU stand-in for the device word."""
+    import torch
+
+    from mlx_gptq_b200 import _lib
+
+    word = torch.tensor([_lib.GQ_ERR_TIMEOUT], dtype=torch.int32)
+    monkeypatch.setattr(_lib, "status_word", lambda device=None: word)
+    with pytest.raises(_lib.GQError) as ei:
+        _lib.raise_on_device_timeout("cpu")
+    assert ei.value.status == _lib.GQ_ERR_TIMEOUT and "gave up" in str(ei.value)
+    assert int(word.item()) == 0  # reported once, then cleared
+    _lib.raise_on_device_timeout("cpu")  # a clear word raises nothing

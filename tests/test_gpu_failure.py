@@ -40,3 +40,24 @@ def test_selftest_rejects_unbounded_limit():
 
     p = 16
     assert L.lib().gq_selftest_wait_timeout(10_000_000_000, p, p, None) == L.GQ_ERR_ARG
+
+
+def test_hessian_path_raises_on_a_timed_out_status_word():
+    """The Hessian wrappers pass the device's status word to every launch and the
+    solver entry points read it: a word holding GQ_ERR_TIMEOUT (set here by the host,
+    as a wait that gave up would) makes Stash.hessian and solve_gptq raise."""
+    from mlx_gptq_b200 import _lib as L
+    from mlx_gptq_b200 import Stash, solve_gptq
+
+    st = Stash("probe", 64)
+    st.add(torch.randn(256, 64, device="cuda").to(torch.bfloat16))
+    word = L.status_word(torch.device("cuda", torch.cuda.current_device()))
+    word.fill_(L.GQ_ERR_TIMEOUT)
+    with pytest.raises(L.GQError):
+        st.hessian("cuda")
+    assert int(word.item()) == 0
+    H = st.hessian("cuda")  # clear word: normal result
+    word.fill_(L.GQ_ERR_TIMEOUT)
+    with pytest.raises(L.GQError):
+        solve_gptq(torch.randn(1, 8, 64, device="cuda") * 0.02, H.unsqueeze(0).clone(), 4, 32, mode="mxfp4")
+    assert int(word.item()) == 0

@@ -4,11 +4,20 @@ Some callers cannot allocate device memory themselves: a host that owns every
 byte through its own pool, a loop that must not allocate while it runs, or a
 foreign-language binding that is handed only the tensors to read and write.
 For them the library offers a variant of gq_gptq_mxfp whose rel_err scratch is
-a fixed array inside the library instead of a caller workspace. This test calls
-it through the C ABI, twice in a row on different inputs, and compares every
-output with the workspace-taking entry point on the same inputs (it must be
-bit-identical: same kernels, same reduction order). It also checks that a
-problem larger than the fixed scratch is refused with an argument error.
+a fixed array inside the library instead of a caller workspace. These tests
+call it through the C ABI:
+
+* twice in a row on different inputs, comparing every output, rel_err included,
+  with the workspace-taking entry point on the same inputs: they must be
+  bit-identical (same kernels, same reduction order), and the second call must
+  not see the first call's scratch;
+* on a problem larger than the fixed scratch: refused with an argument error when
+  rel_err is asked for, accepted (and equal to the workspace entry point) when it
+  is not, since the column loop then needs no scratch.
+
+Every pointer handed to the library is a real device buffer of the size the
+call describes, so even a regression in the size check could not make a kernel
+read or write outside memory this test owns.
 
 The file is named so that pytest collects it last.
 """
@@ -63,19 +72,52 @@ def test_noalloc_matches_workspace_entry_point_two_calls():
         f = mxfp_factors(H)
         ref = _solve(lib, L, W, f, noalloc=False)
         got = _solve(lib, L, W, f, noalloc=True)
-        for a, b in zip(ref[:4], got[:4]):
+        for a, b in zip(ref, got):
             assert torch.equal(a, b)
-        torch.testing.assert_close(got[4], ref[4], rtol=1e-6, atol=0.0)
         assert torch.isfinite(got[4]).all() and (got[4] > 0).all()
 
 
-def test_noalloc_rejects_problems_beyond_its_scratch():
+def _oversize():
+    """A problem one row tile past the scratch limit, as real device buffers: B = 512,
+    R = 131,200 (1,025 row tiles of 128), C = 32 gives 524,800 (tile, group) pairs
+    against 524,288. W is bf16 (4.3 GB); H and U are per-item 32 x 32 blocks."""
+    B, R, C = 512, 131200, 32
+    g = torch.Generator(device="cuda").manual_seed(5)
+    W = (torch.randn(B, R, C, generator=g, device="cuda", dtype=torch.float32) * 0.02).to(torch.bfloat16)
+    A = torch.randn(B, C, 2 * C, generator=g, device="cuda")
+    H = A @ A.transpose(1, 2)
+    return W, H
+
+
+def _run_oversize(lib, L, W, f, noalloc, with_rel):
+    B, R, C = W.shape
+    qp = torch.empty(B, R, C // 2, dtype=torch.uint8, device="cuda")
+    s = torch.empty(B, R, C // 32, dtype=torch.uint8, device="cuda")
+    rel = torch.empty(B, dtype=torch.float32, device="cuda") if with_rel else None
+    args = [W.data_ptr(), L.GQ_BF16, f.H.data_ptr(), f.U.data_ptr(), f.dead.data_ptr(), f.info.data_ptr(),
+            B, R, C, L.GQ_MXFP4, L.GQ_MX_SAFE_SCALE_SEARCH, None, qp.data_ptr(), s.data_ptr(), None, L.GQ_F32,
+            None if rel is None else rel.data_ptr()]
+    if noalloc:
+        st = lib.gq_gptq_mxfp_noalloc(*args, L.stream_ptr())
+    else:
+        st = lib.gq_gptq_mxfp(*args, None, 0, L.stream_ptr())
+    torch.cuda.synchronize()
+    return st, qp, s
+
+
+def test_noalloc_size_limit_applies_only_to_rel_err():
     from mlx_gptq_b200 import _lib as L
+    from mlx_gptq_b200.layer import mxfp_factors
 
     lib = L.lib()
-    p = ctypes.c_void_p(256)
-    # 128 * ceil(4096/128) * (8192/32) = 1,048,576 (tile, group) pairs > 524,288
-    st = lib.gq_gptq_mxfp_noalloc(p, L.GQ_F32, p, p, None, None, 128, 4096, 8192, L.GQ_MXFP4,
-                                  L.GQ_MX_SAFE_SCALE_SEARCH, None, None, p, None, L.GQ_F32, p, None)
+    W, H = _oversize()
+    f = mxfp_factors(H)
+    assert int(lib.gq_gptq_mxfp_workspace_size(*W.shape)) // 8 > 524288
+    st, _, _ = _run_oversize(lib, L, W, f, noalloc=True, with_rel=True)
     assert st == L.GQ_ERR_ARG
     assert b"fixed scratch" in lib.gq_last_error()
+    st, qp, s = _run_oversize(lib, L, W, f, noalloc=True, with_rel=False)
+    L.check(st, "noalloc without rel_err")
+    st, qp_ref, s_ref = _run_oversize(lib, L, W, f, noalloc=False, with_rel=False)
+    L.check(st, "workspace entry point without rel_err")
+    assert torch.equal(qp, qp_ref) and torch.equal(s, s_ref)
