@@ -47,43 +47,60 @@ DEFAULT_EXCLUDE = r"(^|\.)gate$|(^|\.)router($|\.)|shared_expert_gate|e_score"  
 # ---------------------------------------------------------------------------
 # weight sources
 # ---------------------------------------------------------------------------
-class RawShardIndex:
-    """Name -> shard lookup over a Hugging Face model directory (sequential.py:44-90)."""
+class ShardIndex:
+    """Tensor name -> file of a Hugging Face safetensors checkpoint (the reference's
+    RawShardIndex contract: ``has``, ``get``, ``get_rows``, ``names_with_prefix``).
+    Files are opened on first use and kept in a small LRU; ``get_rows`` reads only the
+    requested rows of a tensor (lazy per-layer embeddings)."""
 
-    def __init__(self, model_dir: str):
+    INDEX = "model.safetensors.index.json"
+
+    def __init__(self, model_dir: str, single_file: str = "model.safetensors", open_files: int = 16):
+        import glob
+
         self.dir = model_dir
-        idx = os.path.join(model_dir, "model.safetensors.index.json")
-        if os.path.exists(idx):
-            with open(idx) as f:
-                self.weight_map = json.load(f)["weight_map"]
+        index = os.path.join(model_dir, self.INDEX)
+        if os.path.exists(index):
+            with open(index) as f:
+                self.weight_map: dict[str, str] = json.load(f)["weight_map"]
         else:
-            single = os.path.join(model_dir, "model.safetensors")
-            if not os.path.exists(single):
+            files = sorted(glob.glob(os.path.join(model_dir, single_file)))
+            if not files:
                 raise FileNotFoundError(f"no safetensors found in {model_dir}")
-            from safetensors import safe_open
+            fname = os.path.basename(files[0])
+            self.weight_map = dict.fromkeys(self._open(fname).keys(), fname)
+        self._handles: dict[str, object] = {}
+        self._cap = open_files
 
-            with safe_open(single, framework="pt") as f:
-                self.weight_map = {n: "model.safetensors" for n in f.keys()}
-        self._open = {}
+    def _open(self, fname: str):
+        from safetensors import safe_open
 
-    def _file(self, fname):
-        if fname not in self._open:
-            from safetensors import safe_open
+        return safe_open(os.path.join(self.dir, fname), framework="pt")
 
-            self._open[fname] = safe_open(os.path.join(self.dir, fname), framework="pt")
-        return self._open[fname]
+    def _handle(self, name: str):
+        fname = self.weight_map[name]
+        h = self._handles.pop(fname, None)
+        if h is None:
+            h = self._open(fname)
+        self._handles[fname] = h  # most recently used last
+        while len(self._handles) > self._cap:
+            self._handles.pop(next(iter(self._handles)))
+        return h
 
     def has(self, name: str) -> bool:
         return name in self.weight_map
 
     def get(self, name: str) -> torch.Tensor:
-        return self._file(self.weight_map[name]).get_tensor(name)
+        return self._handle(name).get_tensor(name)
 
     def get_rows(self, name: str, rows: list[int]) -> torch.Tensor:
-        return self._file(self.weight_map[name]).get_slice(name)[rows]
+        return self._handle(name).get_slice(name)[rows]
 
     def names_with_prefix(self, prefix: str):
         return [n for n in self.weight_map if n.startswith(prefix)]
+
+
+RawShardIndex = ShardIndex  # the reference's name (mlx_gptq/sequential.py:44-90)
 
 
 class SyntheticWeights:
@@ -159,45 +176,56 @@ def build_model(model_or_config, dtype: torch.dtype = torch.bfloat16):
     return model
 
 
+_FUSED_EXPERT_PARAM = re.compile(r"^(.*)\.(gate_up_proj|gate_proj|up_proj|down_proj)$")
+
+
+def _to(t: torch.Tensor, device, dtype) -> torch.Tensor:
+    """Checkpoint tensor -> device, floating point ones in the runtime dtype."""
+    return (t.to(dtype) if t.is_floating_point() else t).to(device)
+
+
+def _expert_sources(name: str, p: torch.Tensor):
+    """For a fused 3-D expert parameter missing from the checkpoint, the per-expert
+    tensors that make it up: [[gate, up] or [proj]] per expert; None otherwise."""
+    m = _FUSED_EXPERT_PARAM.match(name)
+    if m is None or p.dim() != 3:
+        return None
+    base, kind = m.groups()
+    parts = ("gate_proj", "up_proj") if kind == "gate_up_proj" else (kind,)
+    return [[f"{base}.{e}.{part}.weight" for part in parts] for e in range(p.shape[0])]
+
+
+def _load_param(shards, name: str, p: torch.Tensor, device, dtype) -> torch.Tensor:
+    if shards.has(name):
+        return _to(shards.get(name), device, dtype)
+    sources = _expert_sources(name, p)
+    if sources is None:
+        raise KeyError(f"cannot materialize parameter {name} from checkpoint")
+    fused = torch.empty(p.shape, dtype=dtype, device=device)
+    for e, names in enumerate(sources):  # expert e = its rows stacked ([gate; up] for gate_up)
+        torch.cat([_to(shards.get(n), device, dtype) for n in names], dim=0, out=fused[e])
+    return fused
+
+
+def _load_buffer(shards, name: str, b: torch.Tensor, device, dtype) -> torch.Tensor:
+    if shards.has(name):
+        return _to(shards.get(name), device, dtype)
+    if b.is_meta:
+        raise KeyError(f"meta buffer {name} not in checkpoint")
+    return b.to(device)  # derived buffers built at init (not checkpointed) follow the layer
+
+
 def materialize_module(module: torch.nn.Module, prefix: str, shards, device, dtype) -> None:
-    """Fill a meta module's parameters and buffers from `shards` (sequential.py:93-145),
-    fusing per-expert checkpoint tensors into the runtime 3-D layout
-    (X.gate_up_proj [E, 2I, H] <- X.{e}.gate_proj / X.{e}.up_proj; X.down_proj [E, H, I])."""
-    sd = {}
-    for pname, p in module.named_parameters():
-        raw = f"{prefix}.{pname}"
-        if shards.has(raw):
-            t = shards.get(raw)
-            sd[pname] = (t.to(dtype) if t.is_floating_point() else t).to(device)
-            continue
-        m = re.match(r"^(.*)\.(gate_up_proj|gate_proj|up_proj|down_proj)$", pname)
-        if m and p.dim() == 3:
-            base, kind = m.groups()
-            fused = torch.empty(p.shape, dtype=dtype, device=device)
-            for e in range(p.shape[0]):
-                if kind == "gate_up_proj":
-                    g = shards.get(f"{prefix}.{base}.{e}.gate_proj.weight")
-                    u = shards.get(f"{prefix}.{base}.{e}.up_proj.weight")
-                    fused[e, : g.shape[0]] = g.to(dtype)
-                    fused[e, g.shape[0]:] = u.to(dtype)
-                else:
-                    fused[e] = shards.get(f"{prefix}.{base}.{e}.{kind}.weight").to(dtype)
-            sd[pname] = fused
-            continue
-        raise KeyError(f"cannot materialize parameter {prefix}.{pname} from checkpoint")
-    for bname, b in module.named_buffers():
-        raw = f"{prefix}.{bname}"
-        if shards.has(raw):
-            v = shards.get(raw)
-            sd[bname] = (v.to(dtype) if v.is_floating_point() else v).to(device)
-        elif b.is_meta:
-            raise KeyError(f"meta buffer {prefix}.{bname} not in checkpoint")
-        else:
-            sd[bname] = b.to(device)
-    module.load_state_dict(sd, strict=False, assign=True)
-    for n, p in module.named_parameters():
-        if p.is_meta:
-            raise RuntimeError(f"parameter {prefix}.{n} still on meta after materialize")
+    """Give a meta module real parameters and buffers from `shards` (sequential.py:93-145):
+    checkpoint tensors by name, fused 3-D expert parameters assembled from per-expert
+    checkpoint tensors (gate_up_proj [E, 2I, H] from X.{e}.gate_proj / X.{e}.up_proj,
+    down_proj [E, H, I] from X.{e}.down_proj), derived buffers moved to `device`."""
+    state = {n: _load_param(shards, f"{prefix}.{n}", p, device, dtype) for n, p in module.named_parameters()}
+    state.update({n: _load_buffer(shards, f"{prefix}.{n}", b, device, dtype) for n, b in module.named_buffers()})
+    module.load_state_dict(state, strict=False, assign=True)
+    left = [n for n, p in module.named_parameters() if p.is_meta]
+    if left:
+        raise RuntimeError(f"parameter {prefix}.{left[0]} still on meta after materialize")
 
 
 def free_module(module: torch.nn.Module):
@@ -255,26 +283,40 @@ def install_lazy_ple(module: torch.nn.Module, prefix: str, shards, device, dtype
 # ---------------------------------------------------------------------------
 # layer-0 inputs and per-layer call contexts
 # ---------------------------------------------------------------------------
-class _CatchDone(Exception):
-    pass
+class _StopForward(Exception):
+    """Raised by the last recorder: the rest of the model call is not needed."""
 
 
-class Catcher(torch.nn.Module):
-    """Stands in for every decoder layer during one model call and records the
-    layer-0 hidden states and each layer's (args, kwargs) (sequential.py:253-268)."""
+@dataclass
+class _CallLog:
+    """What one model call looks like from the decoder stack: the hidden states that
+    enter layer 0 and the (args, kwargs) every layer is called with."""
+    n_layers: int
+    hidden: torch.Tensor | None = None
+    contexts: list = field(default_factory=list)
 
-    def __init__(self, store, layer_idx: int, stop: bool = False):
+    def __post_init__(self):
+        self.contexts = [None] * self.n_layers
+
+    def complete(self) -> bool:
+        return self.hidden is not None and all(c is not None for c in self.contexts)
+
+
+class _LayerRecorder(torch.nn.Module):
+    """Stands in for decoder layer `index` during one model call (sequential.py:236-253):
+    records its call into the log and passes the hidden states through; the last one
+    ends the call."""
+
+    def __init__(self, log: _CallLog, index: int):
         super().__init__()
-        self.store = store
-        self.layer_idx = layer_idx
-        self.stop = stop
+        self.log, self.index = log, index
 
     def forward(self, hidden_states, *args, **kwargs):
-        if self.layer_idx == 0:
-            self.store["hidden"] = hidden_states.detach().clone()
-        self.store["contexts"][self.layer_idx] = (args, kwargs)
-        if self.stop:
-            raise _CatchDone
+        if self.index == 0:
+            self.log.hidden = hidden_states.detach().clone()
+        self.log.contexts[self.index] = (args, kwargs)
+        if self.index == self.log.n_layers - 1:
+            raise _StopForward
         return hidden_states
 
 
@@ -391,20 +433,17 @@ class Pipeline:
         original = list(self.layers)
         try:
             for i in range(0, samples.shape[0], batch_size):
-                captured = {"hidden": None, "contexts": [None] * len(self.layers)}
-                for li in range(len(self.layers)):
-                    self.layers[li] = Catcher(captured, li, stop=li == len(self.layers) - 1)
-                ids = samples[i: i + batch_size].to(self.dev0)
-                try:
-                    self.model(input_ids=ids, use_cache=False)
-                except _CatchDone:
-                    pass
-                if captured["hidden"] is None or any(c is None for c in captured["contexts"]):
+                log_ = _CallLog(len(original))
+                for li in range(len(original)):
+                    self.layers[li] = _LayerRecorder(log_, li)
+                with contextlib.suppress(_StopForward):
+                    self.model(input_ids=samples[i: i + batch_size].to(self.dev0), use_cache=False)
+                if not log_.complete():
                     raise RuntimeError("catcher did not observe every decoder layer")
                 memo = {}
                 contexts = [(_detach_context(args, memo), {k: _detach_context(v, memo) for k, v in kwargs.items()})
-                            for args, kwargs in captured["contexts"]]
-                batches.append((captured["hidden"], contexts))
+                            for args, kwargs in log_.contexts]
+                batches.append((log_.hidden, contexts))
         finally:
             for li, layer in enumerate(original):
                 self.layers[li] = layer
