@@ -94,3 +94,37 @@ def solve_mxfp_packed(W: torch.Tensor, f: MxfpFactors, mode: str = "mxfp4", algo
         if bool(failed.any()):
             raise _not_pd_error(f.H, failed.any(dim=1), B)
     return MxfpSolution(codes, scales, w_dq, rel)
+
+
+@torch.no_grad()
+def solve_experts(W: torch.Tensor, H: torch.Tensor, counts, mode: str = "mxfp4", algorithm: str = "auto",
+                  wdq_dtype: torch.dtype = torch.bfloat16, want_rel: bool = True, damp: float = 0.01,
+                  check_info: bool = True) -> MxfpSolution:
+    """A routed expert batch W [E, R, C] against its per-expert Hessians H [E, C, C]
+    (mode mxfp4 / mxfp8): one factor launch and one column-loop launch for all experts;
+    experts that received no token (counts[e] == 0) get data-free RTN instead
+    (rtn_quantize_mxfp, grid.py:142-151), not GPTQ against an all-zero H, which would
+    zero them (gptq.py:216-222)."""
+    f = mxfp_factors(H, damp)
+    sol = solve_mxfp_packed(W, f, mode, algorithm, wdq_dtype, want_rel, check_info=check_info)
+    empty = [e for e, c in enumerate(list(counts)) if int(c) == 0]
+    if empty:
+        idx = torch.tensor(empty, dtype=torch.long, device=W.device)
+        We = L.aligned(W.index_select(0, idx))
+        n, R, C = We.shape
+        q = torch.empty(n, R, C, dtype=torch.uint8, device=W.device)
+        codes = torch.empty((n,) + tuple(sol.codes.shape[1:]), dtype=torch.uint8, device=W.device) \
+            if mode == "mxfp4" else q
+        scales = torch.empty(n, R, C // MX_GROUP_SIZE, dtype=torch.uint8, device=W.device)
+        dq = torch.empty(n, R, C, dtype=torch.float32, device=W.device)
+        qp_ptr = L.ptr(codes) if mode == "mxfp4" else None
+        L.check(L.lib().gq_rtn_mxfp(L.ptr(We), L.DTYPE_CODE[We.dtype], n * R, C, L.MODE_CODE[mode], L.ptr(q), qp_ptr,
+                                    L.ptr(scales), L.ptr(dq), L.GQ_F32, L.stream_ptr(W.device)), "rtn fallback")
+        sol.codes.index_copy_(0, idx, codes)
+        sol.scales.index_copy_(0, idx, scales)
+        sol.w_dq.index_copy_(0, idx, dq.to(sol.w_dq.dtype))
+        if sol.rel_err is not None:
+            Wf = We.float()
+            rel = (dq - Wf).flatten(1).norm(dim=1) / Wf.flatten(1).norm(dim=1).clamp_min(1e-12)
+            sol.rel_err.index_copy_(0, idx, rel)
+    return sol
