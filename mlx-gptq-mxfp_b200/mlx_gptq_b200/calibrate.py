@@ -3,14 +3,18 @@
     python -m mlx_gptq_b200.calibrate --model DIR --output OUT \\
         --calibration-tokens windows.npy --mode mxfp4
 
-Several GPUs are several processes (one per GPU):
+Several GPUs, two ways:
 
+    python -m mlx_gptq_b200.calibrate --devices cuda:0,cuda:1,... --model DIR ...
     torchrun --nproc-per-node 8 -m mlx_gptq_b200.calibrate --model DIR ...
 
-Differences from the reference, all on the device side: one process per GPU
-instead of one thread per entry of --devices (under torchrun the process's GPU is
-LOCAL_RANK; without it the first --devices entry); Hugging Face dataset sources
-(hf:, hfchat:) need a network and are refused; Flint models are not supported.
+The first is the reference's own mode: one process, the layer forward on the first
+device, each fused expert parameter's experts spread over every listed device (one
+worker thread per device), the plain linears on the first device. The second runs
+one process per GPU (the process's GPU is LOCAL_RANK): experts and linears split
+over the ranks, one all-gather of the quantized outputs per task. Hugging Face
+dataset sources (hf:, hfchat:) need a network and are refused; Flint models are not
+supported.
 """
 
 from __future__ import annotations
@@ -70,7 +74,8 @@ def build_parser() -> argparse.ArgumentParser:
     ap.add_argument("--clip", default="mse", choices=("mse", "minmax"))
     ap.add_argument("--damp", type=float, default=0.01)
     ap.add_argument("--dtype", default="bfloat16", choices=("bfloat16", "float16"))
-    ap.add_argument("--devices", default=None, help="comma-separated; the first is this process's device")
+    ap.add_argument("--devices", default=None,
+                    help="comma-separated; the forward runs on the first, experts are spread over all")
     ap.add_argument("--vram-gb", default="16", help="expert-solve budget in GiB (one value or one per device)")
     ap.add_argument("--layers-attr", default="model.layers")
     ap.add_argument("--checkpoint-model-prefix", default=None)

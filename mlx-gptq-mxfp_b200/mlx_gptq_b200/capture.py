@@ -20,6 +20,7 @@ from __future__ import annotations
 import contextlib
 import logging
 import re
+import threading
 from dataclasses import dataclass, field
 
 import torch
@@ -354,7 +355,8 @@ class CaptureManager:
         self._segments: dict[str, SegmentStore] = {}  # sort-based expert modules
         self.reserve_tokens = reserve_tokens
         self._segment_modules: set[str] = set()
-        self._slot_experts: dict[str, torch.Tensor] = {}
+        self._slot_experts: dict[tuple[str, str], torch.Tensor] = {}
+        self._slot_lock = threading.Lock()
         self.global_tokens: dict[str, int] | None = None  # summed over data-parallel ranks
         self._exit_stack: contextlib.ExitStack | None = None
         excl = re.compile(exclude_regex) if exclude_regex else None
@@ -561,9 +563,11 @@ class CaptureManager:
         st = self._segments.get(task.module_name)
         if st is None or st.n_slot == 0:
             return None
-        se = self._slot_experts.get(task.module_name)
-        if se is None:
-            se = self._slot_experts[task.module_name] = st.slot_experts(device)
+        key = (task.module_name, str(torch.device(device)))  # one copy per device (threads per device)
+        with self._slot_lock:
+            se = self._slot_experts.get(key)
+            if se is None:
+                se = self._slot_experts[key] = st.slot_experts(device)
         counts = [st.counts[e] for e in experts]
         S = st.n_slot
         pos = torch.full((st.E,), len(experts), dtype=torch.int64, device=device)

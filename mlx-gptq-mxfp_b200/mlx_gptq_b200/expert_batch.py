@@ -1,0 +1,140 @@
+"""Routed expert batches, sharded over the GPUs of one box.
+
+One MoE layer's experts are independent: expert e's Hessian depends only on the rows
+routed to it, and its solve only on its own H. A batch is therefore partitioned over
+the ranks of a process group (one process per GPU) with no data-path collective until
+the end, where one all-gather per output tensor hands every rank the codes and E8M0
+scales of every expert (what sequential propagation needs). This is the expert split of
+the reference's multi-device mode (mlx_gptq/sequential.py:471-474, 610-626: expert
+spans spread over devices), done with one process per GPU and NCCL.
+
+Inside a rank the expert Hessians are one grouped tcgen05 launch per parameter. A
+routed distribution is skewed (top-k routing with a Zipf bias gives a handful of
+experts nearly every token), so an expert holding most of a rank's rows would leave
+most SM pairs idle: its rows are cut into pieces, each piece is a separate work item
+of the launch (a "virtual expert"), and the pieces are summed afterwards in a fixed
+order. Pieces are laid out first-piece-of-every-expert first, so the summed Hessians
+are a view of the launch's output, not a copy.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from .capture import hessian_grouped, hessian_tile_count, hessian_tiles_per_wave
+from .pipeline import lpt_partition
+
+# Solve cost of one weight element in Hessian units (one token x one C^2 multiply-add):
+# the groupwise MXFP column loop runs ~1.1e11 elements/s on a B200, the Hessian
+# ~8e17 multiply-adds/s, so one element costs about as much as 7,000 Hessian units.
+SOLVE_UNITS_PER_ELEM = 7.0e3
+
+
+def plan_experts(counts, world: int, hess_dims, solve_elems: int) -> list[list[int]]:
+    """Longest-processing-time split of experts over `world` ranks: cost(e) =
+    counts[e] * sum(C^2 over the expert's Hessians) + SOLVE_UNITS_PER_ELEM * elements
+    solved per expert. Returns the sorted expert list of every rank."""
+    per_token = float(sum(c * c for c in hess_dims))
+    costs = [float(n) * per_token + SOLVE_UNITS_PER_ELEM * solve_elems for n in counts]
+    return lpt_partition(costs, world)
+
+
+@dataclass
+class PieceLayout:
+    """Rows of a set of experts cut into pieces for one grouped Hessian launch.
+
+    token_idx: int32 [rows] on the device, the rows of piece v at offsets[v] ..
+    offsets[v + 1]; offsets: int64 [V + 1] on the host. Pieces 0 .. n-1 are the first
+    pieces of experts[0 .. n-1]; extra[j] = (expert position, piece) for the rest.
+    perm: int64 [rows] on the device, token_idx = (the source index array)[perm], so a
+    fresh copy of the same routing can be laid out again with one gather."""
+    token_idx: torch.Tensor
+    offsets: torch.Tensor
+    n: int
+    extra: list[tuple[int, int]]
+    perm: torch.Tensor
+
+
+def piece_layout(token_idx: torch.Tensor, offsets, experts: list[int], c: int, device,
+                 waves: float = 4.0, tiles_per_wave: int | None = None) -> PieceLayout:
+    """Cut the experts' rows (token_idx[offsets[e]:offsets[e+1]]) into pieces of at most
+    P rows, P chosen so that the launch has about `waves` waves of equally long work
+    items (each piece runs hessian_tile_count(c) tiles over its rows; tiles_per_wave
+    defaults to what `device` runs at once)."""
+    off = [int(v) for v in offsets]
+    rows = [off[e + 1] - off[e] for e in experts]
+    tiles = hessian_tile_count(c)
+    slots = (hessian_tiles_per_wave(device) if tiles_per_wave is None else tiles_per_wave) * waves
+    total = sum(rows)
+    cap = max(64, -(-total * tiles // int(max(1, slots)))) if total else 64
+    cap = -(-cap // 64) * 64  # whole 64-row steps per piece
+    first, rest, extra = [], [], []
+    for i, (e, n) in enumerate(zip(experts, rows)):
+        k = max(1, -(-n // cap))
+        bounds = [off[e] + j * n // k for j in range(k + 1)]
+        first.append((bounds[0], bounds[1]))
+        for j in range(1, k):
+            rest.append((bounds[j], bounds[j + 1]))
+            extra.append((i, j))
+    spans = first + rest
+    lens = torch.tensor([b - a for a, b in spans], dtype=torch.int64)
+    new_off = torch.zeros(len(spans) + 1, dtype=torch.int64)
+    new_off[1:] = torch.cumsum(lens, 0)
+    if spans and int(new_off[-1]):
+        perm = torch.cat([torch.arange(a, b, dtype=torch.int64) for a, b in spans if b > a]).to(device)
+        tok = token_idx.index_select(0, perm)
+    else:
+        perm = torch.zeros(0, dtype=torch.int64, device=device)
+        tok = torch.zeros(1, dtype=torch.int32, device=device)
+    return PieceLayout(tok, new_off, len(experts), extra, perm)
+
+
+@torch.no_grad()
+def expert_hessians(X: torch.Tensor, layout: PieceLayout, out: torch.Tensor | None = None) -> torch.Tensor:
+    """H [n, C, C] float32 of the layout's experts: one grouped launch over all pieces,
+    then each expert's extra pieces added to its first, in piece order."""
+    V = layout.offsets.numel() - 1
+    H = hessian_grouped(X, layout.token_idx, layout.offsets, V, H=out)
+    for j, (i, _) in enumerate(layout.extra):
+        H[i].add_(H[layout.n + j])
+    return H[:layout.n]
+
+
+class Exchange:
+    """All-gather of per-rank expert outputs (leading dim = the rank's experts) into
+    expert order on every rank: one padded all_gather_into_tensor per tensor, issued
+    asynchronously so it overlaps the work that follows; wait() reorders."""
+
+    def __init__(self, shares: list[list[int]], rank: int, group, device):
+        self.shares, self.rank, self.group = shares, rank, group
+        self.m = max(len(s) for s in shares)
+        order = [e for s in shares for e in s]
+        self.E = len(order)
+        # position of expert e's slab in the gathered [world * m] buffer
+        slot = []
+        for r, s in enumerate(shares):
+            slot += [r * self.m + i for i in range(len(s))]
+        self.src = torch.tensor(slot, dtype=torch.long, device=device)
+        self.dst = torch.tensor(order, dtype=torch.long, device=device)
+        self.pending = []
+
+    def start(self, t: torch.Tensor, out: torch.Tensor) -> None:
+        """Gather this rank's t [n_r, ...] from every rank into out [E, ...] (expert order)."""
+        import torch.distributed as dist
+
+        world = len(self.shares)
+        pad = t
+        if t.shape[0] != self.m:
+            pad = torch.zeros((self.m,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+            pad[: t.shape[0]].copy_(t)
+        buf = torch.empty((world * self.m,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+        work = dist.all_gather_into_tensor(buf, pad.contiguous(), group=self.group, async_op=True)
+        self.pending.append((work, buf, out, pad))
+
+    def wait(self) -> None:
+        for work, buf, out, _ in self.pending:
+            work.wait()
+            out.index_copy_(0, self.dst, buf.index_select(0, self.src))
+        self.pending = []

@@ -21,10 +21,12 @@ rank 0 writes artifacts). Nothing else crosses ranks.
 
 from __future__ import annotations
 
+import contextlib
 import heapq
 import re
 import threading
 import time
+from concurrent.futures import ThreadPoolExecutor
 from dataclasses import dataclass, field
 
 import torch
@@ -228,9 +230,54 @@ def plan_layer(mgr: CaptureManager, world: int, group=None, device="cpu", per_wa
     return plans, by_stash, ranges
 
 
+def _on(dev: torch.device):
+    """Make `dev` this thread's current CUDA device (no-op for other devices)."""
+    return torch.cuda.device(dev) if dev.type == "cuda" else contextlib.nullcontext()
+
+
+@torch.no_grad()
+def solve_experts_on_devices(mgr: CaptureManager, task: FusedExpertTask, experts: list[int], devices, bits: int,
+                             args: "LayerSolveArgs", timer=None):
+    """One fused task's experts spread over several devices of this process: the
+    reference's multi-device mode (sequential.py:471-474, 610-626, a device queue and
+    one worker thread per device). Experts are split by longest processing time on
+    their routed rows; each device's thread forms its experts' Hessians (one grouped
+    launch) and solves them as one batch; outputs come back to devices[0] and are
+    returned in `experts` order as (q, scales, biases, W_dq, rel_err)."""
+    E, R, C = task.param.shape
+    home = devices[0]
+    costs = [float(mgr.tokens(task.stash_keys[e])) * C * C + SOLVE_COST_PER_ELEM * R * C for e in experts]
+    shares = lpt_partition(costs, len(devices))
+
+    def work(di):
+        dev, sub = devices[di], [experts[i] for i in shares[di]]
+        if not sub:
+            return None
+        with _on(dev):
+            H = mgr.expert_hessians(task, dev, sub)
+            W = task.param.detach()[sub].to(dev)
+            q, s, b, W_dq, rel = _solve_batch(W, H, bits, args)
+            out = tuple(None if t is None else t.to(home) for t in (q, s, b, W_dq.to(task.param.dtype), rel))
+            if dev.type == "cuda":
+                torch.cuda.synchronize(dev)  # the copies to `home` have landed
+        return out
+
+    with ThreadPoolExecutor(max_workers=len(devices), thread_name_prefix="gq-device") as pool:
+        parts = list(pool.map(work, range(len(devices))))
+    if home.type == "cuda":
+        torch.cuda.synchronize(home)
+    order = [experts[i] for share in shares for i in share]
+    pos = torch.tensor([order.index(e) for e in experts], dtype=torch.long, device=home)
+    parts = [p for p in parts if p is not None]
+    cat = [None if parts[0][j] is None else torch.cat([p[j] for p in parts]) for j in range(5)]
+    if timer is not None:
+        timer("expert_solves")
+    return tuple(None if t is None else t.index_select(0, pos) for t in cat)
+
+
 @torch.no_grad()
 def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, device, group=None,
-                on_device: bool = False, dp: bool = False) -> SolveResult:
+                on_device: bool = False, dp: bool = False, devices=None) -> SolveResult:
     """Quantize every task of a captured layer; returns the artifacts (sequential.py:467-635).
 
     dp: the ranks of `group` captured different calibration windows (counts already
@@ -238,10 +285,16 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
     its own rows, expert Hessians reach their owners by one reduce-scatter per fused
     parameter and linear Hessians by one all-reduce per stash. The sums over ranks
     change the fp32 summation order, so the result matches one process within the
-    Hessian tolerance rather than bit for bit."""
+    Hessian tolerance rather than bit for bit.
+
+    devices: several devices of this process (no process group): each fused task's
+    experts are spread over them, one thread per device (solve_experts_on_devices);
+    the plain linears are then solved on `device`, like the reference's serial tail."""
     import torch.distributed as dist
 
     device = torch.device(device)
+    pool = [torch.device(d) for d in (devices or [])]
+    pool = pool if group is None and len(pool) > 1 else None
     result = SolveResult(on_device)
     world = dist.get_world_size(group) if group is not None else 1
     rank = dist.get_rank(group) if group is not None else 0
@@ -299,7 +352,9 @@ def solve_layer(layer_prefix: str, mgr: CaptureManager, args: LayerSolveArgs, de
                 dist.reduce_scatter_tensor(H_dp, H_all, op=dist.ReduceOp.SUM, group=group)
                 del H_all
                 timer("hessian_merge")
-        if mine:
+        if mine and pool is not None:
+            q, s, b, W_dq, rel = solve_experts_on_devices(mgr, task, list(mine), pool, bits, args, timer)
+        elif mine:
             chunk = len(mine) if args.vram_gb is None else expert_chunk_size(C, R, args.vram_gb)
             outs = []
             for i in range(0, len(mine), chunk):

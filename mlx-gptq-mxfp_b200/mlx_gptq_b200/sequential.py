@@ -18,8 +18,10 @@ Differences from the reference, all B200-first:
   * several GPUs are several processes (one per GPU, torch.distributed NCCL):
     every rank runs the same forward, experts and linears are split across ranks
     inside solve_layer, and one all-gather per task returns the quantized
-    weights; rank 0 alone writes artifacts. Within a process the first entry of
-    ``args.devices`` is the device.
+    weights; rank 0 alone writes artifacts;
+  * several devices in one process (``args.devices`` with more than one entry, the
+    reference's own multi-device mode) spread each fused task's experts over the
+    devices, one thread per device; the forward runs on the first device.
 """
 
 from __future__ import annotations
@@ -380,7 +382,8 @@ class Pipeline:
         self.args = args
         self.group = group
         self.dp = bool(dp) and group is not None
-        self.dev0 = torch.device(args.devices[0])
+        self.devices = [torch.device(d) for d in args.devices]
+        self.dev0 = self.devices[0]  # forward device; experts spread over all of self.devices
         self.dtype = torch.bfloat16 if args.dtype == "bfloat16" else torch.float16
         self.storage_dtype = self.dtype
         inner = model
@@ -480,7 +483,8 @@ class Pipeline:
     @torch.no_grad()
     def solve_layer(self, layer_idx: int, mgr: CaptureManager):
         prefix = self.artifact_layers_prefix_fmt.format(layer_idx)
-        return solve_layer(prefix, mgr, self.solve_args(), self.dev0, group=self.group, on_device=True, dp=self.dp)
+        return solve_layer(prefix, mgr, self.solve_args(), self.dev0, group=self.group, on_device=True, dp=self.dp,
+                           devices=self.devices)
 
     @torch.no_grad()
     def apply_precomputed(self, layer, layer_idx: int, reader) -> None:

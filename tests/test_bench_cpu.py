@@ -1,5 +1,5 @@
-"""bench.py helpers that need no GPU: the algorithmic byte count and roofline record of
-the column loops, and the clock-sample filter."""
+"""bench.py helpers that need no GPU: the CPU-sample record, the executed-tile count of
+the Hessian roofline, and the clock-sample filter."""
 
 import os
 import sys
@@ -11,13 +11,18 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 import bench  # noqa: E402
 
 
-def test_column_loop_bytes_and_roofline():
-    per_matrix = 11008 * 4096 * 4.5 + 11008 * 4096 // 32
-    expected = 2 * (per_matrix + 4 * 32 * 4096) + (per_matrix + 4 * 32 * 11008)
-    assert bench.column_loop_bytes() == expected
-    r = bench.column_loop_roofline(2.8, 7000.0, "measured")
-    assert abs(r["achieved"] - expected / 2.8e-3 / 1e9) < 1e-6
-    assert abs(r["frac"] - r["achieved"] / 7000.0) < 1e-12 and r["unit"] == "GB/s"
+def test_cpu_sample_record_reports_what_ran():
+    class Sample:
+        elems = 1000
+
+    rec = bench.cpu_sample_record(Sample(), [2.0, 1.0, 3.0])
+    assert rec["value"] == 1000 / 2.0 and rec["kind"] == "port" and rec["cores"] >= 1
+    assert rec["seconds_per_sample"] == 2.0 and "median of 3 runs" in rec["sample"]
+
+
+def test_hessian_executed_elems_counts_upper_tiles():
+    assert bench.hessian_executed_elems(2048) == 256 * 256 * 36
+    assert bench.hessian_executed_elems(768) == 256 * 256 * 6
 
 
 def test_clock_samples_inside_the_timed_region():

@@ -290,3 +290,41 @@ def test_cli_two_processes(tmp_path, dp):
             a = st.load_file(os.path.join(out1, f"layer_{li:04d}.safetensors"))
             b = st.load_file(os.path.join(out2, f"layer_{li:04d}.safetensors"))
             assert a.keys() == b.keys() and all(torch.equal(a[k], b[k]) for k in a)
+
+
+def test_cli_spreads_experts_over_every_listed_device(tmp_path, monkeypatch):
+    """--devices with several entries in one process (the reference's multi-device mode,
+    sequential.py:471-474, 610-626): every fused task's experts go to a worker thread per
+    device and the artifacts equal a one-device run's. Two host "devices" stand in for
+    GPUs, with the fake solver."""
+    import safetensors.torch as st
+    import test_pipeline_cpu as fakes
+
+    from mlx_gptq_b200 import artifacts, capture, grid, pipeline
+
+    fakes.install_fakes(pipeline, capture, monkeypatch.setattr)
+    for mod, name, fn in ((artifacts, "pack_nibbles", fakes._fake_pack), (artifacts, "unpack_nibbles", fakes._fake_unpack),
+                          (grid, "dequantize_artifact", fakes._fake_dequant)):
+        monkeypatch.setattr(mod, name, fn)
+    calls = []
+    real = pipeline.solve_experts_on_devices
+
+    def spy(mgr, task, experts, devices, *a, **k):
+        calls.append((task.param_name, len(experts), [str(d) for d in devices]))
+        return real(mgr, task, experts, devices, *a, **k)
+
+    monkeypatch.setattr(pipeline, "solve_experts_on_devices", spy)
+    model_dir = write_tiny_checkpoint(str(tmp_path / "model"))
+    toks = tmp_path / "t.npy"
+    np.save(toks, np.random.default_rng(1).integers(0, 512, (4, 32)).astype(np.int64))
+    outs = {}
+    for devs in ("cpu", "cpu,cpu"):
+        out = str(tmp_path / devs.replace(",", "_"))
+        calibrate.main(["--model", model_dir, "--output", out, "--calibration-tokens", str(toks), "--mode", "mxfp4",
+                        "--devices", devs, "--batch-size", "2"])
+        outs[devs] = out
+    assert calls and all(d == ["cpu", "cpu"] and n == 8 for _, n, d in calls)
+    for li in (0, 1):
+        a = st.load_file(os.path.join(outs["cpu"], f"layer_{li:04d}.safetensors"))
+        b = st.load_file(os.path.join(outs["cpu,cpu"], f"layer_{li:04d}.safetensors"))
+        assert sorted(a) == sorted(b) and all(torch.equal(a[k], b[k]) for k in a)

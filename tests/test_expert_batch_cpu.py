@@ -1,0 +1,71 @@
+"""Host-side logic of the sharded expert batch (mlx_gptq_b200.expert_batch), on CPU:
+the LPT expert split, the piece layout of a skewed routing, and the exchange's
+all-gather into expert order across two gloo ranks."""
+
+import os
+
+import pytest
+import torch
+
+
+def test_plan_experts_balances_a_skewed_batch():
+    from mlx_gptq_b200.expert_batch import SOLVE_UNITS_PER_ELEM, plan_experts
+
+    counts = [500_000] * 8 + [100] * 112 + [0] * 8
+    shares = plan_experts(counts, 8, (2048, 768), 4_718_592)
+    assert sorted(e for s in shares for e in s) == list(range(128))
+    per_tok = 2048 ** 2 + 768 ** 2
+    loads = [sum(counts[e] * per_tok + SOLVE_UNITS_PER_ELEM * 4_718_592 for e in s) for s in shares]
+    assert max(loads) <= 1.05 * (sum(loads) / 8)
+    assert all(sum(1 for e in s if counts[e] == 500_000) == 1 for s in shares)  # one heavy expert each
+
+
+def test_piece_layout_cuts_heavy_experts_and_keeps_rows():
+    from mlx_gptq_b200.expert_batch import piece_layout
+
+    counts = [4000, 64, 0, 900]
+    offsets = torch.zeros(5, dtype=torch.int64)
+    offsets[1:] = torch.cumsum(torch.tensor(counts), 0)
+    tok = torch.randperm(sum(counts)).to(torch.int32)
+    lay = piece_layout(tok, offsets, [0, 1, 2, 3], 2048, "cpu", waves=1.0, tiles_per_wave=74)
+    n = lay.offsets.numel() - 1
+    assert lay.n == 4 and n == 4 + len(lay.extra)
+    assert int(lay.offsets[-1]) == sum(counts)
+    # every expert's rows appear exactly once across its pieces
+    pieces = {i: [lay.token_idx[int(lay.offsets[i]):int(lay.offsets[i + 1])]] for i in range(4)}
+    for j, (i, _) in enumerate(lay.extra):
+        pieces[i].append(lay.token_idx[int(lay.offsets[4 + j]):int(lay.offsets[5 + j])])
+    for i, c in enumerate(counts):
+        got = torch.cat(pieces[i]).sort().values
+        want = tok[int(offsets[i]):int(offsets[i + 1])].sort().values
+        assert torch.equal(got, want)
+    assert any(i == 0 for i, _ in lay.extra)  # the heavy expert is cut
+    assert torch.equal(tok.index_select(0, lay.perm), lay.token_idx)
+
+
+def _exchange_rank(rank, world, port, out):
+    import torch.distributed as dist
+
+    from mlx_gptq_b200.expert_batch import Exchange
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    shares = [[0, 3, 4], [1, 2]]
+    ex = Exchange(shares, rank, dist.group.WORLD, "cpu")
+    mine = torch.tensor([[e * 10, e * 10 + 1] for e in shares[rank]], dtype=torch.int32)
+    full = torch.empty(5, 2, dtype=torch.int32)
+    ex.start(mine, full)
+    ex.wait()
+    out[rank] = full.tolist()
+    dist.destroy_process_group()
+
+
+def test_exchange_gathers_into_expert_order():
+    import torch.multiprocessing as mp
+
+    port = 29500 + os.getpid() % 1000
+    with mp.Manager() as m:
+        out = m.dict()
+        mp.spawn(_exchange_rank, args=(2, port, out), nprocs=2, join=True)
+        want = [[e * 10, e * 10 + 1] for e in range(5)]
+        assert out[0] == want and out[1] == want
