@@ -152,8 +152,8 @@ class C3Step:
         self.inp, self.device, self.world = inp, device, world
         n = len(inp.mine)
         self.lay_gu = piece_layout(inp.tok, inp.offsets, list(range(n)), C3_H, device)
-        slots = torch.arange(inp.acts.shape[0], dtype=torch.int32, device=device)
-        self.lay_dn = piece_layout(slots, inp.offsets, list(range(n)), C3_I, device)
+        # down inputs are laid out expert by expert: read in place as spans
+        self.lay_dn = piece_layout(None, inp.offsets, list(range(n)), C3_I, device)
         self.H_gu = torch.empty(self.lay_gu.offsets.numel() - 1, C3_H, C3_H, device=device)
         self.H_dn = torch.empty(self.lay_dn.offsets.numel() - 1, C3_I, C3_I, device=device)
         self.exchange = Exchange(inp.shares, rank, group, device) if world > 1 else None
@@ -168,9 +168,10 @@ class C3Step:
         self.last = None
 
     def launches(self) -> int:
-        """Kernels of this library per step: per parameter the gather pass and the
-        Hessian, dead columns, block factors, column loop, rel_err reduction, and RTN
-        when this rank has experts without tokens."""
+        """Kernels of this library per step: per parameter the row pass (gate_up: the
+        routed-row gather; down: the partial-step tails) and the Hessian, dead columns,
+        block factors, column loop, rel_err reduction, and RTN when this rank has
+        experts without tokens."""
         rtn = 1 if any(c == 0 for c in self.inp.counts_mine) else 0
         return 2 * (2 + 4 + rtn)
 
@@ -738,6 +739,16 @@ def profile_case(case, device):
         show("batched solve (128 experts gate_up, groupwise)",
              lambda: layer.solve_experts(W, H.clone(), r.counts.tolist(), "mxfp4", "groupwise", torch.bfloat16,
                                          True, check_info=False), 3)
+    elif case == "solve-groupwise":
+        X = S.student_t_bf16(8192, 2048, 7, device)
+        H = torch.empty(2048, 2048, device=device)
+        hessian_accumulate(X, H, 1.0, 0.0)
+        W = S.weights_bf16((32, 1536, 2048), 8, device)  # 32 experts' gate_up: 200 MB bf16 in
+        Hb = H.unsqueeze(0).repeat(32, 1, 1)
+        f = layer.mxfp_factors(Hb)
+        show("solve [32, 1536, 2048] groupwise", lambda: layer.solve_mxfp_packed(
+            W, f, "mxfp4", "groupwise", torch.bfloat16, True, check_info=False), 4,
+             lambda ms: f"{W.numel() / ms / 1e6:.2f} G elems/s")
     elif case == "c3-step":
         inp = C3Inputs(device, 0, 1)
         step = C3Step(inp, device, 0, 1)
@@ -958,7 +969,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the other configurations and the pack kernel")
     ap.add_argument("--profile-case", default=None,
-                    choices=["hessian", "hessian-full", "solve", "affine", "moe", "moe-small", "c3-step", "pack"],
+                    choices=["hessian", "hessian-full", "solve", "solve-groupwise", "affine", "moe", "moe-small",
+                             "c3-step", "pack"],
                     help="run a small case of one kernel for an ncu capture and exit")
     ap.add_argument("--config", choices=["c3", "c5"], default="c3",
                     help="c3: the routed expert batch (default); c5: the synthetic Qwen3-MoE layer stack")

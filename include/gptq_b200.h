@@ -114,6 +114,20 @@ int gq_hessian_grouped_bf16(const void* X, int64_t n, int64_t c, int64_t ldx, co
                             const int64_t* offsets, const int64_t* host_offsets, int64_t E, float* H, float alpha,
                             float beta, void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
 
+/* Per-expert Hessians over contiguous row spans, in one launch:
+ * H[e] = beta * H[e] + alpha * X[s_e .. s_e + k_e)^T X[s_e .. s_e + k_e), e < E, with
+ * host_spans[2e] = s_e and host_spans[2e+1] = k_e (host memory; spans may overlap and
+ * come in any order, 0 <= s_e, s_e + k_e <= n). The rows are read in place; only each
+ * expert's partial last 64-row step (k_e % 64 rows, zero-padded) is copied into the
+ * workspace (gq_hessian_spans_workspace_size bytes). Always the 2-SM kernel.
+ * Replaces the per-expert Stash.hessian calls of mlx_gptq/sequential.py:546-555 when
+ * each expert's stash is one contiguous block of rows (capture.py:33-76 stores an
+ * expert's rows as its own chunks), e.g. down_proj inputs laid out expert by expert. */
+size_t gq_hessian_spans_workspace_size(const int64_t* host_spans, int64_t E, int64_t c);
+int gq_hessian_spans_bf16(const void* X, int64_t n, int64_t c, int64_t ldx, const int64_t* host_spans, int64_t E,
+                          float* H, float alpha, float beta, void* workspace, size_t workspace_bytes, int32_t* status,
+                          void* stream);
+
 /* ------------------------------------------------------------------------
  * Solver pieces (mlx_gptq/gptq.py)
  * ------------------------------------------------------------------------ */

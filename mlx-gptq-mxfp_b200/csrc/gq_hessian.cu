@@ -344,11 +344,16 @@ __device__ __forceinline__ void umma_commit_2sm(uint64_t* bar) {
 }
 }  // namespace two
 
+// Span form (span != nullptr): expert e's rows are X[span[2e] .. span[2e] + span[2e+1]),
+// read in place with tiled loads (tmap over X); its partial last 64-row step, if any,
+// comes from a tail buffer (tail_map, rows tail_off[e] .. +63: the remaining rows, then
+// zeros), so a step never reads another expert's rows and nothing is copied but tails.
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
-    hessian2_kernel(const __grid_constant__ CUtensorMap tmap, int64_t n, int64_t c, float* __restrict__ H,
-                    int64_t ldh, float alpha, float beta, int32_t* status, const int32_t* __restrict__ sched,
-                    const int64_t* __restrict__ seg, int64_t tiles_per_expert,
-                    int64_t tile_begin) {
+    hessian2_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap tail_map,
+                    int64_t n, int64_t c, float* __restrict__ H, int64_t ldh, float alpha, float beta,
+                    int32_t* status, const int32_t* __restrict__ sched, const int64_t* __restrict__ seg,
+                    int64_t tiles_per_expert, int64_t tile_begin, const int64_t* __restrict__ span,
+                    const int64_t* __restrict__ tail_off) {
   constexpr int STAGES = two::STAGES;
   constexpr uint32_t STAGE_BYTES = two::STAGE_BYTES, HALF_BYTES = two::HALF_BYTES;
   using two::arrive_remote;
@@ -369,17 +374,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cta_rank();
-  int64_t q = (blockIdx.x >> 1) + tile_begin, y0 = 0;
+  int64_t q = (blockIdx.x >> 1) + tile_begin, y0 = 0, ytail = 0;
   if (sched) {
     const int64_t v = sched[q], e = v / tiles_per_expert;
     q = v % tiles_per_expert;
-    y0 = seg[e];
-    n = seg[e + 1] - y0;
+    if (span) {
+      y0 = span[2 * e];
+      n = span[2 * e + 1];
+      ytail = tail_off[e];
+    } else {
+      y0 = seg[e];
+      n = seg[e + 1] - y0;
+    }
     H += e * c * ldh;
   }
   int64_t tm, tn;
   two::tile_of(q, (c + 255) / 256, tm, tn);
   const int KT = int((n + BK - 1) / BK);
+  const int full_steps = span ? int(n / BK) : KT;  // steps read in place; the rest from the tail buffer
   const int NCH = (KT + kChunkTiles - 1) / kChunkTiles;
 
   if (threadIdx.x == 0) {
@@ -407,6 +419,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap)) : "memory");
+      if (span) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tail_map)) : "memory");
       int issued = 0;
       for (int kt = 0; kt < KT; ++kt) {
         const int s = kt % STAGES;
@@ -414,12 +427,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, status)) break;
         if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * STAGE_BYTES);  // both CTAs' bytes
         uint8_t* st = smem + s * STAGE_BYTES;
-        const int y = int(y0) + kt * BK;
+        const bool tail = kt >= full_steps;
+        const CUtensorMap* m = tail ? &tail_map : &tmap;
+        const int y = tail ? int(ytail) : int(y0) + kt * BK;
         const int xa = int(tm * 256 + rank * 128), xb = int(tn * 256 + rank * 128);
-        tma_load_2sm(st, &tmap, xa, y, &full[s]);
-        tma_load_2sm(st + BOX_BYTES, &tmap, xa + 64, y, &full[s]);
-        tma_load_2sm(st + HALF_BYTES, &tmap, xb, y, &full[s]);
-        tma_load_2sm(st + HALF_BYTES + BOX_BYTES, &tmap, xb + 64, y, &full[s]);
+        tma_load_2sm(st, m, xa, y, &full[s]);
+        tma_load_2sm(st + BOX_BYTES, m, xa + 64, y, &full[s]);
+        tma_load_2sm(st + HALF_BYTES, m, xb, y, &full[s]);
+        tma_load_2sm(st + HALF_BYTES + BOX_BYTES, m, xb + 64, y, &full[s]);
         issued = kt + 1;
       }
       if (*abort_flag && rank == 0) {  // let copies already in flight land before the CTA exits
@@ -569,6 +584,52 @@ __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ X, int64_t 
   }
 }
 
+// Span form: tail slot t (expert tail_expert[t]) gets rows 64t .. 64t+63 = the rows of
+// the expert's partial last step, then zeros.
+__global__ void span_tails_kernel(const __nv_bfloat16* __restrict__ X, int64_t c, int64_t ldx,
+                                  const int64_t* __restrict__ span, const int32_t* __restrict__ tail_expert,
+                                  int64_t rows, __nv_bfloat16* __restrict__ dst) {
+  const int64_t row = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int64_t e = tail_expert[row / BK], i = row % BK;
+  const int64_t cnt = span[2 * e + 1], first = cnt / BK * BK;
+  uint4* d = reinterpret_cast<uint4*>(dst + row * c);
+  const int64_t nvec = c / 8;
+  if (first + i < cnt) {
+    const uint4* src = reinterpret_cast<const uint4*>(X + (span[2 * e] + first + i) * ldx);
+    for (int64_t k = lane; k < nvec; k += 32) d[k] = src[k];
+  } else {
+    for (int64_t k = lane; k < nvec; k += 32) d[k] = make_uint4(0, 0, 0, 0);
+  }
+}
+
+// Span-form plan: tail slots, and the CTA schedule (experts by descending rows).
+struct SpanPlan {
+  std::vector<int64_t> tail_off;     // E: first tail-buffer row (0 when the expert has no tail)
+  std::vector<int32_t> tail_expert;  // tail slot -> expert
+  std::vector<int32_t> sched;
+};
+
+static SpanPlan plan_spans(const int64_t* host_spans, int64_t E, int64_t tpe) {
+  SpanPlan p;
+  p.tail_off.assign(E, 0);
+  std::vector<int64_t> order(E);
+  for (int64_t e = 0; e < E; ++e) {
+    order[e] = e;
+    if (host_spans[2 * e + 1] % BK) {
+      p.tail_off[e] = int64_t(p.tail_expert.size()) * BK;
+      p.tail_expert.push_back(int32_t(e));
+    }
+  }
+  std::stable_sort(order.begin(), order.end(),
+                   [&](int64_t a, int64_t b) { return host_spans[2 * a + 1] > host_spans[2 * b + 1]; });
+  p.sched.reserve(E * tpe);
+  for (int64_t e : order)
+    for (int64_t t = 0; t < tpe; ++t) p.sched.push_back(int32_t(e * tpe + t));
+  return p;
+}
+
 struct GroupedPlan {
   std::vector<int64_t> seg;     // E + 1 padded row starts
   std::vector<int32_t> sched;   // one entry per CTA
@@ -604,12 +665,14 @@ static int64_t tiles_for(int64_t c, bool two_sm) { return two_sm ? two::tiles(c)
 
 static int launch(const CUtensorMap& map, int64_t n, int64_t c, float* H, int64_t ldh, float alpha, float beta,
                   int32_t* status, const int32_t* sched, const int64_t* seg, int64_t tpe, int64_t units,
-                  bool two_sm, cudaStream_t s, int64_t tile_begin = 0) {
+                  bool two_sm, cudaStream_t s, int64_t tile_begin = 0, const CUtensorMap* tail_map = nullptr,
+                  const int64_t* span = nullptr, const int64_t* tail_off = nullptr) {
   if (two_sm) {
     GQ_CUDA_TRY(cudaFuncSetAttribute(hessian2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      int(two::SMEM_BYTES)));
-    hessian2_kernel<<<unsigned(2 * units), THREADS, two::SMEM_BYTES, s>>>(map, n, c, H, ldh, alpha, beta, status,
-                                                                         sched, seg, tpe, tile_begin);
+    hessian2_kernel<<<unsigned(2 * units), THREADS, two::SMEM_BYTES, s>>>(
+        map, tail_map ? *tail_map : map, n, c, H, ldh, alpha, beta, status, sched, seg, tpe, tile_begin, span,
+        tail_off);
     return check_launch("hessian2_kernel");
   }
   GQ_CUDA_TRY(cudaFuncSetAttribute(hessian_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(SMEM_BYTES)));
@@ -712,4 +775,69 @@ extern "C" int gq_hessian_bf16(const void* X, int64_t n, int64_t c, int64_t ldx,
                                float beta, int32_t* status, void* stream) {
   GQ_REQUIRE(c > 0, "gq_hessian_bf16: sizes");
   return gq_hessian_bf16_range(X, n, c, ldx, H, ldh, alpha, beta, 0, gq_hessian_tile_count(c), status, stream);
+}
+
+static size_t spans_tail_bytes(const int64_t* host_spans, int64_t E, int64_t c) {
+  int64_t tails = 0;
+  for (int64_t e = 0; e < E; ++e) tails += host_spans[2 * e + 1] % 64 ? 1 : 0;
+  return align256(size_t(std::max<int64_t>(tails, 1)) * 64 * size_t(c) * 2);
+}
+
+extern "C" size_t gq_hessian_spans_workspace_size(const int64_t* host_spans, int64_t E, int64_t c) {
+  if (!host_spans || E <= 0 || c <= 0) return 0;
+  return spans_tail_bytes(host_spans, E, c) + align256(size_t(E) * 16) + 2 * align256(size_t(E) * 8) +
+         align256(size_t(E) * size_t(gq::hess::two::tiles(c)) * 4);
+}
+
+extern "C" int gq_hessian_spans_bf16(const void* X, int64_t n, int64_t c, int64_t ldx, const int64_t* host_spans,
+                                    int64_t E, float* H, float alpha, float beta, void* workspace,
+                                    size_t workspace_bytes, int32_t* status, void* stream) {
+  GQ_REQUIRE(H && host_spans && E > 0, "gq_hessian_spans_bf16: null pointer or E <= 0");
+  GQ_REQUIRE(c > 0 && c % 8 == 0 && ldx >= c && ldx % 8 == 0, "gq_hessian_spans_bf16: c, ldx must be multiples of 8");
+  GQ_REQUIRE(aligned16(H), "gq_hessian_spans_bf16: H must be 16-byte aligned");
+  GQ_REQUIRE(n >= 0 && n < (int64_t(1) << 31), "gq_hessian_spans_bf16: n");
+  int64_t rows = 0;
+  for (int64_t e = 0; e < E; ++e) {
+    const int64_t a = host_spans[2 * e], k = host_spans[2 * e + 1];
+    GQ_REQUIRE(a >= 0 && k >= 0 && a + k <= n, "gq_hessian_spans_bf16: span %lld = [%lld, +%lld) outside [0, %lld)",
+               (long long)e, (long long)a, (long long)k, (long long)n);
+    rows += k;
+  }
+  const size_t need = gq_hessian_spans_workspace_size(host_spans, E, c);
+  GQ_REQUIRE(workspace && workspace_bytes >= need && aligned16(workspace),
+             "gq_hessian_spans_bf16: workspace too small (%zu < %zu)", workspace_bytes, need);
+  GQ_REQUIRE(rows == 0 || (X && aligned16(X)), "gq_hessian_spans_bf16: X");
+  const int64_t tpe = hess::two::tiles(c);
+  GQ_REQUIRE(E * tpe < (int64_t(1) << 31), "gq_hessian_spans_bf16: too many experts");
+  hess::SpanPlan plan = hess::plan_spans(host_spans, E, tpe);
+  const int64_t tails = int64_t(plan.tail_expert.size());
+  cudaStream_t s = (cudaStream_t)stream;
+  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  __nv_bfloat16* tail_buf = reinterpret_cast<__nv_bfloat16*>(ws);
+  ws += spans_tail_bytes(host_spans, E, c);
+  int64_t* span = reinterpret_cast<int64_t*>(ws);
+  ws += align256(size_t(E) * 16);
+  int64_t* tail_off = reinterpret_cast<int64_t*>(ws);
+  ws += align256(size_t(E) * 8);
+  int32_t* tail_expert = reinterpret_cast<int32_t*>(ws);
+  ws += align256(size_t(E) * 8);
+  int32_t* sched = reinterpret_cast<int32_t*>(ws);
+  GQ_CUDA_TRY(cudaMemcpyAsync(span, host_spans, size_t(E) * 16, cudaMemcpyHostToDevice, s));
+  GQ_CUDA_TRY(cudaMemcpyAsync(tail_off, plan.tail_off.data(), size_t(E) * 8, cudaMemcpyHostToDevice, s));
+  GQ_CUDA_TRY(cudaMemcpyAsync(sched, plan.sched.data(), plan.sched.size() * 4, cudaMemcpyHostToDevice, s));
+  if (tails > 0) {
+    GQ_CUDA_TRY(cudaMemcpyAsync(tail_expert, plan.tail_expert.data(), size_t(tails) * 4, cudaMemcpyHostToDevice, s));
+    hess::span_tails_kernel<<<unsigned((tails * 64 + 7) / 8), 256, 0, s>>>(
+        reinterpret_cast<const __nv_bfloat16*>(X), c, ldx, span, tail_expert, tails * 64, tail_buf);
+    int st = check_launch("span_tails_kernel");
+    if (st != GQ_OK) return st;
+  }
+  // a map needs at least one row: with no rows at all every CTA has KT == 0
+  CUtensorMap xmap, tmap;
+  int st = hess::make_x_map(&xmap, rows > 0 ? X : workspace, rows > 0 ? n : 1, c, rows > 0 ? ldx : c);
+  if (st != GQ_OK) return st;
+  st = hess::make_x_map(&tmap, tail_buf, std::max<int64_t>(tails, 1) * 64, c, c);
+  if (st != GQ_OK) return st;
+  return hess::launch(xmap, 0, c, H, c, alpha, beta, status, sched, nullptr, tpe, int64_t(plan.sched.size()), true,
+                      s, 0, &tmap, span, tail_off);
 }

@@ -118,6 +118,30 @@ def hessian_grouped(X: torch.Tensor, token_idx: torch.Tensor, offsets: torch.Ten
     return H
 
 
+@torch.no_grad()
+def hessian_spans(X: torch.Tensor, spans, H: torch.Tensor | None = None, alpha: float = 1.0,
+                  beta: float = 0.0) -> torch.Tensor:
+    """Per-expert H[e] = beta*H[e] + alpha * X[a:a+k]^T X[a:a+k] for spans[e] = (a, k), in one
+    launch, reading the rows in place (an expert's stash as one contiguous block of
+    rows). X: bf16 [n, c] on a CUDA device. Returns H float32 [E, c, c]."""
+    L.require_cuda(X)
+    if X.dtype != torch.bfloat16 or X.dim() != 2:
+        raise ValueError("X must be bfloat16 [n, c]")
+    if X.stride(1) != 1 or X.stride(0) % 8 or X.data_ptr() % 16:
+        X = X.contiguous()
+    n, c = X.shape
+    sp = torch.tensor([[int(a), int(k)] for a, k in spans], dtype=torch.int64).reshape(-1, 2).contiguous()
+    E = sp.shape[0]
+    if H is None:
+        H = torch.empty(E, c, c, dtype=torch.float32, device=X.device)
+    lib = L.lib()
+    ws = torch.empty(lib.gq_hessian_spans_workspace_size(sp.data_ptr(), E, c), dtype=torch.uint8, device=X.device)
+    L.check(lib.gq_hessian_spans_bf16(L.ptr(X), n, c, X.stride(0), sp.data_ptr(), E, L.ptr(H), float(alpha),
+                                      float(beta), L.ptr(ws), ws.numel(), L.ptr(L.status_word(X.device)),
+                                      L.stream_ptr(X.device)), "hessian_spans")
+    return H
+
+
 class Stash:
     """Captured input rows for one logical weight matrix (capture.py:33-79)."""
 

@@ -23,7 +23,7 @@ from dataclasses import dataclass
 
 import torch
 
-from .capture import hessian_grouped, hessian_tile_count, hessian_tiles_per_wave
+from .capture import hessian_grouped, hessian_spans, hessian_tile_count, hessian_tiles_per_wave
 from .pipeline import lpt_partition
 
 # Solve cost of one weight element in Hessian units (one token x one C^2 multiply-add):
@@ -45,24 +45,28 @@ def plan_experts(counts, world: int, hess_dims, solve_elems: int) -> list[list[i
 class PieceLayout:
     """Rows of a set of experts cut into pieces for one grouped Hessian launch.
 
-    token_idx: int32 [rows] on the device, the rows of piece v at offsets[v] ..
-    offsets[v + 1]; offsets: int64 [V + 1] on the host. Pieces 0 .. n-1 are the first
-    pieces of experts[0 .. n-1]; extra[j] = (expert position, piece) for the rest.
-    perm: int64 [rows] on the device, token_idx = (the source index array)[perm], so a
-    fresh copy of the same routing can be laid out again with one gather."""
-    token_idx: torch.Tensor
-    offsets: torch.Tensor
+    Pieces 0 .. n-1 are the first pieces of experts[0 .. n-1]; extra[j] = (expert
+    position, piece) for the rest (piece n + j). Gather form (rows named by token ids):
+    token_idx int32 [rows] on the device, the rows of piece v at offsets[v] ..
+    offsets[v + 1] (offsets int64 [V + 1] on the host), and perm int64 [rows] on the
+    device with token_idx = (the source index array)[perm], so a fresh copy of the same
+    routing is laid out again with one gather. Span form (each expert's rows one
+    contiguous block of X): spans[v] = (first row, rows) of piece v, read in place."""
     n: int
     extra: list[tuple[int, int]]
-    perm: torch.Tensor
+    offsets: torch.Tensor
+    token_idx: torch.Tensor | None = None
+    perm: torch.Tensor | None = None
+    spans: list[tuple[int, int]] | None = None
 
 
-def piece_layout(token_idx: torch.Tensor, offsets, experts: list[int], c: int, device,
+def piece_layout(token_idx: torch.Tensor | None, offsets, experts: list[int], c: int, device,
                  waves: float = 4.0, tiles_per_wave: int | None = None) -> PieceLayout:
-    """Cut the experts' rows (token_idx[offsets[e]:offsets[e+1]]) into pieces of at most
-    P rows, P chosen so that the launch has about `waves` waves of equally long work
-    items (each piece runs hessian_tile_count(c) tiles over its rows; tiles_per_wave
-    defaults to what `device` runs at once)."""
+    """Cut the experts' rows into pieces of at most P rows, P chosen so that the launch
+    has about `waves` waves of equally long work items (each piece runs
+    hessian_tile_count(c) tiles over its rows; tiles_per_wave defaults to what `device`
+    runs at once). Expert e's rows are token_idx[offsets[e]:offsets[e+1]] (gather
+    form) or, with token_idx None, rows offsets[e] .. offsets[e+1] of X (span form)."""
     off = [int(v) for v in offsets]
     rows = [off[e + 1] - off[e] for e in experts]
     tiles = hessian_tile_count(c)
@@ -82,13 +86,15 @@ def piece_layout(token_idx: torch.Tensor, offsets, experts: list[int], c: int, d
     lens = torch.tensor([b - a for a, b in spans], dtype=torch.int64)
     new_off = torch.zeros(len(spans) + 1, dtype=torch.int64)
     new_off[1:] = torch.cumsum(lens, 0)
+    if token_idx is None:
+        return PieceLayout(len(experts), extra, new_off, spans=[(a, b - a) for a, b in spans])
     if spans and int(new_off[-1]):
         perm = torch.cat([torch.arange(a, b, dtype=torch.int64) for a, b in spans if b > a]).to(device)
         tok = token_idx.index_select(0, perm)
     else:
         perm = torch.zeros(0, dtype=torch.int64, device=device)
         tok = torch.zeros(1, dtype=torch.int32, device=device)
-    return PieceLayout(tok, new_off, len(experts), extra, perm)
+    return PieceLayout(len(experts), extra, new_off, token_idx=tok, perm=perm)
 
 
 @torch.no_grad()
@@ -96,7 +102,10 @@ def expert_hessians(X: torch.Tensor, layout: PieceLayout, out: torch.Tensor | No
     """H [n, C, C] float32 of the layout's experts: one grouped launch over all pieces,
     then each expert's extra pieces added to its first, in piece order."""
     V = layout.offsets.numel() - 1
-    H = hessian_grouped(X, layout.token_idx, layout.offsets, V, H=out)
+    if layout.spans is not None:
+        H = hessian_spans(X, layout.spans, H=out)
+    else:
+        H = hessian_grouped(X, layout.token_idx, layout.offsets, V, H=out)
     for j, (i, _) in enumerate(layout.extra):
         H[i].add_(H[layout.n + j])
     return H[:layout.n]

@@ -69,3 +69,19 @@ def test_exchange_gathers_into_expert_order():
         mp.spawn(_exchange_rank, args=(2, port, out), nprocs=2, join=True)
         want = [[e * 10, e * 10 + 1] for e in range(5)]
         assert out[0] == want and out[1] == want
+
+
+def test_span_layout_covers_each_expert_once():
+    from mlx_gptq_b200.expert_batch import piece_layout
+
+    counts = [5000, 10, 0, 700, 64]
+    offsets = torch.zeros(6, dtype=torch.int64)
+    offsets[1:] = torch.cumsum(torch.tensor(counts), 0)
+    lay = piece_layout(None, offsets, [0, 1, 2, 3, 4], 768, "cpu", waves=1.0, tiles_per_wave=74)
+    assert lay.token_idx is None and lay.spans is not None and len(lay.spans) == 5 + len(lay.extra)
+    rows = {i: [lay.spans[i]] for i in range(5)}
+    for j, (i, _) in enumerate(lay.extra):
+        rows[i].append(lay.spans[5 + j])
+    for i, c in enumerate(counts):
+        covered = sorted(r for a, k in rows[i] for r in range(a, a + k))
+        assert covered == list(range(int(offsets[i]), int(offsets[i]) + c))

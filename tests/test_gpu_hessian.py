@@ -170,3 +170,26 @@ def test_hessian_tile_ranges_compose_bit_exact(parts, c):
     assert torch.equal(total, full)
     with pytest.raises(ValueError):
         hessian_accumulate(X, full, 1.0, 0.0, tiles=(0, T + 1))
+
+
+@pytest.mark.parametrize("c", [96, 768, 2048])
+def test_hessian_spans_match_per_expert_dense(c):
+    """Span form (rows read in place, partial last steps from the tail buffer) == the
+    dense kernel on each span's rows, bit for bit: odd lengths, an empty span, a span
+    of exactly 64 rows, overlapping and unordered spans; beta accumulates."""
+    from mlx_gptq_b200 import hessian_from_rows
+    from mlx_gptq_b200.capture import hessian_spans
+
+    g = torch.Generator(device="cuda").manual_seed(c)
+    X = (torch.randn(5000, c, generator=g, device="cuda") * 3.0).to(torch.bfloat16)
+    spans = [(0, 1000), (1000, 37), (1037, 0), (1100, 64), (40, 3900), (4999, 1), (2000, 2999)]
+    H = hessian_spans(X, spans)
+    for e, (a, k) in enumerate(spans):
+        if k == 0:
+            assert int(torch.count_nonzero(H[e])) == 0
+            continue
+        assert torch.equal(H[e], hessian_from_rows(X[a:a + k])), (c, e)
+    H2 = hessian_spans(X, spans, H=H.clone(), alpha=1.0, beta=1.0)
+    torch.testing.assert_close(H2, 2.0 * H, rtol=0, atol=0)
+    with pytest.raises(ValueError):
+        hessian_spans(X, [(4990, 20)])  # past the last row
