@@ -216,6 +216,74 @@ __device__ __forceinline__ float quad32(const float (&e)[32], float* S, const ui
   return o0 + o1;
 }
 
+// e^T H_g e for the 32 rows of a warp whose error vectors the lanes have already
+// written, column-major, into Se (Se[c * kES + lane] = e[c] of the lane's row). Y = E * H_g
+// comes from the same 3xTF32 mma.sync products as quad32; each lane then multiplies its
+// Y fragments by the matching E entries (rows g, g+8, g+16, g+24 of its quad), the four
+// lanes of a quad sum their partials, and each row's total is sent to the row's lane.
+// No staging area for Y and no e[] in registers.
+__device__ __forceinline__ float quad32_staged(const float* Se, const uint32_t* Hhi, const uint32_t* Hlo, int lane) {
+  __syncwarp();
+  const int g = lane >> 2, tq = lane & 3;
+  float acc[2][4][4];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) acc[mt][nt][0] = acc[mt][nt][1] = acc[mt][nt][2] = acc[mt][nt][3] = 0.0f;
+#pragma unroll
+  for (int kt = 0; kt < 4; ++kt) {
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      const float* ec = Se + (8 * kt + tq) * kES + 16 * mt + g;
+      const float av[4] = {ec[0], ec[8], ec[4 * kES], ec[4 * kES + 8]};
+      uint32_t ahi[4], alo[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        ahi[i] = to_tf32(av[i]);
+        alo[i] = to_tf32(av[i] - __uint_as_float(ahi[i]));
+      }
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        const int o0 = (8 * kt + tq) * kES + 8 * nt + g, o1 = o0 + 4 * kES;
+        mma_tf32(acc[mt][nt], ahi, Hhi[o0], Hhi[o1]);
+        mma_tf32(acc[mt][nt], ahi, Hlo[o0], Hlo[o1]);
+        mma_tf32(acc[mt][nt], alo, Hhi[o0], Hhi[o1]);
+      }
+    }
+  }
+  // acc[mt][nt] = Y[16mt+g][8nt+2tq], Y[16mt+g][8nt+2tq+1], Y[16mt+g+8][8nt+2tq], Y[16mt+g+8][8nt+2tq+1]
+  float part[4];  // rows g, g+8, g+16, g+24
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt) {
+    float lo = 0.0f, hi = 0.0f;
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      const int col = 8 * nt + 2 * tq, row = 16 * mt + g;
+      lo = fmaf(acc[mt][nt][0], Se[col * kES + row], lo);
+      lo = fmaf(acc[mt][nt][1], Se[(col + 1) * kES + row], lo);
+      hi = fmaf(acc[mt][nt][2], Se[col * kES + row + 8], hi);
+      hi = fmaf(acc[mt][nt][3], Se[(col + 1) * kES + row + 8], hi);
+    }
+    part[2 * mt] = lo;
+    part[2 * mt + 1] = hi;
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    part[i] += __shfl_xor_sync(0xFFFFFFFFu, part[i], 1);
+    part[i] += __shfl_xor_sync(0xFFFFFFFFu, part[i], 2);
+  }
+  // row r = 8 * (r >> 3) + (r & 7): held as part[r >> 3] by lanes 4 * (r & 7) .. + 3
+  const int src = 4 * (lane & 7), which = lane >> 3;
+  float v = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float x = __shfl_sync(0xFFFFFFFFu, part[i], src);
+    v = which == i ? x : v;
+  }
+  __syncwarp();  // Se is rewritten by the next call
+  return v;
+}
+
 // Grid value (without the scale) of w * inv for the mode.
 template <int MODE>
 __device__ __forceinline__ float mx_round(float w, float inv) {
@@ -292,16 +360,29 @@ template <int MODE> struct Codes {
   }
 };
 
+// Grid values (without the scale) of a code pair as stored in Codes.
+template <int MODE>
+__device__ __forceinline__ float2 code_pair_values(uint32_t pair) {
+  return MODE == GQ_MXFP4 ? e2m1x2_to_f32(pair) : e4m3x2_to_f32(pair);
+}
+
+// One thread per weight row, one CTA per (32-column group, 128-row tile, batch item).
+// Registers hold the row's 32 original values and the 32 working values of the GPTQ
+// pass; codes are packed as they are produced and every grid value is read back from
+// its code (exact: the codes are the hardware casts of on-grid values), so no grid
+// value or error array is kept. Error vectors for the objectives go straight to the
+// warp's shared-memory staging area.
 template <int MODE, bool SAFE, typename Tin, typename Tout>
-__global__ void __launch_bounds__(128, 3) mx_gptq_kernel(const Tin* __restrict__ W, const float* __restrict__ H,
+__global__ void __launch_bounds__(128, SAFE ? 3 : 4) mx_gptq_kernel(const Tin* __restrict__ W, const float* __restrict__ H,
                                                       const float* __restrict__ U, const uint8_t* __restrict__ dead,
                                                       const int32_t* __restrict__ info, int64_t R, int64_t C,
                                                       uint8_t* __restrict__ q, uint8_t* __restrict__ qp,
                                                       uint8_t* __restrict__ scales, Tout* __restrict__ wdq,
                                                       float* __restrict__ partials, int64_t partials_cap) {
-  __shared__ __align__(16) uint32_t Hhi[32 * kES], Hlo[32 * kES];  // tf32 split of H_g
+  constexpr int kStageFloats = SAFE ? 32 * kES : 1;
+  __shared__ __align__(16) uint32_t Hhi[SAFE ? 32 * kES : 1], Hlo[SAFE ? 32 * kES : 1];  // tf32 split of H_g
   __shared__ __align__(16) float Us[32][32];
-  __shared__ __align__(16) float Sst[4][32 * kES];  // per-warp staging for quad32
+  __shared__ __align__(16) float Se[4][kStageFloats];  // per-warp error vectors (column-major)
   __shared__ float red[2][4];
   __shared__ uint32_t s_dmask;
   const int64_t G = C / 32;
@@ -315,15 +396,17 @@ __global__ void __launch_bounds__(128, 3) mx_gptq_kernel(const Tin* __restrict__
     if (p_out && tid == 0) p_out[0] = p_out[1] = 0.0f;  // rel_err then ignores this group
     return;
   }
-  const float* Hg = H + (b * C + g * 32) * C + g * 32;
   const float* Ug = U + (b * G + g) * 1024;
-  for (int i = tid; i < 1024; i += 128) {
-    const float h = Hg[int64_t(i >> 5) * C + (i & 31)];
-    const uint32_t hi = to_tf32(h);
-    Hhi[(i >> 5) * kES + (i & 31)] = hi;
-    Hlo[(i >> 5) * kES + (i & 31)] = to_tf32(h - __uint_as_float(hi));
-    Us[i >> 5][i & 31] = Ug[i];
+  if (SAFE) {
+    const float* Hg = H + (b * C + g * 32) * C + g * 32;
+    for (int i = tid; i < 1024; i += 128) {
+      const float h = Hg[int64_t(i >> 5) * C + (i & 31)];
+      const uint32_t hi = to_tf32(h);
+      Hhi[(i >> 5) * kES + (i & 31)] = hi;
+      Hlo[(i >> 5) * kES + (i & 31)] = to_tf32(h - __uint_as_float(hi));
+    }
   }
+  for (int i = tid; i < 1024; i += 128) Us[i >> 5][i & 31] = Ug[i];
   if (tid < 32) {
     const bool d = dead ? dead[b * C + g * 32 + tid] != 0 : false;
     const uint32_t m = __ballot_sync(0xFFFFFFFFu, d);
@@ -333,7 +416,7 @@ __global__ void __launch_bounds__(128, 3) mx_gptq_kernel(const Tin* __restrict__
   const uint32_t dmask = s_dmask;
   const int64_t r = tile * 128 + tid;
   const int lane = tid & 31;
-  float* stage = Sst[tid >> 5];
+  float* se = Se[tid >> 5];
   float num = 0.0f, den = 0.0f;
   const bool active = r < R;  // rows past R run on zeros (the objectives need whole warps)
   {
@@ -368,10 +451,9 @@ __global__ void __launch_bounds__(128, 3) mx_gptq_kernel(const Tin* __restrict__
         int e = e0 + d;
         e = e < -127 ? -127 : (e > 127 ? 127 : e);
         const float sc = exp2i(e), inv = exp2i(-e);
-        float err[32];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) err[c] = mx_round<MODE>(o[c], inv) * sc - o[c];
-        const float obj = quad32(err, stage, Hhi, Hlo, lane);
+        for (int c = 0; c < 32; ++c) se[c * kES + lane] = mx_round<MODE>(o[c], inv) * sc - o[c];
+        const float obj = quad32_staged(se, Hhi, Hlo, lane);
         if (t == 0 || obj < best_obj) {
           best_obj = obj;
           best_e = e;
@@ -379,80 +461,89 @@ __global__ void __launch_bounds__(128, 3) mx_gptq_kernel(const Tin* __restrict__
       }
     }
     const float sc = exp2i(best_e), inv = exp2i(-best_e);
+    const float limit = fmaxf(amax * 32.0f, 1.1754943508222875e-38f);  // range guard bound
 
-    // sequential GPTQ over the 32 columns with the fixed scale. After column c is
-    // quantized, wv[c] is reused for its error dq[c] - o[c].
-    float wv[32], gv[32];  // gv: grid values (dq = gv * sc) of the GPTQ pass
+    // sequential GPTQ over the 32 columns with the fixed scale: codes packed as they
+    // are produced (pairs), the range guard tracked on the way; after column c is
+    // quantized wv[c] holds its error dq[c] - o[c] (the GPTQ objective's vector)
+    Codes<MODE> code;
+    code.clear();
+    bool valid = true;
+    float wv[32];
 #pragma unroll
     for (int c = 0; c < 32; ++c) wv[c] = o[c];
+    float gprev = 0.0f;
 #pragma unroll
     for (int c = 0; c < 32; ++c) {
-      gv[c] = mx_round<MODE>(wv[c], inv);
-      const float dq = gv[c] * sc;
+      const float gvc = mx_round<MODE>(wv[c], inv);
+      const float dq = gvc * sc;
+      valid = valid && (fabsf(dq) <= limit);
       const float err = (wv[c] - dq) / Us[c][c];
 #pragma unroll
       for (int k = c + 1; k < 32; ++k) wv[k] = wv[k] - err * Us[c][k];
       wv[c] = dq - o[c];
+      if (c & 1) code.put2(c - 1, MODE == GQ_MXFP4 ? cvt_e2m1x2(gprev, gvc) : cvt_e4m3x2(gprev, gvc));
+      gprev = gvc;
     }
     bool use_gptq = true;
-    if (SAFE) use_gptq = quad32(wv, stage, Hhi, Hlo, lane) <= best_obj;
-    // range guard: |dq| <= max(32 * max|w|, 2^-126), else the RTN baseline
-    const float limit = fmaxf(amax * 32.0f, 1.1754943508222875e-38f);
-    if (use_gptq) {
-      bool valid = true;
+    if (SAFE) {
 #pragma unroll
-      for (int c = 0; c < 32; ++c) valid = valid && (fabsf(gv[c] * sc) <= limit);
-      use_gptq = valid;
+      for (int c = 0; c < 32; ++c) se[c * kES + lane] = wv[c];
+      use_gptq = quad32_staged(se, Hhi, Hlo, lane) <= best_obj;
     }
+    use_gptq = use_gptq && valid;
     if (!use_gptq) {  // baseline: RTN with the chosen scale
+      code.clear();
 #pragma unroll
-      for (int c = 0; c < 32; ++c) gv[c] = mx_round<MODE>(o[c], inv);
-    }
-    // codes of the grid values: the hardware cast of an on-grid value is exact and
-    // the sign of zero already follows the reference
-    Codes<MODE> code;
-    code.clear();
-    float gdq[32];
-#pragma unroll
-    for (int c = 0; c < 32; c += 2) {
-      code.put2(c, MODE == GQ_MXFP4 ? cvt_e2m1x2(gv[c], gv[c + 1]) : cvt_e4m3x2(gv[c], gv[c + 1]));
-      gdq[c] = gv[c] * sc;
-      gdq[c + 1] = gv[c + 1] * sc;
+      for (int c = 0; c < 32; c += 2) {
+        const float g0 = mx_round<MODE>(o[c], inv), g1 = mx_round<MODE>(o[c + 1], inv);
+        code.put2(c, MODE == GQ_MXFP4 ? cvt_e2m1x2(g0, g1) : cvt_e4m3x2(g0, g1));
+      }
     }
     // outputs (active rows only)
     if (active) {
-    if (q) {
-      uint32_t qw[8];
-      if (MODE == GQ_MXFP4) {
+      if (q) {
+        uint32_t qw[8];
+        if (MODE == GQ_MXFP4) {
 #pragma unroll
-        for (int w = 0; w < 8; ++w) {
-          const uint32_t n = (code.w[w >> 1] >> (16 * (w & 1))) & 0xFFFFu;
-          qw[w] = (n & 0xFu) | ((n & 0xF0u) << 4) | ((n & 0xF00u) << 8) | ((n & 0xF000u) << 12);
+          for (int w = 0; w < 8; ++w) {
+            const uint32_t nb = (code.w[w >> 1] >> (16 * (w & 1))) & 0xFFFFu;
+            qw[w] = (nb & 0xFu) | ((nb & 0xF0u) << 4) | ((nb & 0xF00u) << 8) | ((nb & 0xF000u) << 12);
+          }
+        } else {
+#pragma unroll
+          for (int w = 0; w < 8; ++w) qw[w] = code.w[w];
         }
-      } else {
-#pragma unroll
-        for (int w = 0; w < 8; ++w) qw[w] = code.w[w];
+        uint4* qd = reinterpret_cast<uint4*>(q + off);
+        qd[0] = make_uint4(qw[0], qw[1], qw[2], qw[3]);
+        qd[1] = make_uint4(qw[4], qw[5], qw[6], qw[7]);
       }
-      uint4* qd = reinterpret_cast<uint4*>(q + off);
-      qd[0] = make_uint4(qw[0], qw[1], qw[2], qw[3]);
-      qd[1] = make_uint4(qw[4], qw[5], qw[6], qw[7]);
-    }
-    if (MODE == GQ_MXFP4 && qp)
-      *reinterpret_cast<uint4*>(qp + off / 2) = make_uint4(code.w[0], code.w[1], code.w[2], code.w[3]);
-    scales[(b * R + r) * G + g] = uint8_t(best_e + 127);
-    if (wdq) store_row32<Tout>(wdq + off, gdq);
-    if (partials) {
-      if (dmask) {  // dead columns: compare against the raw weights
+      if (MODE == GQ_MXFP4 && qp)
+        *reinterpret_cast<uint4*>(qp + off / 2) = make_uint4(code.w[0], code.w[1], code.w[2], code.w[3]);
+      scales[(b * R + r) * G + g] = uint8_t(best_e + 127);
+      if (dmask && partials) {  // dead columns: rel_err compares against the raw weights
 #pragma unroll
         for (int c = 0; c < 32; ++c)
           if (dmask & (1u << c)) o[c] = to_f32<Tin>(W[off + c]);
       }
+      // dequantized values pair by pair from the codes: W_dq and the rel_err numerator
+      float gdq[32];
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const float d = gdq[c] - o[c];
-        num = fmaf(d, d, num);
+      for (int c = 0; c < 32; c += 2) {
+        const uint32_t pair = MODE == GQ_MXFP4 ? (code.w[c >> 3] >> (4 * (c & 7))) & 0xFFu
+                                               : (code.w[c >> 2] >> (8 * (c & 3))) & 0xFFFFu;
+        const float2 v = code_pair_values<MODE>(pair);
+        gdq[c] = v.x * sc;
+        gdq[c + 1] = v.y * sc;
       }
-    }
+      if (wdq) store_row32<Tout>(wdq + off, gdq);
+      if (partials) {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const float d = gdq[c] - o[c];
+          num = fmaf(d, d, num);
+        }
+      }
     }  // active
   }
   if (partials) {
