@@ -103,6 +103,65 @@ __global__ void pack_q_kernel(const uint8_t* __restrict__ q, int64_t nwords, int
   words[i] = w;
 }
 
+// Vectorized forms (q and the output 16-byte aligned): every thread turns 16 x BITS/2
+// code bytes into four words (one 16-byte store), or 16 codes into 8 nibble bytes and
+// back; the scalar kernels above finish any remainder.
+template <int BITS>
+__device__ __forceinline__ uint32_t pack_word(const uint8_t* b) {  // 32/BITS codes, LSB first
+  constexpr int per = 32 / BITS;
+  constexpr uint32_t mask = (1u << BITS) - 1u;
+  uint32_t w = 0;
+#pragma unroll
+  for (int k = 0; k < per; ++k) w |= (uint32_t(b[k]) & mask) << (BITS * k);
+  return w;
+}
+
+template <int BITS>
+__global__ void pack_q_vec_kernel(const uint4* __restrict__ q, int64_t nquads, uint4* __restrict__ words) {
+  constexpr int per = 32 / BITS, loads = per / 4;  // uint4 loads per 4 output words
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= nquads) return;
+  uint4 in[loads];
+#pragma unroll
+  for (int l = 0; l < loads; ++l) in[l] = q[i * loads + l];
+  const uint8_t* b = reinterpret_cast<const uint8_t*>(in);
+  words[i] = make_uint4(pack_word<BITS>(b), pack_word<BITS>(b + per), pack_word<BITS>(b + 2 * per),
+                        pack_word<BITS>(b + 3 * per));
+}
+
+__global__ void pack_nibbles_vec_kernel(const uint4* __restrict__ q, int64_t n16, uint2* __restrict__ out) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n16) return;
+  const uint4 v = q[i];
+  const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+  uint32_t h[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {  // bytes b0..b3 -> (b0 | b1 << 4) | (b2 | b3 << 4) << 8
+    const uint32_t x = u[k] & 0xFFFFFFFFu;
+    const uint32_t lo = (x & 0xFFu) | ((x >> 4) & 0xFF0u);          // b0 | b1 << 4 (bits 0-11)
+    const uint32_t hi = ((x >> 16) & 0xFFu) | ((x >> 20) & 0xFF0u);  // b2 | b3 << 4
+    h[k] = (lo & 0xFFu) | ((hi & 0xFFu) << 8);
+  }
+  out[i] = make_uint2(h[0] | (h[1] << 16), h[2] | (h[3] << 16));
+}
+
+__global__ void unpack_nibbles_vec_kernel(const uint2* __restrict__ p, int64_t n8, uint4* __restrict__ q) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n8) return;
+  const uint2 v = p[i];
+  const uint32_t u[2] = {v.x, v.y};
+  uint32_t o[4];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {  // 4 packed bytes -> 8 code bytes
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const uint32_t x = (u[k] >> (16 * half)) & 0xFFFFu;  // two packed bytes
+      o[2 * k + half] = (x & 0xFu) | ((x & 0xF0u) << 4) | ((x & 0xF00u) << 8) | ((x & 0xF000u) << 12);
+    }
+  }
+  q[i] = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 __global__ void unpack_q_kernel(const uint32_t* __restrict__ words, int64_t rows, int64_t nw, int bits,
                                 int64_t out_cols, uint8_t* __restrict__ q) {
   const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -201,7 +260,28 @@ extern "C" int gq_pack_q(const uint8_t* q, int64_t rows, int64_t C, int bits, ui
   const int64_t nw = rows * C / (32 / bits);
   if (nw == 0) return GQ_OK;
   GQ_REQUIRE(q && words, "gq_pack_q: null pointer");
-  pack_q_kernel<<<blocks_for(nw, 256), 256, 0, (cudaStream_t)stream>>>(q, nw, bits, words);
+  cudaStream_t s = (cudaStream_t)stream;
+  int64_t done = 0;  // words written by the vectorized kernel (whole groups of four)
+  if (aligned16(q) && aligned16(words)) {
+    const int64_t nquads = nw / 4;
+    if (nquads > 0) {
+      if (bits == 4)
+        pack_q_vec_kernel<4><<<blocks_for(nquads, 256), 256, 0, s>>>(reinterpret_cast<const uint4*>(q), nquads,
+                                                                    reinterpret_cast<uint4*>(words));
+      else if (bits == 2)
+        pack_q_vec_kernel<2><<<blocks_for(nquads, 256), 256, 0, s>>>(reinterpret_cast<const uint4*>(q), nquads,
+                                                                    reinterpret_cast<uint4*>(words));
+      else
+        pack_q_vec_kernel<8><<<blocks_for(nquads, 256), 256, 0, s>>>(reinterpret_cast<const uint4*>(q), nquads,
+                                                                    reinterpret_cast<uint4*>(words));
+      int st = check_launch("pack_q_vec_kernel");
+      if (st != GQ_OK) return st;
+      done = nquads * 4;
+    }
+  }
+  if (done == nw) return GQ_OK;
+  const int64_t per = 32 / bits;
+  pack_q_kernel<<<blocks_for(nw - done, 256), 256, 0, s>>>(q + done * per, nw - done, bits, words + done);
   return check_launch("pack_q_kernel");
 }
 
@@ -221,7 +301,20 @@ extern "C" int gq_pack_nibbles(const uint8_t* q, int64_t rows, int64_t C, uint8_
   const int64_t n = rows * C / 2;
   if (n == 0) return GQ_OK;
   GQ_REQUIRE(q && out, "gq_pack_nibbles: null pointer");
-  pack_nibbles_kernel<<<blocks_for(n, 256), 256, 0, (cudaStream_t)stream>>>(q, n, out);
+  cudaStream_t s = (cudaStream_t)stream;
+  int64_t done = 0;  // output bytes written by the vectorized kernel (whole groups of eight)
+  if (aligned16(q) && (reinterpret_cast<uintptr_t>(out) & 7u) == 0) {
+    const int64_t n8 = n / 8;
+    if (n8 > 0) {
+      pack_nibbles_vec_kernel<<<blocks_for(n8, 256), 256, 0, s>>>(reinterpret_cast<const uint4*>(q), n8,
+                                                                 reinterpret_cast<uint2*>(out));
+      int st = check_launch("pack_nibbles_vec_kernel");
+      if (st != GQ_OK) return st;
+      done = n8 * 8;
+    }
+  }
+  if (done == n) return GQ_OK;
+  pack_nibbles_kernel<<<blocks_for(n - done, 256), 256, 0, s>>>(q + 2 * done, n - done, out + done);
   return check_launch("pack_nibbles_kernel");
 }
 
@@ -229,6 +322,19 @@ extern "C" int gq_unpack_nibbles(const uint8_t* packed, int64_t rows, int64_t n_
   const int64_t n = rows * n_bytes;
   if (n == 0) return GQ_OK;
   GQ_REQUIRE(packed && q, "gq_unpack_nibbles: null pointer");
-  unpack_nibbles_kernel<<<blocks_for(n, 256), 256, 0, (cudaStream_t)stream>>>(packed, n, q);
+  cudaStream_t s = (cudaStream_t)stream;
+  int64_t done = 0;  // packed bytes consumed by the vectorized kernel (whole groups of eight)
+  if ((reinterpret_cast<uintptr_t>(packed) & 7u) == 0 && aligned16(q)) {
+    const int64_t n8 = n / 8;
+    if (n8 > 0) {
+      unpack_nibbles_vec_kernel<<<blocks_for(n8, 256), 256, 0, s>>>(reinterpret_cast<const uint2*>(packed), n8,
+                                                                   reinterpret_cast<uint4*>(q));
+      int st = check_launch("unpack_nibbles_vec_kernel");
+      if (st != GQ_OK) return st;
+      done = n8 * 8;
+    }
+  }
+  if (done == n) return GQ_OK;
+  unpack_nibbles_kernel<<<blocks_for(n - done, 256), 256, 0, s>>>(packed + done, n - done, q + 2 * done);
   return check_launch("unpack_nibbles_kernel");
 }
