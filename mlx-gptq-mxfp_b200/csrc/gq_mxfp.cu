@@ -4,8 +4,10 @@
 //
 // Layout: W / W_dq / q [B, R, C] row-major, H [B, C, C], U_g [B, C/32, 32, 32].
 // The column loop runs one thread per weight row and one CTA per
-// (32-column group, 128-row tile, batch item); the group's H_g and U_g sit in
-// shared memory and are read by all 128 threads as broadcasts.
+// (32-column group, 128-row tile, batch item); U_g sits in shared memory and is
+// read by all 128 threads as broadcasts. For safe-scale-search the eight objectives
+// e^T H_g e of the tile's 128 rows run on the tensor cores (tcgen05, kind::tf32,
+// accumulators in TMEM, one lane per row).
 #include "gq_affine_grid.cuh"
 
 namespace gq {
@@ -136,152 +138,11 @@ __global__ void __launch_bounds__(128) mx_hinv_kernel(const float* __restrict__ 
 // MXFP column loop
 // --------------------------------------------------------------------------
 
-// ---------------------------------------------------------------------------
-// e^T H_g e on the tensor cores (the einsum of gptq.py:123-125, 168)
-// ---------------------------------------------------------------------------
-// Each warp evaluates the objective of its 32 rows (lane = row) at once:
-// Y = E * H_g with mma.sync m16n8k8 in 3xTF32 (x = hi + lo, hi*hi + hi*lo + lo*hi:
-// about fp32 accuracy, so candidate comparisons behave like the fp32 reference),
-// then obj_r = sum_n Y[r][n] * E[r][n]. Staging strides (40 for E and H, 36 for Y)
-// make every fragment load/store and every row access bank-conflict free.
-constexpr int kES = 40, kYS = 36;
-
+// tf32 part of x (round to nearest, ties away): the hi term of the 3xTF32 split.
 __device__ __forceinline__ uint32_t to_tf32(float x) {
   uint32_t r;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
   return r;
-}
-
-__device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-      "{%0, %1, %2, %3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// S: this warp's staging area (E first, then reused for Y = E*H once E is in
-// fragments); Hhi/Hlo: tf32 split of H_g, row-major, stride kES.
-__device__ __forceinline__ float quad32(const float (&e)[32], float* S, const uint32_t* Hhi, const uint32_t* Hlo,
-                                        int lane) {
-#pragma unroll
-  for (int c = 0; c < 32; ++c) S[c * kES + lane] = e[c];  // column-major E
-  __syncwarp();
-  const int g = lane >> 2, tq = lane & 3;
-  float acc[2][4][4];
-#pragma unroll
-  for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) acc[mt][nt][0] = acc[mt][nt][1] = acc[mt][nt][2] = acc[mt][nt][3] = 0.0f;
-#pragma unroll
-  for (int kt = 0; kt < 4; ++kt) {
-#pragma unroll
-    for (int mt = 0; mt < 2; ++mt) {
-      const float* ec = S + (8 * kt + tq) * kES + 16 * mt + g;
-      const float av[4] = {ec[0], ec[8], ec[4 * kES], ec[4 * kES + 8]};
-      uint32_t ahi[4], alo[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        ahi[i] = to_tf32(av[i]);
-        alo[i] = to_tf32(av[i] - __uint_as_float(ahi[i]));
-      }
-#pragma unroll
-      for (int nt = 0; nt < 4; ++nt) {
-        const int o0 = (8 * kt + tq) * kES + 8 * nt + g, o1 = o0 + 4 * kES;
-        mma_tf32(acc[mt][nt], ahi, Hhi[o0], Hhi[o1]);
-        mma_tf32(acc[mt][nt], ahi, Hlo[o0], Hlo[o1]);
-        mma_tf32(acc[mt][nt], alo, Hhi[o0], Hhi[o1]);
-      }
-    }
-  }
-  __syncwarp();  // every lane has its E fragments: the area now holds Y
-#pragma unroll
-  for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-      float* y = S + (8 * nt + 2 * tq) * kYS + 16 * mt + g;
-      y[0] = acc[mt][nt][0];
-      y[kYS] = acc[mt][nt][1];
-      y[8] = acc[mt][nt][2];
-      y[kYS + 8] = acc[mt][nt][3];
-    }
-  __syncwarp();
-  float o0 = 0.0f, o1 = 0.0f;
-#pragma unroll
-  for (int c = 0; c < 32; c += 2) {
-    o0 = fmaf(S[c * kYS + lane], e[c], o0);
-    o1 = fmaf(S[(c + 1) * kYS + lane], e[c + 1], o1);
-  }
-  __syncwarp();  // staging is reused by the next call
-  return o0 + o1;
-}
-
-// e^T H_g e for the 32 rows of a warp whose error vectors the lanes have already
-// written, column-major, into Se (Se[c * kES + lane] = e[c] of the lane's row). Y = E * H_g
-// comes from the same 3xTF32 mma.sync products as quad32; each lane then multiplies its
-// Y fragments by the matching E entries (rows g, g+8, g+16, g+24 of its quad), the four
-// lanes of a quad sum their partials, and each row's total is sent to the row's lane.
-// No staging area for Y and no e[] in registers.
-__device__ __forceinline__ float quad32_staged(const float* Se, const uint32_t* Hhi, const uint32_t* Hlo, int lane) {
-  __syncwarp();
-  const int g = lane >> 2, tq = lane & 3;
-  float acc[2][4][4];
-#pragma unroll
-  for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) acc[mt][nt][0] = acc[mt][nt][1] = acc[mt][nt][2] = acc[mt][nt][3] = 0.0f;
-#pragma unroll
-  for (int kt = 0; kt < 4; ++kt) {
-#pragma unroll
-    for (int mt = 0; mt < 2; ++mt) {
-      const float* ec = Se + (8 * kt + tq) * kES + 16 * mt + g;
-      const float av[4] = {ec[0], ec[8], ec[4 * kES], ec[4 * kES + 8]};
-      uint32_t ahi[4], alo[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        ahi[i] = to_tf32(av[i]);
-        alo[i] = to_tf32(av[i] - __uint_as_float(ahi[i]));
-      }
-#pragma unroll
-      for (int nt = 0; nt < 4; ++nt) {
-        const int o0 = (8 * kt + tq) * kES + 8 * nt + g, o1 = o0 + 4 * kES;
-        mma_tf32(acc[mt][nt], ahi, Hhi[o0], Hhi[o1]);
-        mma_tf32(acc[mt][nt], ahi, Hlo[o0], Hlo[o1]);
-        mma_tf32(acc[mt][nt], alo, Hhi[o0], Hhi[o1]);
-      }
-    }
-  }
-  // acc[mt][nt] = Y[16mt+g][8nt+2tq], Y[16mt+g][8nt+2tq+1], Y[16mt+g+8][8nt+2tq], Y[16mt+g+8][8nt+2tq+1]
-  float part[4];  // rows g, g+8, g+16, g+24
-#pragma unroll
-  for (int mt = 0; mt < 2; ++mt) {
-    float lo = 0.0f, hi = 0.0f;
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-      const int col = 8 * nt + 2 * tq, row = 16 * mt + g;
-      lo = fmaf(acc[mt][nt][0], Se[col * kES + row], lo);
-      lo = fmaf(acc[mt][nt][1], Se[(col + 1) * kES + row], lo);
-      hi = fmaf(acc[mt][nt][2], Se[col * kES + row + 8], hi);
-      hi = fmaf(acc[mt][nt][3], Se[(col + 1) * kES + row + 8], hi);
-    }
-    part[2 * mt] = lo;
-    part[2 * mt + 1] = hi;
-  }
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    part[i] += __shfl_xor_sync(0xFFFFFFFFu, part[i], 1);
-    part[i] += __shfl_xor_sync(0xFFFFFFFFu, part[i], 2);
-  }
-  // row r = 8 * (r >> 3) + (r & 7): held as part[r >> 3] by lanes 4 * (r & 7) .. + 3
-  const int src = 4 * (lane & 7), which = lane >> 3;
-  float v = 0.0f;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float x = __shfl_sync(0xFFFFFFFFu, part[i], src);
-    v = which == i ? x : v;
-  }
-  __syncwarp();  // Se is rewritten by the next call
-  return v;
 }
 
 // Grid value (without the scale) of w * inv for the mode.
@@ -360,6 +221,108 @@ template <int MODE> struct Codes {
   }
 };
 
+// ---------------------------------------------------------------------------
+// Objectives of a 128-row tile on the 5th-generation tensor cores (safe-scale-search)
+// ---------------------------------------------------------------------------
+// Y = E * H_g for the CTA's 128 rows at once: one tcgen05.mma (kind::tf32, M = 128,
+// N = 32, K = 8) per K step and split term, issued by one thread, accumulating in 32
+// TMEM columns; TMEM lane r is row r, so thread r reads its row of Y with one
+// tcgen05.ld and forms e_r^T H_g e_r = sum_c Y[r][c] * e_r[c] itself. E and H_g go to
+// shared memory as 3xTF32 splits (x = hi + lo, hi = tf32(x); D = Ehi*Hhi + Ehi*Hlo +
+// Elo*Hhi) in the K-major 128-byte-swizzled layout: row r (128 bytes = 32 fp32) at
+// r * 128, 16-byte chunk j stored at chunk j ^ (r % 8).
+namespace tc {
+constexpr uint32_t kRows = 128, kRowBytes = 128;
+constexpr uint32_t A_BYTES = kRows * kRowBytes;  // 16 KB per split of E
+constexpr uint32_t B_BYTES = 32 * kRowBytes;     // 4 KB per split of H_g
+constexpr uint32_t TMEM_COLS = 32;
+
+__device__ __forceinline__ uint32_t swz(uint32_t row, uint32_t col) {  // byte offset of (row, fp32 col)
+  return row * kRowBytes + ((((col >> 2) ^ (row & 7u)) << 4) | ((col & 3u) << 2));
+}
+// Shared-memory descriptor: K-major, SWIZZLE_128B, 8-row groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t addr) {
+  uint64_t d = 0;
+  d |= uint64_t((addr >> 4) & 0x3FFFu);
+  d |= uint64_t(1) << 16;             // leading byte offset (unused: K fits one swizzle atom)
+  d |= uint64_t(1024 >> 4) << 32;     // stride byte offset: next 8-row group
+  d |= uint64_t(1) << 46;             // descriptor version for sm_100
+  d |= uint64_t(2) << 61;             // SWIZZLE_128B
+  return d;
+}
+// Instruction descriptor, kind::tf32: f32 accumulate, tf32 A and B, both K-major.
+constexpr uint32_t idesc_tf32(int M, int N) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
+}
+__device__ __forceinline__ void mma_tf32_128x32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  constexpr uint32_t idesc = idesc_tf32(128, 32);
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+}  // namespace tc
+
+// Writes this thread's error vector (row `row` of E) as its hi/lo tf32 split.
+__device__ __forceinline__ void tc_stage_row(uint8_t* ahi, uint8_t* alo, uint32_t row, const float (&e)[32]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {  // one 16-byte chunk (4 columns) at a time
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      h[i] = to_tf32(e[4 * j + i]);
+      l[i] = __float_as_uint(e[4 * j + i] - __uint_as_float(h[i]));
+    }
+    const uint32_t off = tc::swz(row, 4 * j);
+    *reinterpret_cast<uint4*>(ahi + off) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(alo + off) = make_uint4(l[0], l[1], l[2], l[3]);
+  }
+}
+
+// e_r^T H_g e_r for the thread's row after every thread of the CTA staged its row:
+// thread 0 issues the 12 MMAs and commits to `bar`; every thread waits for that phase,
+// reads its TMEM lane and contracts it with e.
+__device__ __forceinline__ float tc_objective(uint32_t ahi, uint32_t alo, uint32_t bhi, uint32_t blo,
+                                              uint32_t tmem, uint64_t* bar, uint32_t& phase, const float (&e)[32],
+                                              int tid, volatile int* abort_flag) {
+  tc::fence_proxy_async_smem();  // this thread's rows are visible to the tensor cores
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (tid == 0) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {  // K = 8 tf32 = 32 bytes per step inside the 128-byte rows
+      const uint32_t ko = uint32_t(k) * 32u;
+      const uint64_t dahi = tc::desc_kmajor_sw128(ahi + ko), dalo = tc::desc_kmajor_sw128(alo + ko);
+      const uint64_t dbhi = tc::desc_kmajor_sw128(bhi + ko), dblo = tc::desc_kmajor_sw128(blo + ko);
+      tc::mma_tf32_128x32(tmem, dahi, dbhi, k > 0 ? 1u : 0u);
+      tc::mma_tf32_128x32(tmem, dahi, dblo, 1u);
+      tc::mma_tf32_128x32(tmem, dalo, dbhi, 1u);
+    }
+    umma_commit(bar);
+  }
+  mbar_wait(bar, phase, abort_flag, nullptr);
+  phase ^= 1u;
+  tc_fence_after();
+  float o0 = 0.0f, o1 = 0.0f;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {  // 16 columns at a time keeps the row's Y out of the register peak
+    uint32_t y[16];
+    tmem_ld16(tmem + (uint32_t((tid >> 5) * 32) << 16) + uint32_t(16 * h), y);
+    tmem_ld_wait();
+#pragma unroll
+    for (int c = 0; c < 16; c += 2) {
+      o0 = fmaf(__uint_as_float(y[c]), e[16 * h + c], o0);
+      o1 = fmaf(__uint_as_float(y[c + 1]), e[16 * h + c + 1], o1);
+    }
+  }
+  tc_fence_before();  // the TMEM reads finish before the next MMA (after the next barrier)
+  return o0 + o1;
+}
+
 // Grid values (without the scale) of a code pair as stored in Codes.
 template <int MODE>
 __device__ __forceinline__ float2 code_pair_values(uint32_t pair) {
@@ -379,12 +342,15 @@ __global__ void __launch_bounds__(128, SAFE ? 3 : 4) mx_gptq_kernel(const Tin* _
                                                       uint8_t* __restrict__ q, uint8_t* __restrict__ qp,
                                                       uint8_t* __restrict__ scales, Tout* __restrict__ wdq,
                                                       float* __restrict__ partials, int64_t partials_cap) {
-  constexpr int kStageFloats = SAFE ? 32 * kES : 1;
-  __shared__ __align__(16) uint32_t Hhi[SAFE ? 32 * kES : 1], Hlo[SAFE ? 32 * kES : 1];  // tf32 split of H_g
+  // safe-scale-search: E (hi, lo) and H_g (hi, lo) operand tiles of the objectives
+  constexpr uint32_t kTcBytes = SAFE ? 2 * tc::A_BYTES + 2 * tc::B_BYTES : 16;
+  __shared__ __align__(1024) uint8_t Tsm[kTcBytes];
   __shared__ __align__(16) float Us[32][32];
-  __shared__ __align__(16) float Se[4][kStageFloats];  // per-warp error vectors (column-major)
   __shared__ float red[2][4];
   __shared__ uint32_t s_dmask;
+  __shared__ uint64_t s_bar;         // MMA completion (safe-scale-search)
+  __shared__ uint32_t s_tmem;        // TMEM base of the 32 accumulator columns
+  __shared__ int s_abort;
   const int64_t G = C / 32;
   const int64_t g = blockIdx.x, tile = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x;
@@ -397,14 +363,26 @@ __global__ void __launch_bounds__(128, SAFE ? 3 : 4) mx_gptq_kernel(const Tin* _
     return;
   }
   const float* Ug = U + (b * G + g) * 1024;
+  uint8_t* const a_hi = Tsm;  // (groupwise: a 16-byte placeholder, never used)
+  uint8_t* const a_lo = Tsm + (SAFE ? tc::A_BYTES : 0u);
+  uint8_t* const b_hi = Tsm + (SAFE ? 2 * tc::A_BYTES : 0u);
+  uint8_t* const b_lo = b_hi + (SAFE ? tc::B_BYTES : 0u);
   if (SAFE) {
+    // B operand: row n of H_g (symmetric, so B[n][k] = H_g[k][n] = H_g[n][k]), hi/lo split
     const float* Hg = H + (b * C + g * 32) * C + g * 32;
     for (int i = tid; i < 1024; i += 128) {
-      const float h = Hg[int64_t(i >> 5) * C + (i & 31)];
+      const uint32_t n = uint32_t(i >> 5), k = uint32_t(i & 31);
+      const float h = Hg[int64_t(n) * C + k];
       const uint32_t hi = to_tf32(h);
-      Hhi[(i >> 5) * kES + (i & 31)] = hi;
-      Hlo[(i >> 5) * kES + (i & 31)] = to_tf32(h - __uint_as_float(hi));
+      *reinterpret_cast<uint32_t*>(b_hi + tc::swz(n, k)) = hi;
+      *reinterpret_cast<uint32_t*>(b_lo + tc::swz(n, k)) = __float_as_uint(h - __uint_as_float(hi));
     }
+    if (tid == 0) {
+      mbar_init(&s_bar, 1);
+      s_abort = 0;
+      fence_mbar_init();
+    }
+    if (tid < 32) tmem_alloc(&s_tmem, tc::TMEM_COLS);
   }
   for (int i = tid; i < 1024; i += 128) Us[i >> 5][i & 31] = Ug[i];
   if (tid < 32) {
@@ -412,11 +390,14 @@ __global__ void __launch_bounds__(128, SAFE ? 3 : 4) mx_gptq_kernel(const Tin* _
     const uint32_t m = __ballot_sync(0xFFFFFFFFu, d);
     if (tid == 0) s_dmask = m;
   }
+  if (SAFE) tc_fence_before();
   __syncthreads();
+  if (SAFE) tc_fence_after();
   const uint32_t dmask = s_dmask;
   const int64_t r = tile * 128 + tid;
-  const int lane = tid & 31;
-  float* se = Se[tid >> 5];
+  const uint32_t tmem = SAFE ? s_tmem : 0u;
+  const uint32_t sa_hi = smem_u32(a_hi), sa_lo = smem_u32(a_lo), sb_hi = smem_u32(b_hi), sb_lo = smem_u32(b_lo);
+  uint32_t phase = 0;
   float num = 0.0f, den = 0.0f;
   const bool active = r < R;  // rows past R run on zeros (the objectives need whole warps)
   {
@@ -451,9 +432,11 @@ __global__ void __launch_bounds__(128, SAFE ? 3 : 4) mx_gptq_kernel(const Tin* _
         int e = e0 + d;
         e = e < -127 ? -127 : (e > 127 ? 127 : e);
         const float sc = exp2i(e), inv = exp2i(-e);
+        float err[32];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) se[c * kES + lane] = mx_round<MODE>(o[c], inv) * sc - o[c];
-        const float obj = quad32_staged(se, Hhi, Hlo, lane);
+        for (int c = 0; c < 32; ++c) err[c] = mx_round<MODE>(o[c], inv) * sc - o[c];
+        tc_stage_row(a_hi, a_lo, uint32_t(tid), err);
+        const float obj = tc_objective(sa_hi, sa_lo, sb_hi, sb_lo, tmem, &s_bar, phase, err, tid, &s_abort);
         if (t == 0 || obj < best_obj) {
           best_obj = obj;
           best_e = e;
@@ -487,9 +470,8 @@ __global__ void __launch_bounds__(128, SAFE ? 3 : 4) mx_gptq_kernel(const Tin* _
     }
     bool use_gptq = true;
     if (SAFE) {
-#pragma unroll
-      for (int c = 0; c < 32; ++c) se[c * kES + lane] = wv[c];
-      use_gptq = quad32_staged(se, Hhi, Hlo, lane) <= best_obj;
+      tc_stage_row(a_hi, a_lo, uint32_t(tid), wv);
+      use_gptq = tc_objective(sa_hi, sa_lo, sb_hi, sb_lo, tmem, &s_bar, phase, wv, tid, &s_abort) <= best_obj;
     }
     use_gptq = use_gptq && valid;
     if (!use_gptq) {  // baseline: RTN with the chosen scale
@@ -557,6 +539,14 @@ __global__ void __launch_bounds__(128, SAFE ? 3 : 4) mx_gptq_kernel(const Tin* _
     if (tid == 0 && p_out) {
       p_out[0] = (red[0][0] + red[0][1]) + (red[0][2] + red[0][3]);
       p_out[1] = (red[1][0] + red[1][1]) + (red[1][2] + red[1][3]);
+    }
+  }
+  if (SAFE) {  // every TMEM read is done: release the columns
+    tc_fence_before();
+    __syncthreads();
+    if (tid < 32) {
+      tc_fence_after();
+      tmem_dealloc(tmem, tc::TMEM_COLS);
     }
   }
 }
