@@ -228,12 +228,22 @@ class C3Step:
 class C3E2E:
     """The C3 step with this rank's inputs copied from pinned host memory on a side
     stream every step (X, gate_up weights and token ids first; down activations and
-    weights second, overlapping the gate_up stage) and every expert's codes and scales
-    read back to pinned host memory."""
+    weights second, overlapping the gate_up stage) and this rank's results read back.
 
-    def __init__(self, step: C3Step):
-        self.step, self.device = step, step.device
+    X, the layer input every rank needs, crosses PCIe once per step in all: with N
+    ranks each copies 1/N of its rows and one all-gather over NVLink assembles it on
+    every rank (the host link is the slow one). Each rank reads back the codes and
+    scales of its own experts (sharded artifacts; the exchange still hands every rank
+    every expert's outputs for the next layer)."""
+
+    def __init__(self, step: C3Step, rank: int, world: int, group=None):
+        self.step, self.device, self.rank, self.world, self.group = step, step.device, rank, world, group
         self.host = step.inp.host_copy()
+        T = self.host["X"].shape[0]
+        self.rows = T // world if world > 1 and T % world == 0 else None
+        if self.rows is not None:  # only this rank's slice of X is copied from the host
+            self.host["X"] = self.host["X"][rank * self.rows:(rank + 1) * self.rows].clone().pin_memory()
+            self.x_full = torch.empty(T, self.host["X"].shape[1], dtype=torch.bfloat16, device=self.device)
         self.dev = {k: torch.empty_like(v, device=self.device) for k, v in self.host.items()}
         self.cs = torch.cuda.Stream(self.device)
         self.h2d_bytes = sum(v.numel() * v.element_size() for v in self.host.values())
@@ -251,9 +261,19 @@ class C3E2E:
                 e = torch.cuda.Event()
                 e.record(self.cs)
                 ready.append(e)
-        self.step.run(X=self.dev["X"], W_gu=self.dev["W_gu"], W_dn=self.dev["W_dn"], acts=self.dev["acts"],
+        X = self.dev["X"]
+        if self.rows is not None:
+            import torch.distributed as dist
+
+            ms.wait_event(ready[0])
+            dist.all_gather_into_tensor(self.x_full, self.dev["X"], group=self.group)
+            X = self.x_full
+            ready[0] = torch.cuda.Event()
+            ready[0].record(ms)
+        self.step.run(X=X, W_gu=self.dev["W_gu"], W_dn=self.dev["W_dn"], acts=self.dev["acts"],
                       tok=self.dev["tok"], ready=ready)
-        outs = self.step.outputs()
+        gu, dn = self.step.last
+        outs = [gu.codes, gu.scales, dn.codes, dn.scales]  # this rank's experts
         if self.out_host is None:
             self.out_host = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in outs]
             self.d2h_bytes = sum(o.numel() * o.element_size() for o in outs)
@@ -863,7 +883,7 @@ def run_c3(args, ws, rank, local):
 
     e2e = None
     if not args.no_e2e:
-        leg = C3E2E(step)
+        leg = C3E2E(step, rank, ws, group)
         for _ in range(2):
             leg.run()
         torch.cuda.synchronize()
@@ -879,8 +899,8 @@ def run_c3(args, ws, rank, local):
         ms_e2e = _max_over_ranks(a.elapsed_time(b) / n, pg, device)
         e2e = {"value": C3_ELEMS / (ms_e2e / 1e3), "unit": "elems/s", "ms_per_step": ms_e2e,
                "h2d_bytes_per_step": leg.h2d_bytes, "d2h_bytes_per_step": leg.d2h_bytes,
-               "note": "per rank: its inputs host->device (X, its experts' weights, token ids and slot "
-                       "activations) and every expert's codes + E8M0 scales device->host"}
+               "note": "per rank: 1/N of X's rows host->device (all-gathered over NVLink), its experts' "
+                       "weights, token ids and slot activations; its experts' codes + E8M0 scales device->host"}
         del leg
     reps = None if args.no_extras else c2_replicas(device, rank, ws, pg, 5) if ws > 1 else None
     outs = step.outputs()

@@ -264,22 +264,36 @@ class LazyShardedEmbedding(torch.nn.Module):
         return rows.to(self.device)[inverse.to(self.device)].reshape(*ids.shape, self.dim)
 
 
+_PLE_TABLE = "ple.ple_embedding.ngram_embedding"
+_SHARD_NO = re.compile(r"\.shard_(\d+)\.weight$")
+
+
+def _ple_shard_count(shards, table_name: str) -> int:
+    """Number of row shards stored for one per-layer embedding table: shard_0 ..
+    shard_{n-1}, every one present."""
+    found = sorted({int(m.group(1)) for n in shards.names_with_prefix(table_name + ".shard_")
+                    if (m := _SHARD_NO.search(n))})
+    if not found:
+        raise KeyError(f"no PLE shards found for {table_name}")
+    if found != list(range(len(found))):
+        raise KeyError(f"PLE shards of {table_name} are not numbered 0..{len(found) - 1}: {found}")
+    return len(found)
+
+
 def install_lazy_ple(module: torch.nn.Module, prefix: str, shards, device, dtype):
-    """Replace every fused per-layer embedding table (`...ple.ple_embedding.ngram_embedding`)
-    under `module` by a LazyShardedEmbedding over its checkpoint shards (sequential.py:193-229)."""
-    for name, child in list(module.named_modules()):
-        if not name.endswith("ple.ple_embedding.ngram_embedding"):
-            continue
-        parent_name, attr = name.rsplit(".", 1)
-        total_rows, dim = child.weight.shape
-        shard_names = shards.names_with_prefix(f"{prefix}.{name}.shard_")
-        if not shard_names:
-            raise KeyError(f"no PLE shards found for {prefix}.{name}")
-        n = len(shard_names)
-        if total_rows % n:
-            raise ValueError(f"PLE rows {total_rows} are not divisible by {n} shards")
-        setattr(module.get_submodule(parent_name), attr,
-                LazyShardedEmbedding(f"{prefix}.{name}", shards, n, total_rows // n, dim, device, dtype))
+    """Swap every fused per-layer embedding table under `module` (a module path ending
+    in ple.ple_embedding.ngram_embedding, the Gemma-4 layout of sequential.py:193-229)
+    for a LazyShardedEmbedding reading its rows from the checkpoint's row shards."""
+    tables = [(name, child) for name, child in module.named_modules() if name.endswith(_PLE_TABLE)]
+    for name, child in tables:
+        rows, dim = child.weight.shape
+        n = _ple_shard_count(shards, f"{prefix}.{name}")
+        per, rem = divmod(rows, n)
+        if rem:
+            raise ValueError(f"PLE rows {rows} are not divisible by {n} shards")
+        owner, attr = name.rsplit(".", 1)
+        setattr(module.get_submodule(owner), attr,
+                LazyShardedEmbedding(f"{prefix}.{name}", shards, n, per, dim, device, dtype))
 
 
 # ---------------------------------------------------------------------------
@@ -322,26 +336,32 @@ class _LayerRecorder(torch.nn.Module):
         return hidden_states
 
 
-def _detach_context(value, memo):
-    """Detach the tensors of a layer call context, copying tuples, lists and dicts
-    but keeping each object's identity shared across layers (one memo per batch):
-    a container that layer i mutates and layer i+1 reads stays one object
-    (sequential.py:271-293). Tensors stay on the forward device."""
-    key = id(value)
-    if key in memo:
-        return memo[key]
-    if isinstance(value, torch.Tensor):
-        out = value.detach()
-    elif isinstance(value, tuple):
-        out = tuple(_detach_context(v, memo) for v in value)
-    elif isinstance(value, list):
-        out = [_detach_context(v, memo) for v in value]
-    elif isinstance(value, dict):
-        out = {k: _detach_context(v, memo) for k, v in value.items()}
-    else:
-        out = value
-    memo[key] = out
-    return out
+class _ContextDetacher:
+    """Detached copy of the layer call contexts of one batch: tensors detached (they
+    stay on the forward device), tuples / lists / dicts rebuilt, anything else kept as
+    is, and every object mapped once, so a container that layer i mutates and layer
+    i+1 reads stays one shared object across the copied contexts (the identity rule of
+    sequential.py:271-293)."""
+
+    def __init__(self):
+        self._seen: dict[int, object] = {}
+
+    def __call__(self, value):
+        hit = self._seen.get(id(value), self)
+        if hit is not self:
+            return hit
+        if isinstance(value, torch.Tensor):
+            out = value.detach()
+        elif isinstance(value, dict):
+            out = {k: self(v) for k, v in value.items()}
+        elif isinstance(value, tuple):
+            out = tuple(self(v) for v in value)
+        elif isinstance(value, list):
+            out = [self(v) for v in value]
+        else:
+            out = value
+        self._seen[id(value)] = out
+        return out
 
 
 # ---------------------------------------------------------------------------
@@ -443,8 +463,8 @@ class Pipeline:
                     self.model(input_ids=samples[i: i + batch_size].to(self.dev0), use_cache=False)
                 if not log_.complete():
                     raise RuntimeError("catcher did not observe every decoder layer")
-                memo = {}
-                contexts = [(_detach_context(args, memo), {k: _detach_context(v, memo) for k, v in kwargs.items()})
+                detach = _ContextDetacher()
+                contexts = [(detach(args), {k: detach(v) for k, v in kwargs.items()})
                             for args, kwargs in log_.contexts]
                 batches.append((log_.hidden, contexts))
         finally:
