@@ -222,6 +222,20 @@ int gq_gptq_affine(float* W, const void* W_orig, int w_dtype, const float* U, in
                    int bits, int group_size, int block_size, int clip, int storage_dtype, uint8_t* q, void* scales,
                    void* biases, float* rel_err, void* workspace, size_t workspace_bytes, void* stream);
 
+/* The float32 GEMM the affine solver runs its trailing updates and factor
+ * products on, exposed for testing: per batch item z = outer * n_inner + inner,
+ * C = alpha * op(A) op(B) + beta * C with op(A)(r, t) = A[t*lda + r] if trans_a else
+ * A[r*lda + t] (M x K), op(B)(t, c) = B[c*ldb + t] if trans_b else B[t*ldb + c]
+ * (K x N), item offsets outer*s?_o + inner*s?_i (elements); items whose outer index
+ * has skip[outer] != 0 are left alone (skip nullable). engine 1: TMA-fed tcgen05
+ * kind::tf32 in a 3xTF32 split (16-byte aligned A and B, leading dimensions and
+ * strides multiples of 4); engine 0: the mma.sync 3xTF32 kernels. No counterpart in
+ * the reference (its torch.bmm / matmul calls, gptq.py:269-270). */
+int gq_gemm_f32(const float* A, const float* Bm, float* Cm, int64_t M, int64_t N, int64_t K, int64_t lda,
+                int64_t ldb, int64_t ldc, int trans_a, int trans_b, int64_t batches, int64_t n_inner, int64_t sa_o,
+                int64_t sa_i, int64_t sb_o, int64_t sb_i, int64_t sc_o, int64_t sc_i, float alpha, float beta,
+                const int32_t* skip, int engine, int32_t* status, void* stream);
+
 /* W_out (fp32 [B, R, C]) = W_in converted to fp32, with columns where
  * dead[b, j] != 0 set to zero (the W.float().clone() + dead-column zeroing of
  * gptq.py:288 and gptq.py:219-221). dead is nullable. */

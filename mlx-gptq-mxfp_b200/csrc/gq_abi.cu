@@ -1,10 +1,25 @@
-// Version, status strings and the per-thread last-error message.
+// Version, status strings, the per-thread last-error message and the driver lookups.
 #include <stdarg.h>
 #include <stdio.h>
+
+#include <mutex>
 
 #include "gq_common.cuh"
 
 namespace gq {
+
+EncodeTiledFn tensor_map_encoder() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
 
 static thread_local char g_last_error[512] = "";
 

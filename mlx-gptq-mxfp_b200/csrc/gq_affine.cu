@@ -20,6 +20,7 @@
 #include <vector>
 
 #include "gq_affine_grid.cuh"
+#include "gq_gemm.cuh"
 
 namespace gq {
 namespace aff {
@@ -156,19 +157,7 @@ __device__ __forceinline__ void tile_store(float* __restrict__ Cm, int64_t ldc, 
     }
 }
 
-// Batched GEMM C = alpha*A*B + beta*C on 64x64 tiles; batch index z = outer*n_inner + inner.
-struct GemmBatch {
-  const float* A;
-  const float* Bm;
-  float* Cm;
-  int64_t lda, ldb, ldc;
-  int64_t sa_o, sb_o, sc_o;  // outer strides (elements)
-  int64_t sa_i, sb_i, sc_i;  // inner strides
-  int n_inner;
-  int M, N, K;
-  float alpha, beta;
-  const int32_t* skip;  // per outer item: nonzero = skip (nullable)
-};
+// Batched GEMM C = alpha*A*B + beta*C (GemmBatch, gq_gemm.cuh) on 64x64 tiles.
 
 template <bool TRANS_A, bool TRANS_B>
 __global__ void __launch_bounds__(256) gemm_kernel(GemmBatch p) {
@@ -348,6 +337,15 @@ static int launch_gemm(const GemmBatch& p, bool trans_a, bool trans_b, int64_t b
   else
     gemm_kernel<false, false><<<grid, 256, 0, s>>>(p);
   return check_launch("gemm_kernel");
+}
+
+// Products whose tiles fill the 128 x 128 tensor-core tile go to tc_gemm (TMA-fed
+// tcgen05, gq_tc_gemm.cu); smaller ones and layouts a tensor map cannot describe to
+// the mma.sync kernels above.
+static int gemm(const GemmBatch& p, bool trans_a, bool trans_b, int64_t batches, cudaStream_t s) {
+  if (p.M >= 128 && p.N >= 128 && tc_gemm_usable(p, trans_a, trans_b))
+    return tc_gemm(p, trans_a, trans_b, batches, nullptr, s);
+  return launch_gemm(p, trans_a, trans_b, batches, s);
 }
 
 // ---------------------------------------------------------------------------
@@ -847,7 +845,7 @@ extern "C" int gq_prepare_hinv(const float* H, int64_t B, int64_t C, float damp,
       g1.alpha = 1.0f;
       g1.beta = 0.0f;
       g1.skip = st.info;
-      int r = launch_gemm(g1, true, true, B * npairs, s);
+      int r = gemm(g1, true, true, B * npairs, s);
       if (r != GQ_OK) return r;
       GemmBatch g2 = g1;  // Linv(r0.., c0..) = -Dinv * X, X(t, c) = Xt[c][t]
       g2.A = U + r0 * C + r0;
@@ -857,7 +855,7 @@ extern "C" int gq_prepare_hinv(const float* H, int64_t B, int64_t C, float damp,
       g2.N = int(sz);
       g2.K = int(dsz);
       g2.alpha = -1.0f;
-      r = launch_gemm(g2, false, true, B * npairs, s);
+      r = gemm(g2, false, true, B * npairs, s);
       if (r != GQ_OK) return r;
     }
   }
@@ -940,7 +938,7 @@ extern "C" int gq_gptq_affine(float* W, const void* W_orig, int w_dtype, const f
       g.K = int(bs);
       g.alpha = -1.0f;
       g.beta = 1.0f;
-      r = launch_gemm(g, false, false, B, s);
+      r = gemm(g, false, false, B, s);
       if (r != GQ_OK) return r;
     }
   }
@@ -957,4 +955,42 @@ extern "C" int gq_gptq_affine(float* W, const void* W_orig, int w_dtype, const f
     return launch_rel_err(partials, B, 1024, rel_err, s);
   }
   return GQ_OK;
+}
+
+extern "C" int gq_gemm_f32(const float* A, const float* Bm, float* Cm, int64_t M, int64_t N, int64_t K, int64_t lda,
+                           int64_t ldb, int64_t ldc, int trans_a, int trans_b, int64_t batches, int64_t n_inner,
+                           int64_t sa_o, int64_t sa_i, int64_t sb_o, int64_t sb_i, int64_t sc_o, int64_t sc_i,
+                           float alpha, float beta, const int32_t* skip, int engine, int32_t* status, void* stream) {
+  GQ_REQUIRE(A && Bm && Cm, "gq_gemm_f32: null pointer");
+  GQ_REQUIRE(M > 0 && N > 0 && K > 0 && M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31),
+             "gq_gemm_f32: bad sizes");
+  GQ_REQUIRE(batches > 0 && n_inner > 0 && batches % n_inner == 0 && batches < 65536,
+             "gq_gemm_f32: bad batch counts");
+  GemmBatch g{};
+  g.A = A;
+  g.Bm = Bm;
+  g.Cm = Cm;
+  g.lda = lda;
+  g.ldb = ldb;
+  g.ldc = ldc;
+  g.sa_o = sa_o;
+  g.sa_i = sa_i;
+  g.sb_o = sb_o;
+  g.sb_i = sb_i;
+  g.sc_o = sc_o;
+  g.sc_i = sc_i;
+  g.n_inner = int(n_inner);
+  g.M = int(M);
+  g.N = int(N);
+  g.K = int(K);
+  g.alpha = alpha;
+  g.beta = beta;
+  g.skip = skip;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (engine == 1) {
+    GQ_REQUIRE(tc_gemm_usable(g, trans_a != 0, trans_b != 0), "gq_gemm_f32: layout not supported by tcgen05 path");
+    return tc_gemm(g, trans_a != 0, trans_b != 0, batches, status, s);
+  }
+  GQ_REQUIRE(engine == 0, "gq_gemm_f32: engine must be 0 (mma.sync) or 1 (tcgen05)");
+  return launch_gemm(g, trans_a != 0, trans_b != 0, batches, s);
 }

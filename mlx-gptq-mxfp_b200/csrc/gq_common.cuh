@@ -23,6 +23,12 @@ namespace gq {
 void set_last_error(const char* fmt, ...);
 int check_launch(const char* what);  // GQ_OK or GQ_ERR_CUDA (message recorded)
 
+// cuTensorMapEncodeTiled from the driver (looked up once), or nullptr.
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn tensor_map_encoder();
+
 #define GQ_REQUIRE(cond, ...)              \
   do {                                     \
     if (!(cond)) {                         \

@@ -513,22 +513,7 @@ __global__ void scale_kernel(float* H, int64_t c, int64_t ldh, float beta) {
   *p = beta == 0.0f ? 0.0f : beta * *p;
 }
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
-  return fn;
-}
+static EncodeTiledFn encode_fn() { return tensor_map_encoder(); }
 
 // 2-D bf16 tensor map over X [rows, cols] (row stride ld elements), 64 x 64 boxes, 128B swizzle.
 int make_x_map(CUtensorMap* map, const void* X, int64_t rows, int64_t cols, int64_t ld) {

@@ -50,6 +50,8 @@ SIGNATURES = {
     "gq_gptq_mxfp_noalloc": (I32, [P, I32, P, P, P, P, I64, I64, I64, I32, I32, P, P, P, P, I32, P, P]),
     "gq_gptq_affine_workspace_size": (SZ, [I64, I64, I64, I32, I32]),
     "gq_gptq_affine": (I32, [P, P, I32, P, I64, I64, I64, I32, I32, I32, I32, I32, P, P, P, P, P, SZ, P]),
+    "gq_gemm_f32": (I32, [P, P, P, I64, I64, I64, I64, I64, I64, I32, I32, I64, I64, I64, I64, I64, I64, I64, I64,
+                          F32, F32, P, I32, P, P]),
     "gq_prepare_weights": (I32, [P, I32, P, I64, I64, I64, P, P]),
     "gq_rtn_affine": (I32, [P, I32, I64, I64, I32, I32, I32, I32, P, P, P, P, I32, P]),
     "gq_rtn_mxfp": (I32, [P, I32, I64, I64, I32, P, P, P, P, I32, P]),
