@@ -128,6 +128,16 @@ int gq_hessian_spans_bf16(const void* X, int64_t n, int64_t c, int64_t ldx, cons
                           float* H, float alpha, float beta, void* workspace, size_t workspace_bytes, int32_t* status,
                           void* stream);
 
+/* Partial Hessians of an expert whose rows were cut into pieces (one grouped launch
+ * over all pieces), summed into the expert's first: for t < n_targets,
+ * H[targets[t]] += H[p] for p = pieces[piece_ptr[t]] .. pieces[piece_ptr[t+1] - 1],
+ * added in that order (the same bits as adding them one by one). H: fp32 [V, c, c];
+ * targets [n_targets], piece_ptr [n_targets + 1], pieces: int64 device arrays.
+ * No counterpart in the reference, which forms each expert's Hessian in one call
+ * (mlx_gptq/sequential.py:546-555). */
+int gq_hessian_merge_pieces(float* H, int64_t c, int64_t n_targets, const int64_t* targets,
+                            const int64_t* piece_ptr, const int64_t* pieces, void* stream);
+
 /* ------------------------------------------------------------------------
  * Solver pieces (mlx_gptq/gptq.py)
  * ------------------------------------------------------------------------ */

@@ -7,14 +7,16 @@
 // Cholesky factor of the reversed matrix: one factorization and one triangular
 // inversion (C^3/3 each) instead of factor + cholesky_inverse + factor. Both run
 // blocked on 64x64 tiles in float32: the factorization right-looking (diagonal
-// block factor + inverse, panel solve, trailing SYRK), the inversion by
-// doubling (inverses of 2^k-blocks combined pairwise with two GEMMs).
+// block factor + inverse in one CTA, then the panel solve, the next block column's
+// update and the rest of the trailing update as tcgen05 GEMMs, the rest on a side
+// stream), the inversion by doubling (inverses of 2^k-blocks combined pairwise
+// with two GEMMs).
 //
 // Column loop. One warp per weight row owns one block of bs columns in
 // registers (lane l holds columns l, l+32, ...): the clip search at each group
 // start, the per-column quantize / error / in-block rank-1 update. Err [B, R, bs]
 // goes to the workspace and the trailing update W[:, :, i2:] -= Err * U[i1:i2, i2:]
-// is a batched float32 GEMM.
+// is a batched float32 GEMM on the tensor cores (gq_tc_gemm.cu).
 #include <map>
 #include <mutex>
 #include <vector>
@@ -392,36 +394,67 @@ __global__ void build_reversed_kernel(const float* __restrict__ H, int64_t C, fl
   }
 }
 
+// 1 / sqrt(piv) for a positive pivot: the hardware reciprocal square root, or the
+// correctly rounded quotient for pivots below the smallest normal float.
+__device__ __forceinline__ float inv_sqrt_pivot(float piv) {
+  return piv >= 1.17549435e-38f ? rsqrtf(piv) : 1.0f / sqrtf(piv);
+}
+
 // One warp, 32 x 32 blocks held in registers, lane i owning row i (a[0..31]).
 // Cholesky, right-looking: the pivot and column k come from lane k / lane j by
-// shuffles; every update of a step is independent. Returns 0, or the failing
-// column + 1 (a non-positive pivot); a[] then holds L (lower; upper part garbage).
-__device__ __forceinline__ int warp_potrf32_reg(float (&a)[32], int lane) {
+// shuffles; every update of a step is independent. Each step multiplies by
+// 1/sqrt(pivot) instead of dividing. Returns 0, or the failing column + 1 (a
+// non-positive pivot); a[] then holds L (lower; upper part garbage) and inv_diag
+// this lane's 1 / L[lane][lane].
+__device__ __forceinline__ int warp_potrf32_reg(float (&a)[32], float& inv_diag, int lane) {
 #pragma unroll
   for (int k = 0; k < 32; ++k) {
     const float piv = __shfl_sync(0xFFFFFFFFu, a[k], k);
     if (!(piv > 0.0f)) return k + 1;  // uniform across the warp
-    const float d = sqrtf(piv);
-    const float lik = lane == k ? d : a[k] / d;
+    const float r = inv_sqrt_pivot(piv);
+    if (lane == k) inv_diag = r;
+    const float lik = lane == k ? piv * r : a[k] * r;
     a[k] = lane >= k ? lik : a[k];
 #pragma unroll
     for (int j = k + 1; j < 32; ++j) {
       const float ljk = __shfl_sync(0xFFFFFFFFu, lik, j);
-      a[j] = a[j] - lik * ljk;
+      a[j] = fmaf(-lik, ljk, a[j]);
     }
   }
   return 0;
 }
 
-// Column `lane` of X = L^-1 for a 32x32 lower L in shared memory: L x = e_lane.
-__device__ __forceinline__ void col_trinv32(float (&x)[32], const float* L, int ld, int lane) {
+// Column `lane` of X = L^-1 for a 32x32 lower L in shared memory: L x = e_lane,
+// forward substitution with the diagonal reciprocals inv_d[t].
+__device__ __forceinline__ void col_trinv32(float (&x)[32], const float* L, int ld, const float* inv_d, int lane) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) x[i] = i == lane ? 1.0f : 0.0f;
 #pragma unroll
   for (int t = 0; t < 32; ++t) {
-    x[t] = x[t] / L[t * ld + t];
+    x[t] = x[t] * inv_d[t];
 #pragma unroll
-    for (int i = t + 1; i < 32; ++i) x[i] = x[i] - L[i * ld + t] * x[t];
+    for (int i = t + 1; i < 32; ++i) x[i] = fmaf(-L[i * ld + t], x[t], x[i]);
+  }
+}
+
+// 32 x 32 x 32 shared-memory product for 128 threads, each a 4 x 2 block of outputs
+// (rows i0..i0+3, columns j0, j0+1) with eight independent accumulators:
+// acc[a][c] = sum_t P[(i0+a)*pld + t] * Q(t, j0+c), Q(t, j) = QT ? Q[j*qld + t] : Q[t*qld + j].
+template <bool QT>
+__device__ __forceinline__ void mm32_4x2(const float* P, int pld, const float* Q, int qld, int i0, int j0,
+                                         float (&acc)[4][2]) {
+#pragma unroll
+  for (int a = 0; a < 4; ++a) acc[a][0] = acc[a][1] = 0.0f;
+#pragma unroll
+  for (int t = 0; t < 32; ++t) {
+    const float q0 = QT ? Q[j0 * qld + t] : Q[t * qld + j0];
+    const float q1 = QT ? Q[(j0 + 1) * qld + t] : Q[t * qld + j0 + 1];
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+      const float pv = P[(i0 + a) * pld + t];
+      acc[a][0] = fmaf(pv, q0, acc[a][0]);
+      acc[a][1] = fmaf(pv, q1, acc[a][1]);
+    }
   }
 }
 
@@ -431,19 +464,34 @@ __device__ __forceinline__ void col_trinv32(float (&x)[32], const float* L, int 
 // the instruction cache), warp 0 factors the diagonal piece in registers
 // (L_hh = chol(A_hh)) and inverts it (X_hh = L_hh^-1); after the first half all four
 // warps form L21 = A21 X11^T and A22 -= L21 L21^T in shared memory; at the end
-// X21 = -X22 (L21 X11).
+// X21 = -X22 (L21 X11). The block is read with every load in flight at once; the
+// chain runs on fused multiply-adds and reciprocal square roots.
 __global__ void __launch_bounds__(128) potrf_diag_kernel(float* __restrict__ Hr, int64_t C, int k,
                                                          float* __restrict__ Dinv, FactorState st) {
   constexpr int LD = NB + 1;
   __shared__ float S[NB * LD];   // the block, then L (lower)
   __shared__ float X[NB * LD];   // L^-1 (lower)
   __shared__ float T[32 * 33];   // A21 / L21 X11 scratch
+  __shared__ float inv_d[NB];    // 1 / L[i][i]
   __shared__ int fail_s;
   const int64_t b = blockIdx.x;
   if (st.skip[b] || st.info[b]) return;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int i0 = (tid >> 4) * 4, j0 = (tid & 15) * 2;  // this thread's 4 x 2 block of 32 x 32 products
   float* blk = Hr + (b * C + int64_t(k) * NB) * C + int64_t(k) * NB;
-  for (int i = tid; i < NB * NB; i += 128) S[(i >> 6) * LD + (i & 63)] = blk[int64_t(i >> 6) * C + (i & 63)];
+  {
+    float v[NB * NB / 128];
+#pragma unroll
+    for (int r = 0; r < NB * NB / 128; ++r) {
+      const int i = tid + 128 * r;
+      v[r] = blk[int64_t(i >> 6) * C + (i & 63)];
+    }
+#pragma unroll
+    for (int r = 0; r < NB * NB / 128; ++r) {
+      const int i = tid + 128 * r;
+      S[(i >> 6) * LD + (i & 63)] = v[r];
+    }
+  }
   if (tid == 0) fail_s = 0;
   __syncthreads();
 #pragma unroll 1
@@ -453,15 +501,17 @@ __global__ void __launch_bounds__(128) potrf_diag_kernel(float* __restrict__ Hr,
       float a[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) a[j] = S[(o + lane) * LD + o + j];
-      const int f = warp_potrf32_reg(a, lane);
+      float inv = 0.0f;
+      const int f = warp_potrf32_reg(a, inv, lane);
       if (f) {
         if (lane == 0) fail_s = o + f;
       } else {
+        inv_d[o + lane] = inv;
 #pragma unroll
         for (int j = 0; j < 32; ++j)
           if (j <= lane) S[(o + lane) * LD + o + j] = a[j];
         __syncwarp();
-        col_trinv32(a, S + o * LD + o, LD, lane);
+        col_trinv32(a, S + o * LD + o, LD, inv_d + o, lane);
 #pragma unroll
         for (int i = 0; i < 32; ++i) X[(o + i) * LD + o + lane] = a[i];
       }
@@ -474,98 +524,53 @@ __global__ void __launch_bounds__(128) potrf_diag_kernel(float* __restrict__ Hr,
     if (h == 0) {
       for (int e = tid; e < 32 * 32; e += 128) T[(e >> 5) * 33 + (e & 31)] = S[(32 + (e >> 5)) * LD + (e & 31)];
       __syncthreads();
-      for (int e = tid; e < 32 * 32; e += 128) {  // L21 = A21 X11^T (X11 lower: t <= j)
-        const int i = e >> 5, j = e & 31;
-        float acc = 0.0f;
-        for (int t = 0; t <= j; ++t) acc = acc + T[i * 33 + t] * X[j * LD + t];
-        S[(32 + i) * LD + j] = acc;
+      float acc[4][2];
+      // L21 = A21 X11^T (X11 is lower with exact zeros above, so the full sum is exact)
+      mm32_4x2<true>(T, 33, X, LD, i0, j0, acc);
+#pragma unroll
+      for (int a = 0; a < 4; ++a) {
+        S[(32 + i0 + a) * LD + j0] = acc[a][0];
+        S[(32 + i0 + a) * LD + j0 + 1] = acc[a][1];
       }
       __syncthreads();
-      for (int e = tid; e < 32 * 32; e += 128) {  // A22 -= L21 L21^T (lower)
-        const int i = e >> 5, j = e & 31;
-        if (j > i) continue;
-        float acc = 0.0f;
-        for (int t = 0; t < 32; ++t) acc = acc + S[(32 + i) * LD + t] * S[(32 + j) * LD + t];
-        S[(32 + i) * LD + 32 + j] = S[(32 + i) * LD + 32 + j] - acc;
-      }
+      // A22 -= L21 L21^T (lower)
+      mm32_4x2<true>(S + 32 * LD, LD, S + 32 * LD, LD, i0, j0, acc);
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+          if (j0 + c <= i0 + a) S[(32 + i0 + a) * LD + 32 + j0 + c] -= acc[a][c];
       __syncthreads();
     }
   }
+#pragma unroll 4
   for (int i = tid; i < NB * NB; i += 128) {  // write L back (lower)
     const int r = i >> 6, c = i & 63;
     if (c <= r) blk[int64_t(r) * C + c] = S[r * LD + c];
   }
-  for (int e = tid; e < 32 * 32; e += 128) {  // T = L21 X11 (X11 lower: t >= j)
-    const int i = e >> 5, j = e & 31;
-    float acc = 0.0f;
-    for (int t = j; t < 32; ++t) acc = acc + S[(32 + i) * LD + t] * X[t * LD + j];
-    T[i * 33 + j] = acc;
-  }
-  __syncthreads();
-  for (int e = tid; e < 32 * 32; e += 128) {  // X21 = -X22 T (X22 lower: t <= i)
-    const int i = e >> 5, j = e & 31;
-    float acc = 0.0f;
-    for (int t = 0; t <= i; ++t) acc = acc + X[(32 + i) * LD + 32 + t] * T[t * 33 + j];
-    X[(32 + i) * LD + j] = -acc;
+  {
+    float acc[4][2];
+    mm32_4x2<false>(S + 32 * LD, LD, X, LD, i0, j0, acc);  // T = L21 X11
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+      T[(i0 + a) * 33 + j0] = acc[a][0];
+      T[(i0 + a) * 33 + j0 + 1] = acc[a][1];
+    }
+    __syncthreads();
+    mm32_4x2<false>(X + 32 * LD + 32, LD, T, 33, i0, j0, acc);  // X21 = -X22 T
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+      X[(32 + i0 + a) * LD + j0] = -acc[a][0];
+      X[(32 + i0 + a) * LD + j0 + 1] = -acc[a][1];
+    }
   }
   __syncthreads();
   float* D = Dinv + (b * (C / NB) + k) * NB * NB;
+#pragma unroll 4
   for (int i = tid; i < NB * NB; i += 128) {
     const int r = i >> 6, c = i & 63;
     D[i] = c <= r ? X[r * LD + c] : 0.0f;
   }
-}
-
-// Panel solve: A[i][k] = A[i][k] * L_kk^-T for block rows i > k (in place, one CTA per block).
-__global__ void __launch_bounds__(256) trsm_panel_kernel(float* __restrict__ Hr, int64_t C, int k,
-                                                         const float* __restrict__ Dinv, FactorState st) {
-  __shared__ __align__(16) float As[16][TS];
-  __shared__ __align__(16) float Bs[16][TS];
-  const int64_t b = blockIdx.y;
-  if (st.skip[b] || st.info[b]) return;
-  const int i = k + 1 + blockIdx.x;
-  float* blk = Hr + (b * C + int64_t(i) * NB) * C + int64_t(k) * NB;
-  const float* D = Dinv + (b * (C / NB) + k) * NB * NB;
-  float acc[4][4] = {};
-  tile_gemm<false, true>(blk, C, D, NB, NB, NB, NB, acc, As, Bs);  // out(r,c) = sum_t A(r,t) * D(c,t)
-  // all reads of blk are done (tile_gemm ends with a barrier): store in place
-  tile_store(blk, C, NB, NB, acc, 1.0f, 0.0f);
-}
-
-// Trailing update on block tiles (i, j) with k < j <= i: A_ij -= A_ik A_jk^T.
-// part 0: every such tile; part 1: the next block column only (j = k + 1), the
-// one the next diagonal factor and panel solve wait for; part 2: the rest
-// (j >= k + 2), which can run beside them.
-__global__ void __launch_bounds__(256) syrk_kernel(float* __restrict__ Hr, int64_t C, int k, int part,
-                                                   FactorState st) {
-  __shared__ __align__(16) float As[16][TS];
-  __shared__ __align__(16) float Bs[16][TS];
-  const int64_t b = blockIdx.y;
-  if (st.skip[b] || st.info[b]) return;
-  int ii, jj;
-  if (part == 1) {
-    ii = blockIdx.x;
-    jj = 0;
-  } else {
-    // linear tile index -> (ii, jj), 0 <= jj <= ii (over the triangle from column
-    // k + 1, or from k + 2 for part 2)
-    const int t = blockIdx.x;
-    ii = int((sqrtf(8.0f * float(t) + 1.0f) - 1.0f) * 0.5f);
-    while ((ii + 1) * (ii + 2) / 2 <= t) ++ii;
-    while (ii * (ii + 1) / 2 > t) --ii;
-    jj = t - ii * (ii + 1) / 2;
-    if (part == 2) {
-      ++ii;
-      ++jj;
-    }
-  }
-  const int i = k + 1 + ii, j = k + 1 + jj;
-  const float* Aik = Hr + (b * C + int64_t(i) * NB) * C + int64_t(k) * NB;
-  const float* Ajk = Hr + (b * C + int64_t(j) * NB) * C + int64_t(k) * NB;
-  float* Aij = Hr + (b * C + int64_t(i) * NB) * C + int64_t(j) * NB;
-  float acc[4][4] = {};
-  tile_gemm<false, true>(Aik, C, Ajk, C, NB, NB, NB, acc, As, Bs);
-  tile_store(Aij, C, NB, NB, acc, -1.0f, 1.0f);
 }
 
 // Linv initialisation: diagonal blocks = Dinv, everything else zero.
@@ -607,79 +612,161 @@ __global__ void escalate_kernel(int64_t B, FactorState st) {
 }
 
 // ---------------------------------------------------------------------------
-// affine column loop: one warp per (row, item); block columns [i1, i1 + 32*VPB)
+// affine column loop: a segment of LPR lanes per (row, item), 32 / LPR rows per
+// warp; block columns [i1, i1 + 16*LPR), lane `sl` of a segment holding columns
+// sl, sl + LPR, ... (16 slots). The per-column scalar work (quantize, error) is
+// done by the LPR lanes of the row's segment, not by a whole warp.
 // ---------------------------------------------------------------------------
-template <int VPL, int VPB>
-__global__ void __launch_bounds__(512) affine_block_kernel(float* __restrict__ W, const float* __restrict__ U,
-                                                           int64_t R, int64_t C, int64_t i1, int nslots, int bits,
-                                                           int nshrink, int storage, uint8_t* __restrict__ q,
-                                                           void* __restrict__ scales, void* __restrict__ biases,
-                                                           float* __restrict__ Err) {
-  constexpr int G = 32 * VPL, BS = 32 * VPB;
-  constexpr bool kSmemU = VPB <= 4;  // 128 x 128 U block (64 KB) staged in shared memory
+template <int W>
+__device__ __forceinline__ float seg_sum(float x) {
+#pragma unroll
+  for (int o = W / 2; o > 0; o >>= 1) x += __shfl_xor_sync(0xFFFFFFFFu, x, o);
+  return x;
+}
+template <int W>
+__device__ __forceinline__ float seg_min(float x) {
+#pragma unroll
+  for (int o = W / 2; o > 0; o >>= 1) x = fminf(x, __shfl_xor_sync(0xFFFFFFFFu, x, o));
+  return x;
+}
+template <int W>
+__device__ __forceinline__ float seg_max(float x) {
+#pragma unroll
+  for (int o = W / 2; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xFFFFFFFFu, x, o));
+  return x;
+}
+
+// choose_qparams (grid.py:167-212) over one segment-held group of GS * LPR values:
+// every lane of the segment returns the same storage-rounded (s, b); candidate
+// errors are butterfly-reduced inside the segment (bit-identical on its lanes) and
+// the first minimum wins (strict <), as in the reference. Candidates are evaluated
+// three at a time so their reductions overlap.
+template <int GS, int LPR>
+__device__ __forceinline__ void seg_choose_qparams(const float (&v)[GS], float maxq, const float* pr, const float* pf,
+                                                   int nshrink, int storage, float& s_best, float& b_best) {
+  float mn = v[0], mx = v[0];
+#pragma unroll
+  for (int k = 1; k < GS; ++k) {
+    mn = fminf(mn, v[k]);
+    mx = fmaxf(mx, v[k]);
+  }
+  mn = seg_min<LPR>(mn);
+  mx = seg_max<LPR>(mx);
+  const float rng = mx - mn;
+  float best = 0.0f;
+  constexpr int U = 3;
+  for (int i0 = 0; i0 < nshrink; i0 += U) {
+    float sc[U], bc[U], err[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = i0 + u < nshrink ? i0 + u : i0;
+      sc[u] = round_storage(rng * pr[i], storage);
+      bc[u] = round_storage(mn * pf[i], storage);
+      err[u] = 0.0f;
+#pragma unroll
+      for (int k = 0; k < GS; ++k) {
+        float q;
+        const float d = affine_quant(v[k], sc[u], bc[u], maxq, q) - v[k];
+        err[u] = fmaf(d, d, err[u]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) err[u] = seg_sum<LPR>(err[u]);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (i0 + u < nshrink && (i0 + u == 0 || err[u] < best)) {
+        best = err[u];
+        s_best = sc[u];
+        b_best = bc[u];
+      }
+    }
+  }
+}
+
+template <int LPR, int GS>
+__global__ void __launch_bounds__(128) affine_rows_kernel(float* __restrict__ W, const float* __restrict__ U,
+                                                          int64_t R, int64_t C, int64_t i1, int nslots, int bits,
+                                                          int nshrink, int storage, uint8_t* __restrict__ q,
+                                                          void* __restrict__ scales, void* __restrict__ biases,
+                                                          float* __restrict__ Err) {
+  constexpr int SL = 16, BS = SL * LPR, RPW = 32 / LPR, G = GS * LPR;
+  constexpr bool kSmemU = BS <= 128;  // 128 x 128 U block (64 KB) staged in shared memory
   __shared__ float pr[kMaxShrinks], pf[kMaxShrinks];
-  extern __shared__ float Us[];  // [BS][BS] when kSmemU
-  const int lane = threadIdx.x & 31;
+  extern __shared__ __align__(16) float Us[];  // [BS][BS] when kSmemU
+  const int lane = threadIdx.x & 31, sl = lane % LPR;
   const int64_t b = blockIdx.y;
   const float* Ug = U + b * C * C + i1 * C + i1;  // U1 = U[i1:i2, i1:i2], row stride C
   if (threadIdx.x < kMaxShrinks) shrink_factors(threadIdx.x, bits, pr[threadIdx.x], pf[threadIdx.x]);
-  if (kSmemU) {
-    const int n = nslots * 32;
-    for (int i = threadIdx.x; i < n * n; i += blockDim.x) Us[(i / n) * BS + (i % n)] = Ug[int64_t(i / n) * C + (i % n)];
+  if (kSmemU) {  // 16-byte loads, eight in flight per thread (rows of U are 16-byte aligned: C % 32 == 0)
+    const int n = nslots * LPR, nv = n / 4, total = n * nv;
+    for (int i0 = threadIdx.x; i0 < total; i0 += 8 * blockDim.x) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + u * blockDim.x;
+        if (i < total) v[u] = __ldg(reinterpret_cast<const float4*>(Ug + int64_t(i / nv) * C) + (i % nv));
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + u * blockDim.x;
+        if (i < total) reinterpret_cast<float4*>(Us + (i / nv) * BS)[i % nv] = v[u];
+      }
+    }
   }
   __syncthreads();
-  const int64_t r = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (r >= R) return;
+  const int64_t r = (int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5)) * RPW + lane / LPR;
+  const bool row_ok = r < R;  // rows past R still take part in the segment shuffles
   const int64_t ng = C / G;
-  float* wrow = W + (b * R + r) * C + i1;
-  // nslots = columns in this block / 32 (< VPB only for the last, partial block)
-  float w[VPB], dqv[VPB], ev[VPB], qv[VPB];
+  float* wrow = W + (b * R + (row_ok ? r : 0)) * C + i1;
+  // nslots = columns in this block / LPR (< SL only for the last, partial block)
+  float w[SL], dqv[SL], ev[SL], qv[SL];
 #pragma unroll
-  for (int k = 0; k < VPB; ++k) w[k] = k < nslots ? wrow[lane + 32 * k] : 0.0f;
+  for (int k = 0; k < SL; ++k) w[k] = row_ok && k < nslots ? wrow[sl + LPR * k] : 0.0f;
   const float maxq = float((1 << bits) - 1);
   float s = 0.0f, bb = 0.0f;
 #pragma unroll
-  for (int k = 0; k < VPB; ++k) {  // slot k = columns 32k .. 32k+31 of the block
+  for (int k = 0; k < SL; ++k) {  // slot k = columns LPR*k .. LPR*k + LPR-1 of the block
     if (k >= nslots) break;
-    if ((32 * k) % G == 0) {       // group start (gptq.py:250-256)
-      float v[VPL];
+    if (k % GS == 0) {  // group start (gptq.py:250-256)
+      float v[GS];
 #pragma unroll
-      for (int t = 0; t < VPL; ++t) v[t] = w[k + t];
-      warp_choose_qparams<VPL>(v, maxq, pr, pf, nshrink, storage, s, bb);
-      if (lane == 0) {
-        const int64_t g = (i1 + 32 * k) / G;
+      for (int t = 0; t < GS; ++t) v[t] = w[k + t];
+      seg_choose_qparams<GS, LPR>(v, maxq, pr, pf, nshrink, storage, s, bb);
+      if (sl == 0 && row_ok) {
+        const int64_t g = (i1 + LPR * k) / G;
         store_any(scales, (b * R + r) * ng + g, s, storage);
         store_any(biases, (b * R + r) * ng + g, bb, storage);
       }
     }
 #pragma unroll 1
-    for (int l = 0; l < 32; ++l) {
-      const int j = 32 * k + l;
-      const float wj = __shfl_sync(0xFFFFFFFFu, w[k], l);
+    for (int l = 0; l < LPR; ++l) {
+      const int j = LPR * k + l;
+      const float wj = __shfl_sync(0xFFFFFFFFu, w[k], l, LPR);
       float qj;
       const float dq = affine_quant(wj, s, bb, maxq, qj);
       const float* urow = kSmemU ? Us + j * BS : Ug + int64_t(j) * C;
       const float e = (wj - dq) / urow[j];
-      if (lane == l) {
+      if (sl == l) {
         dqv[k] = dq;
         ev[k] = e;
         qv[k] = qj;
       }
 #pragma unroll
-      for (int kk = k; kk < VPB; ++kk) {
-        const int col = 32 * kk + lane;
+      for (int kk = k; kk < SL; ++kk) {
+        const int col = LPR * kk + sl;
         if (kk < nslots && col > j) w[kk] = w[kk] - e * urow[col];
       }
     }
   }
+  if (!row_ok) return;
   uint8_t* qrow = q + (b * R + r) * C + i1;
   float* erow = Err + (b * R + r) * BS;
 #pragma unroll
-  for (int k = 0; k < VPB; ++k) {
+  for (int k = 0; k < SL; ++k) {
     if (k >= nslots) break;
-    wrow[lane + 32 * k] = dqv[k];
-    qrow[lane + 32 * k] = uint8_t(qv[k]);
-    erow[lane + 32 * k] = ev[k];
+    wrow[sl + LPR * k] = dqv[k];
+    qrow[sl + LPR * k] = uint8_t(qv[k]);
+    erow[sl + LPR * k] = ev[k];
   }
 }
 
@@ -781,14 +868,48 @@ extern "C" int gq_prepare_hinv(const float* H, int64_t B, int64_t C, float damp,
       potrf_diag_kernel<<<unsigned(B), 128, 0, s>>>(Hr, C, k, Dinv, st);
       const int m = nb - k - 1;
       if (m > 0) {
-        trsm_panel_kernel<<<dim3(unsigned(m), unsigned(B)), 256, 0, s>>>(Hr, C, k, Dinv, st);
+        // panel: L[i][k] = A[i][k] * Dinv_k^T for block rows i > k, in place
+        GemmBatch g{};
+        g.A = Hr + int64_t(k + 1) * NB * C + int64_t(k) * NB;
+        g.lda = C;
+        g.Bm = Dinv + int64_t(k) * NB * NB;
+        g.ldb = NB;
+        g.Cm = Hr + int64_t(k + 1) * NB * C + int64_t(k) * NB;
+        g.ldc = C;
+        g.sa_o = g.sc_o = C * C;
+        g.sb_o = C * NB;
+        g.n_inner = 1;
+        g.M = m * NB;
+        g.N = NB;
+        g.K = NB;
+        g.alpha = 1.0f;
+        g.beta = 0.0f;
+        g.skip = st.skip;
+        int r = tc_gemm(g, false, true, B, nullptr, s);
+        if (r != GQ_OK) return r;
         if (side_pending) GQ_CUDA_TRY(cudaStreamWaitEvent(s, ev_side, 0));
-        syrk_kernel<<<dim3(unsigned(m), unsigned(B)), 256, 0, s>>>(Hr, C, k, 1, st);
+        // next block column: A[i][k+1] -= L[i][k] L[k+1][k]^T, i > k
+        GemmBatch u = g;
+        u.Bm = g.A;
+        u.ldb = C;
+        u.sb_o = C * C;
+        u.Cm = Hr + int64_t(k + 1) * NB * C + int64_t(k + 1) * NB;
+        u.alpha = -1.0f;
+        u.beta = 1.0f;
+        r = tc_gemm(u, false, true, B, nullptr, s);
+        if (r != GQ_OK) return r;
         side_pending = false;
         if (m > 1) {
+          // the rest, beside the next steps: A[i][j] -= L[i][k] L[j][k]^T, k + 2 <= j <= i
           GQ_CUDA_TRY(cudaEventRecord(ev_main, s));
           GQ_CUDA_TRY(cudaStreamWaitEvent(side, ev_main, 0));
-          syrk_kernel<<<dim3(unsigned((m - 1) * m / 2), unsigned(B)), 256, 0, side>>>(Hr, C, k, 2, st);
+          GemmBatch w = u;
+          w.A = Hr + int64_t(k + 2) * NB * C + int64_t(k) * NB;
+          w.Bm = w.A;
+          w.Cm = Hr + int64_t(k + 2) * NB * C + int64_t(k + 2) * NB;
+          w.M = w.N = (m - 1) * NB;
+          r = tc_gemm(w, false, true, B, nullptr, side, true);
+          if (r != GQ_OK) return r;
           GQ_CUDA_TRY(cudaEventRecord(ev_side, side));
           side_pending = true;
         }
@@ -895,30 +1016,34 @@ extern "C" int gq_gptq_affine(float* W, const void* W_orig, int w_dtype, const f
   float* Err = reinterpret_cast<float*>(workspace);
   float* partials = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + align256(size_t(B) * R * bs * 4));
   const int nshrink = clip == GQ_CLIP_MSE ? kMaxShrinks : 1;
-  const dim3 cgrid(unsigned((R + 15) / 16), unsigned(B));  // 16 rows (warps) per CTA
   for (int64_t i1 = 0; i1 < C; i1 += bs) {
     // the last block may be partial (gptq.py:242); it is still a whole number of groups
     const int64_t n = std::min<int64_t>(bs, C - i1);
-    const int nslots = int(n / 32);
-#define AB(VPL, VPB)                                                                                               \
+#define AB(LPR, GS)                                                                                                \
   do {                                                                                                            \
-    const size_t sm = VPB <= 4 ? size_t(32 * VPB) * (32 * VPB) * 4 : 0;                                            \
-    if (sm) GQ_CUDA_TRY(cudaFuncSetAttribute(affine_block_kernel<VPL, VPB>,                                         \
+    const size_t sm = 16 * LPR <= 128 ? size_t(16 * LPR) * (16 * LPR) * 4 : 0;                                    \
+    if (sm) GQ_CUDA_TRY(cudaFuncSetAttribute(affine_rows_kernel<LPR, GS>,                                          \
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm)));               \
-    affine_block_kernel<VPL, VPB><<<cgrid, 512, sm, s>>>(W, U, R, C, i1, nslots, bits, nshrink, storage_dtype, q,  \
-                                                         scales, biases, Err);                                     \
+    const dim3 cgrid(unsigned((R + 4 * (32 / LPR) - 1) / (4 * (32 / LPR))), unsigned(B));                        \
+    affine_rows_kernel<LPR, GS><<<cgrid, 128, sm, s>>>(W, U, R, C, i1, int(n / LPR), bits, nshrink, storage_dtype, \
+                                                       q, scales, biases, Err);                                   \
   } while (0)
-    if (bs == 128) {
+    if (bs == 128) {  // 8 lanes per row, 4 rows per warp
       switch (group_size) {
-        case 32: AB(1, 4); break;
-        case 64: AB(2, 4); break;
-        default: AB(4, 4); break;
+        case 32: AB(8, 4); break;
+        case 64: AB(8, 8); break;
+        default: AB(8, 16); break;
       }
-    } else {
-      AB(8, 8);
+    } else {  // 256 columns: 16 lanes per row, 2 rows per warp
+      switch (group_size) {
+        case 32: AB(16, 2); break;
+        case 64: AB(16, 4); break;
+        case 128: AB(16, 8); break;
+        default: AB(16, 16); break;
+      }
     }
 #undef AB
-    int r = check_launch("affine_block_kernel");
+    int r = check_launch("affine_rows_kernel");
     if (r != GQ_OK) return r;
     const int64_t i2 = i1 + n;
     if (i2 < C) {

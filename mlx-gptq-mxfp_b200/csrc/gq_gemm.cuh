@@ -27,7 +27,10 @@ struct GemmBatch {
 // in a 3xTF32 split, accumulators in TMEM), for operands a tensor map can describe:
 // tc_gemm_usable says whether it takes this product; tc_gemm launches it. A device
 // wait that gives up writes GQ_ERR_TIMEOUT to *status (device int32, nullable).
+// lower_only (square products): 128 x 128 tiles strictly above the diagonal are not
+// computed; tiles on it are computed whole (their upper part included).
 bool tc_gemm_usable(const GemmBatch& p, bool trans_a, bool trans_b);
-int tc_gemm(const GemmBatch& p, bool trans_a, bool trans_b, int64_t batches, int32_t* status, cudaStream_t s);
+int tc_gemm(const GemmBatch& p, bool trans_a, bool trans_b, int64_t batches, int32_t* status, cudaStream_t s,
+            bool lower_only = false);
 
 }  // namespace gq

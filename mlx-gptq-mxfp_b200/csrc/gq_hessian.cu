@@ -774,6 +774,52 @@ extern "C" size_t gq_hessian_spans_workspace_size(const int64_t* host_spans, int
          align256(size_t(E) * size_t(gq::hess::two::tiles(c)) * 4);
 }
 
+namespace gq {
+namespace hess {
+// H[targets[t]] += H[p] for p = pieces[piece_ptr[t]], ..., pieces[piece_ptr[t+1] - 1], added
+// one after another in that order (bit-identical to adding them one by one).
+template <int V>
+__global__ void merge_pieces_kernel(float* __restrict__ H, int64_t cc, const int64_t* __restrict__ targets,
+                                    const int64_t* __restrict__ piece_ptr, const int64_t* __restrict__ pieces) {
+  const int64_t t = blockIdx.y;
+  const int64_t i = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) * V;
+  if (i >= cc) return;
+  float* dst = H + targets[t] * cc + i;
+  const int64_t p0 = piece_ptr[t], p1 = piece_ptr[t + 1];
+  if (V == 4) {
+    float4 acc = *reinterpret_cast<const float4*>(dst);
+    for (int64_t p = p0; p < p1; ++p) {
+      const float4 v = *reinterpret_cast<const float4*>(H + pieces[p] * cc + i);
+      acc.x += v.x, acc.y += v.y, acc.z += v.z, acc.w += v.w;
+    }
+    *reinterpret_cast<float4*>(dst) = acc;
+  } else {
+    float acc = *dst;
+    for (int64_t p = p0; p < p1; ++p) acc += H[pieces[p] * cc + i];
+    *dst = acc;
+  }
+}
+}  // namespace hess
+}  // namespace gq
+
+extern "C" int gq_hessian_merge_pieces(float* H, int64_t c, int64_t n_targets, const int64_t* targets,
+                                       const int64_t* piece_ptr, const int64_t* pieces, void* stream) {
+  GQ_REQUIRE(c > 0 && n_targets >= 0, "gq_hessian_merge_pieces: sizes");
+  if (n_targets == 0) return GQ_OK;
+  GQ_REQUIRE(H && targets && piece_ptr && pieces, "gq_hessian_merge_pieces: null pointer");
+  GQ_REQUIRE(n_targets < 65536, "gq_hessian_merge_pieces: too many targets");
+  const int64_t cc = c * c;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (cc % 4 == 0 && aligned16(H)) {
+    const dim3 grid(unsigned((cc / 4 + 255) / 256), unsigned(n_targets));
+    gq::hess::merge_pieces_kernel<4><<<grid, 256, 0, s>>>(H, cc, targets, piece_ptr, pieces);
+  } else {
+    const dim3 grid(unsigned((cc + 255) / 256), unsigned(n_targets));
+    gq::hess::merge_pieces_kernel<1><<<grid, 256, 0, s>>>(H, cc, targets, piece_ptr, pieces);
+  }
+  return check_launch("merge_pieces_kernel");
+}
+
 extern "C" int gq_hessian_spans_bf16(const void* X, int64_t n, int64_t c, int64_t ldx, const int64_t* host_spans,
                                     int64_t E, float* H, float alpha, float beta, void* workspace,
                                     size_t workspace_bytes, int32_t* status, void* stream) {

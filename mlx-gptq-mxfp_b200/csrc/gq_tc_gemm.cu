@@ -154,16 +154,26 @@ __device__ __forceinline__ void convert_row(const uint8_t* raw, uint8_t* hi, uin
   }
 }
 
+// Tile t -> (outer, inner item, m0, n0). lower: only tiles on or below the diagonal
+// of a square product (per item tiles_n * (tiles_n + 1) / 2, row by row).
 struct TileWalk {
   int64_t tiles, per_item;
-  int tiles_n, n_inner;
+  int tiles_n, n_inner, lower;
   const int32_t* skip;
   __device__ bool at(int64_t t, int64_t& o, int64_t& in, int& m0, int& n0) const {
     const int64_t z = t / per_item, r = t % per_item;
     o = z / n_inner;
     in = z % n_inner;
-    m0 = int(r / tiles_n) * BM;
-    n0 = int(r % tiles_n) * BN;
+    if (lower) {
+      int mi = int((sqrtf(8.0f * float(r) + 1.0f) - 1.0f) * 0.5f);
+      while (int64_t(mi + 1) * (mi + 2) / 2 <= r) ++mi;
+      while (int64_t(mi) * (mi + 1) / 2 > r) --mi;
+      m0 = mi * BM;
+      n0 = int(r - int64_t(mi) * (mi + 1) / 2) * BN;
+    } else {
+      m0 = int(r / tiles_n) * BM;
+      n0 = int(r % tiles_n) * BN;
+    }
     return !(skip && skip[o]);
   }
 };
@@ -444,8 +454,18 @@ static int sm_count() {
 template <bool AK, bool BK_>
 static int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const GemmBatch& p,
                      const TileWalk& w, int epi_mode, int32_t* status, cudaStream_t s) {
-  GQ_CUDA_TRY(cudaFuncSetAttribute(tc_gemm_kernel<AK, BK_>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   int(SMEM_BYTES)));
+  {  // the shared-memory opt-in, once per device
+    static std::mutex mu;
+    static std::map<int, bool> done;
+    int dev = 0;
+    GQ_CUDA_TRY(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lock(mu);
+    if (!done[dev]) {
+      GQ_CUDA_TRY(cudaFuncSetAttribute(tc_gemm_kernel<AK, BK_>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(SMEM_BYTES)));
+      done[dev] = true;
+    }
+  }
   const int sms = sm_count();
   const int64_t grid = std::min<int64_t>(w.tiles, sms > 0 ? sms : 148);
   tc_gemm_kernel<AK, BK_><<<unsigned(grid), THREADS, SMEM_BYTES, s>>>(ma, mb, mc, p, w, epi_mode, status);
@@ -467,8 +487,10 @@ bool tc_gemm_usable(const GemmBatch& p, bool trans_a, bool trans_b) {
          ok(p.Bm, p.ldb, p.sb_o, p.sb_i);
 }
 
-int tc_gemm(const GemmBatch& p, bool trans_a, bool trans_b, int64_t batches, int32_t* status, cudaStream_t s) {
+int tc_gemm(const GemmBatch& p, bool trans_a, bool trans_b, int64_t batches, int32_t* status, cudaStream_t s,
+            bool lower_only) {
   if (batches <= 0 || p.M <= 0 || p.N <= 0) return GQ_OK;
+  GQ_REQUIRE(!lower_only || p.M == p.N, "tc_gemm: lower_only needs a square product");
   GQ_REQUIRE(tc_gemm_usable(p, trans_a, trans_b), "tc_gemm: operand layout not supported");
   GQ_REQUIRE(batches % p.n_inner == 0, "tc_gemm: batch count not a multiple of the inner batch");
   const int64_t n_outer = batches / p.n_inner;
@@ -491,7 +513,9 @@ int tc_gemm(const GemmBatch& p, bool trans_a, bool trans_b, int64_t batches, int
   }
   tcg::TileWalk w;
   w.tiles_n = (p.N + tcg::BN - 1) / tcg::BN;
-  w.per_item = int64_t((p.M + tcg::BM - 1) / tcg::BM) * w.tiles_n;
+  w.lower = lower_only ? 1 : 0;
+  w.per_item = lower_only ? int64_t(w.tiles_n) * (w.tiles_n + 1) / 2
+                          : int64_t((p.M + tcg::BM - 1) / tcg::BM) * w.tiles_n;
   w.tiles = w.per_item * batches;
   w.n_inner = p.n_inner;
   w.skip = p.skip;

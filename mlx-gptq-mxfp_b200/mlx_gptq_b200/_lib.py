@@ -41,6 +41,7 @@ SIGNATURES = {
     "gq_hessian_grouped_bf16": (I32, [P, I64, I64, I64, P, P, P, I64, P, F32, F32, P, SZ, P, P]),
     "gq_hessian_spans_workspace_size": (SZ, [P, I64, I64]),
     "gq_hessian_spans_bf16": (I32, [P, I64, I64, I64, P, I64, P, F32, F32, P, SZ, P, P]),
+    "gq_hessian_merge_pieces": (I32, [P, I64, I64, P, P, P, P]),
     "gq_dead_columns": (I32, [P, I64, I64, P, P]),
     "gq_mx_prepare_hinv": (I32, [P, I64, I64, F32, P, P, P, P]),
     "gq_prepare_hinv_workspace_size": (SZ, [I64, I64]),

@@ -23,6 +23,7 @@ from dataclasses import dataclass
 
 import torch
 
+from . import _lib as L
 from .capture import hessian_grouped, hessian_spans, hessian_tile_count, hessian_tiles_per_wave
 from .pipeline import lpt_partition
 
@@ -58,6 +59,25 @@ class PieceLayout:
     token_idx: torch.Tensor | None = None
     perm: torch.Tensor | None = None
     spans: list[tuple[int, int]] | None = None
+    merge: tuple[torch.Tensor, torch.Tensor, torch.Tensor] | None = None  # device (targets, piece_ptr, pieces)
+
+    def merge_plan(self, device) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor] | None:
+        """The extra pieces grouped by expert, in piece order, as device arrays for
+        gq_hessian_merge_pieces (built once; None without extra pieces)."""
+        if not self.extra:
+            return None
+        if self.merge is None or self.merge[0].device != torch.device(device):
+            by_expert: dict[int, list[int]] = {}
+            for j, (i, _) in enumerate(self.extra):
+                by_expert.setdefault(i, []).append(self.n + j)
+            targets = sorted(by_expert)
+            ptr, pieces = [0], []
+            for i in targets:
+                pieces += by_expert[i]
+                ptr.append(len(pieces))
+            mk = lambda v: torch.tensor(v, dtype=torch.int64, device=device)
+            self.merge = (mk(targets), mk(ptr), mk(pieces))
+        return self.merge
 
 
 def piece_layout(token_idx: torch.Tensor | None, offsets, experts: list[int], c: int, device,
@@ -100,21 +120,26 @@ def piece_layout(token_idx: torch.Tensor | None, offsets, experts: list[int], c:
 @torch.no_grad()
 def expert_hessians(X: torch.Tensor, layout: PieceLayout, out: torch.Tensor | None = None) -> torch.Tensor:
     """H [n, C, C] float32 of the layout's experts: one grouped launch over all pieces,
-    then each expert's extra pieces added to its first, in piece order."""
+    then one launch adding each expert's extra pieces to its first, in piece order."""
     V = layout.offsets.numel() - 1
     if layout.spans is not None:
         H = hessian_spans(X, layout.spans, H=out)
     else:
         H = hessian_grouped(X, layout.token_idx, layout.offsets, V, H=out)
-    for j, (i, _) in enumerate(layout.extra):
-        H[i].add_(H[layout.n + j])
+    plan = layout.merge_plan(H.device)
+    if plan is not None:  # every expert's extra pieces onto its first, in piece order, one launch
+        t, ptr, pieces = plan
+        L.check(L.lib().gq_hessian_merge_pieces(L.ptr(H), H.shape[-1], t.numel(), L.ptr(t), L.ptr(ptr),
+                                                L.ptr(pieces), L.stream_ptr(H.device)), "hessian_merge_pieces")
     return H[:layout.n]
 
 
 class Exchange:
     """All-gather of per-rank expert outputs (leading dim = the rank's experts) into
     expert order on every rank: one padded all_gather_into_tensor per tensor, issued
-    asynchronously so it overlaps the work that follows; wait() reorders."""
+    asynchronously; a side stream waits for each gather and reorders its result while
+    the caller's stream goes on with the work that follows; wait() joins the side
+    stream."""
 
     def __init__(self, shares: list[list[int]], rank: int, group, device):
         self.shares, self.rank, self.group = shares, rank, group
@@ -127,6 +152,8 @@ class Exchange:
             slot += [r * self.m + i for i in range(len(s))]
         self.src = torch.tensor(slot, dtype=torch.long, device=device)
         self.dst = torch.tensor(order, dtype=torch.long, device=device)
+        dev = torch.device(device)
+        self.side = torch.cuda.Stream(device=dev) if dev.type == "cuda" else None
         self.pending = []
 
     def start(self, t: torch.Tensor, out: torch.Tensor) -> None:
@@ -140,10 +167,20 @@ class Exchange:
             pad[: t.shape[0]].copy_(t)
         buf = torch.empty((world * self.m,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
         work = dist.all_gather_into_tensor(buf, pad.contiguous(), group=self.group, async_op=True)
-        self.pending.append((work, buf, out, pad))
+        if self.side is None:  # host tensors (gloo): reorder in wait()
+            self.pending.append((work, buf, out, pad))
+            return
+        self.side.wait_stream(torch.cuda.current_stream(t.device))  # out and the index arrays are ready
+        with torch.cuda.stream(self.side):
+            work.wait()  # the side stream waits for the gather, the caller's does not
+            out.index_copy_(0, self.dst, buf.index_select(0, self.src))
+        self.pending.append((None, buf, out, pad))  # buffers live until the caller's stream has joined
 
     def wait(self) -> None:
+        if self.side is not None:
+            torch.cuda.current_stream(self.side.device).wait_stream(self.side)
         for work, buf, out, _ in self.pending:
-            work.wait()
-            out.index_copy_(0, self.dst, buf.index_select(0, self.src))
+            if work is not None:
+                work.wait()
+                out.index_copy_(0, self.dst, buf.index_select(0, self.src))
         self.pending = []

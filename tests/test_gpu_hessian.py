@@ -193,3 +193,39 @@ def test_hessian_spans_match_per_expert_dense(c):
     torch.testing.assert_close(H2, 2.0 * H, rtol=0, atol=0)
     with pytest.raises(ValueError):
         hessian_spans(X, [(4990, 20)])  # past the last row
+
+
+@pytest.mark.parametrize("form", ["gather", "spans"])
+def test_expert_pieces_merged_in_order(form):
+    """Heavy experts cut into pieces (one grouped launch over the pieces) and summed by
+    the one-launch merge: bit for bit the pieces' Hessians added one by one in piece
+    order, and within float32 rounding of each expert's dense Hessian."""
+    from mlx_gptq_b200 import hessian_from_rows
+    from mlx_gptq_b200.capture import hessian_grouped, hessian_spans
+    from mlx_gptq_b200.expert_batch import expert_hessians, piece_layout
+
+    c = 256
+    g = torch.Generator(device="cuda").manual_seed(7)
+    counts = [3000, 5, 0, 700, 1999]
+    off = [0]
+    for n in counts:
+        off.append(off[-1] + n)
+    X = torch.randn(off[-1], c, generator=g, device="cuda").to(torch.bfloat16)
+    tok = torch.randperm(off[-1], generator=g, device="cuda").to(torch.int32)
+    lay = piece_layout(tok if form == "gather" else None, torch.tensor(off), list(range(len(counts))), c, "cuda",
+                       waves=1.0, tiles_per_wave=4)
+    assert lay.extra  # the heavy experts were cut
+    V = lay.offsets.numel() - 1
+    raw = (hessian_grouped(X, lay.token_idx, lay.offsets, V) if form == "gather" else hessian_spans(X, lay.spans))
+    for j, (i, _) in enumerate(lay.extra):
+        raw[i].add_(raw[lay.n + j])
+    H = expert_hessians(X, lay)
+    assert torch.equal(H, raw[: lay.n])
+    for e, n in enumerate(counts):
+        rows = X[tok[off[e]:off[e + 1]].long()] if form == "gather" else X[off[e]:off[e + 1]]
+        if n == 0:
+            assert int(torch.count_nonzero(H[e])) == 0
+            continue
+        ref = hessian_from_rows(rows).double()
+        err = float((H[e].double() - ref).norm() / ref.norm())
+        assert err < 1e-5, (form, e, err)
