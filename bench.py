@@ -157,13 +157,13 @@ class C3Step:
         self.H_gu = torch.empty(self.lay_gu.offsets.numel() - 1, C3_H, C3_H, device=device)
         self.H_dn = torch.empty(self.lay_dn.offsets.numel() - 1, C3_I, C3_I, device=device)
         self.exchange = Exchange(inp.shares, rank, group, device) if world > 1 else None
-        E = C3_EXPERTS
         self.all_out = None
-        if world > 1:
-            self.all_out = {"codes_gu": torch.empty(E, 2 * C3_I, C3_H // 2, dtype=torch.uint8, device=device),
-                            "scales_gu": torch.empty(E, 2 * C3_I, C3_H // 32, dtype=torch.uint8, device=device),
-                            "codes_dn": torch.empty(E, C3_H, C3_I // 2, dtype=torch.uint8, device=device),
-                            "scales_dn": torch.empty(E, C3_H, C3_I // 32, dtype=torch.uint8, device=device)}
+        if world > 1:  # every expert's codes and scales on every rank, rank-major (Exchange)
+            ex, u8 = self.exchange, torch.uint8
+            self.all_out = {"codes_gu": ex.buffer((2 * C3_I, C3_H // 2), u8),
+                            "scales_gu": ex.buffer((2 * C3_I, C3_H // 32), u8),
+                            "codes_dn": ex.buffer((C3_H, C3_I // 2), u8),
+                            "scales_dn": ex.buffer((C3_H, C3_I // 32), u8)}
         self.events = None
         self.last = None
 
@@ -221,7 +221,8 @@ class C3Step:
         """Every expert's codes and scales after the step (this rank's when N = 1)."""
         gu, dn = self.last
         if self.all_out is not None:
-            return [self.all_out[k] for k in ("codes_gu", "scales_gu", "codes_dn", "scales_dn")]
+            return [self.exchange.expert_order(self.all_out[k]) for k in ("codes_gu", "scales_gu", "codes_dn",
+                                                                          "scales_dn")]
         return [gu.codes, gu.scales, dn.codes, dn.scales]
 
 

@@ -134,53 +134,92 @@ def expert_hessians(X: torch.Tensor, layout: PieceLayout, out: torch.Tensor | No
     return H[:layout.n]
 
 
-class Exchange:
-    """All-gather of per-rank expert outputs (leading dim = the rank's experts) into
-    expert order on every rank: one padded all_gather_into_tensor per tensor, issued
-    asynchronously; a side stream waits for each gather and reorders its result while
-    the caller's stream goes on with the work that follows; wait() joins the side
-    stream."""
+def _symmetric_memory():
+    """torch's symmetric-memory module when it can map peer buffers here, else None."""
+    try:
+        from torch.distributed import _symmetric_memory as symm
+    except ImportError:
+        return None
+    return symm if hasattr(symm, "empty") and hasattr(symm, "rendezvous") else None
 
-    def __init__(self, shares: list[list[int]], rank: int, group, device):
+
+class Exchange:
+    """Every rank's expert outputs (leading dim = the rank's experts) handed to every
+    rank, one buffer per tensor laid out rank-major: rank r's experts fill slots
+    r*m .. r*m + n_r - 1 (m = the largest share), slot_of[e] names expert e's slot and
+    expert_order() gives the [E, ...] view in expert order.
+
+    On GPUs that map each other's memory (one process per GPU, NVLink) the buffers are
+    symmetric allocations and start() pushes this rank's slab into every peer's
+    buffer with copy-engine copies on a side stream, so no SM of any rank works on the
+    exchange; wait() closes it with a one-element NCCL all-reduce issued after the
+    pushes (a rank passes it only once every rank's pushes have landed) and joins the
+    side stream. Elsewhere (host tensors, gloo) start() is an asynchronous
+    all_gather_into_tensor into the same layout. A buffer must not be read between a
+    start() into it and the wait() that follows, nor written by the caller at all."""
+
+    def __init__(self, shares: list[list[int]], rank: int, group, device, push: bool | None = None):
         self.shares, self.rank, self.group = shares, rank, group
+        self.world = len(shares)
         self.m = max(len(s) for s in shares)
-        order = [e for s in shares for e in s]
-        self.E = len(order)
-        # position of expert e's slab in the gathered [world * m] buffer
-        slot = []
-        for r, s in enumerate(shares):
-            slot += [r * self.m + i for i in range(len(s))]
-        self.src = torch.tensor(slot, dtype=torch.long, device=device)
-        self.dst = torch.tensor(order, dtype=torch.long, device=device)
-        dev = torch.device(device)
-        self.side = torch.cuda.Stream(device=dev) if dev.type == "cuda" else None
+        self.slot_of = {}
+        for r, sh in enumerate(shares):
+            for i, e in enumerate(sh):
+                self.slot_of[e] = r * self.m + i
+        self.E = len(self.slot_of)
+        self.device = torch.device(device)
+        self.order = torch.tensor([self.slot_of[e] for e in range(self.E)], dtype=torch.long, device=self.device)
+        if push is None:
+            push = self.device.type == "cuda" and self.world > 1 and _symmetric_memory() is not None
+        self.push = push
+        self.side = torch.cuda.Stream(device=self.device) if push else None
+        self.peers = {}  # buffer data_ptr -> the buffer as mapped on every rank
+        self.flag = torch.zeros(1, dtype=torch.int32, device=self.device) if push else None
         self.pending = []
 
+    def buffer(self, tail, dtype) -> torch.Tensor:
+        """A rank-major output buffer [world * m, *tail] (symmetric when pushing)."""
+        shape = (self.world * self.m,) + tuple(tail)
+        if not self.push:
+            return torch.empty(shape, dtype=dtype, device=self.device)
+        symm = _symmetric_memory()
+        t = symm.empty(shape, dtype=dtype, device=self.device)
+        h = symm.rendezvous(t, self.group.group_name)
+        self.peers[t.data_ptr()] = [t if p == self.rank else h.get_buffer(p, shape, dtype)
+                                    for p in range(self.world)]
+        return t
+
     def start(self, t: torch.Tensor, out: torch.Tensor) -> None:
-        """Gather this rank's t [n_r, ...] from every rank into out [E, ...] (expert order)."""
+        """Hand this rank's t [n_r, ...] to every rank's out (a buffer() of the same tail)."""
         import torch.distributed as dist
 
-        world = len(self.shares)
+        lo = self.rank * self.m
+        if self.push:
+            self.side.wait_stream(torch.cuda.current_stream(self.device))  # t is complete
+            with torch.cuda.stream(self.side):
+                for dst in self.peers[out.data_ptr()]:
+                    dst[lo:lo + t.shape[0]].copy_(t)
+            t.record_stream(self.side)
+            return
         pad = t
         if t.shape[0] != self.m:
             pad = torch.zeros((self.m,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
             pad[: t.shape[0]].copy_(t)
-        buf = torch.empty((world * self.m,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
-        work = dist.all_gather_into_tensor(buf, pad.contiguous(), group=self.group, async_op=True)
-        if self.side is None:  # host tensors (gloo): reorder in wait()
-            self.pending.append((work, buf, out, pad))
-            return
-        self.side.wait_stream(torch.cuda.current_stream(t.device))  # out and the index arrays are ready
-        with torch.cuda.stream(self.side):
-            work.wait()  # the side stream waits for the gather, the caller's does not
-            out.index_copy_(0, self.dst, buf.index_select(0, self.src))
-        self.pending.append((None, buf, out, pad))  # buffers live until the caller's stream has joined
+        work = dist.all_gather_into_tensor(out, pad.contiguous(), group=self.group, async_op=True)
+        self.pending.append((work, pad))
 
     def wait(self) -> None:
-        if self.side is not None:
-            torch.cuda.current_stream(self.side.device).wait_stream(self.side)
-        for work, buf, out, _ in self.pending:
-            if work is not None:
-                work.wait()
-                out.index_copy_(0, self.dst, buf.index_select(0, self.src))
+        import torch.distributed as dist
+
+        if self.push:
+            with torch.cuda.stream(self.side):
+                dist.all_reduce(self.flag, group=self.group, async_op=True).wait()
+            torch.cuda.current_stream(self.device).wait_stream(self.side)
+            return
+        for work, _ in self.pending:
+            work.wait()
         self.pending = []
+
+    def expert_order(self, out: torch.Tensor) -> torch.Tensor:
+        """out [world * m, ...] -> [E, ...] in expert order (a gather: a new tensor)."""
+        return out.index_select(0, self.order)

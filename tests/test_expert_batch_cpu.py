@@ -52,15 +52,18 @@ def _exchange_rank(rank, world, port, out):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     shares = [[0, 3, 4], [1, 2]]
     ex = Exchange(shares, rank, dist.group.WORLD, "cpu")
+    assert not ex.push  # host tensors: the all_gather form
     mine = torch.tensor([[e * 10, e * 10 + 1] for e in shares[rank]], dtype=torch.int32)
-    full = torch.empty(5, 2, dtype=torch.int32)
+    full = ex.buffer((2,), torch.int32)
+    assert full.shape == (6, 2)  # rank-major, 3 slots per rank
     ex.start(mine, full)
     ex.wait()
-    out[rank] = full.tolist()
+    assert [ex.slot_of[e] for e in range(5)] == [0, 3, 4, 1, 2]
+    out[rank] = ex.expert_order(full).tolist()
     dist.destroy_process_group()
 
 
-def test_exchange_gathers_into_expert_order():
+def test_exchange_gathers_every_expert_to_every_rank():
     import torch.multiprocessing as mp
 
     port = 29500 + os.getpid() % 1000
