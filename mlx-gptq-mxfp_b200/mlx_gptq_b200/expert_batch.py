@@ -31,14 +31,20 @@ from .pipeline import lpt_partition
 # the groupwise MXFP column loop runs ~1.1e11 elements/s on a B200, the Hessian
 # ~8e17 multiply-adds/s, so one element costs about as much as 7,000 Hessian units.
 SOLVE_UNITS_PER_ELEM = 7.0e3
+# An expert without tokens takes the data-free RTN path (layer.solve_experts), a handful
+# of small launches costing about 0.1 ms per parameter on a B200 (measured on the C3
+# split): about as much as the Hessians of 30,000 tokens of a 2048/768 expert.
+RTN_FALLBACK_UNITS = 1.5e11
 
 
 def plan_experts(counts, world: int, hess_dims, solve_elems: int) -> list[list[int]]:
     """Longest-processing-time split of experts over `world` ranks: cost(e) =
     counts[e] * sum(C^2 over the expert's Hessians) + SOLVE_UNITS_PER_ELEM * elements
-    solved per expert. Returns the sorted expert list of every rank."""
+    solved per expert (+ RTN_FALLBACK_UNITS for an expert without tokens). Returns the
+    sorted expert list of every rank."""
     per_token = float(sum(c * c for c in hess_dims))
-    costs = [float(n) * per_token + SOLVE_UNITS_PER_ELEM * solve_elems for n in counts]
+    costs = [float(n) * per_token + SOLVE_UNITS_PER_ELEM * solve_elems + (RTN_FALLBACK_UNITS if int(n) == 0 else 0.0)
+             for n in counts]
     return lpt_partition(costs, world)
 
 

@@ -109,7 +109,8 @@ def solve_experts(W: torch.Tensor, H: torch.Tensor, counts, mode: str = "mxfp4",
     sol = solve_mxfp_packed(W, f, mode, algorithm, wdq_dtype, want_rel, check_info=check_info)
     empty = [e for e, c in enumerate(list(counts)) if int(c) == 0]
     if empty:
-        idx = torch.tensor(empty, dtype=torch.long, device=W.device)
+        # pinned and non-blocking: the index upload does not make the host wait for the GPU
+        idx = torch.tensor(empty, dtype=torch.long).pin_memory().to(W.device, non_blocking=True)
         We = L.aligned(W.index_select(0, idx))
         n, R, C = We.shape
         q = torch.empty(n, R, C, dtype=torch.uint8, device=W.device)
