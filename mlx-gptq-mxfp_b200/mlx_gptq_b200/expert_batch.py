@@ -19,6 +19,7 @@ are a view of the launch's output, not a copy.
 
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 
 import torch
@@ -141,7 +142,10 @@ def expert_hessians(X: torch.Tensor, layout: PieceLayout, out: torch.Tensor | No
 
 
 def _symmetric_memory():
-    """torch's symmetric-memory module when it can map peer buffers here, else None."""
+    """torch's symmetric-memory module when it can map peer buffers here, else None.
+    The exchange needs only peer mappings, so its buffers are kept out of NVLink
+    multicast objects."""
+    os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
     try:
         from torch.distributed import _symmetric_memory as symm
     except ImportError:
