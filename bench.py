@@ -11,8 +11,10 @@ down inputs silu(x Wg^T) * (x Wu^T) per routed slot (4,194,304 slots). One step 
 grouped tcgen05 Hessians of every expert (gate_up over X rows, down over the slot
 activations), damped 32x32 block factors, the MXFP4 column loops writing
 nibble-packed codes, E8M0 scales, bf16 W_dq and rel_err, data-free RTN for the
-experts without tokens, and (N > 1) the exchange: one all-gather of codes and
-scales per parameter, so every rank ends the step with every expert's outputs.
+experts without tokens, and (N > 1) the exchange: per parameter, every rank pushes
+its experts' codes and scales into every peer's symmetric buffer with copy-engine
+copies over NVLink (an all-gather without SM work, closed by a one-element NCCL
+all-reduce), so every rank ends the step with every expert's outputs.
 Under torchrun the experts are split over the ranks by longest processing time
 (strong scaling: the batch is fixed, `value` = the batch's elements / step time,
 max over ranks). Inputs (2.1 GB of X, 6.4 GB of slot activations) exceed the
@@ -932,8 +934,9 @@ def run_c3(args, ws, rank, local):
         "config": {"workload": C3_WORKLOAD, "elems_per_step": C3_ELEMS, "tokens": 524288,
                    "zero_token_experts": inp.zero_experts, "zipf_bias_scale": inp.bias_scale,
                    "l2": "inputs larger than L2 (X 2.1 GB, slot activations 6.4 GB); no flush",
-                   "parallelism": (f"experts split over {ws} ranks (LPT), one all-gather of codes + scales per "
-                                   "parameter inside the step" if ws > 1 else "1 GPU")},
+                   "parallelism": (f"experts split over {ws} ranks (LPT); per parameter codes + scales pushed to "
+                                   "every rank (copy engines into symmetric buffers, NCCL all-reduce to close) "
+                                   "inside the step" if ws > 1 else "1 GPU")},
         "hessian_tflops": sum(2.0 * n * (C3_H ** 2 + C3_I ** 2) for n in inp.counts) / (ms_step / 1e3) / 1e12,
         "stages_ms_rank0": {"hessian_gate_up": stage[0], "solve_gate_up": stage[1], "hessian_down": stage[2],
                             "solve_down": stage[3], "exchange_wait": stage[4]},
