@@ -229,3 +229,27 @@ def test_expert_pieces_merged_in_order(form):
         ref = hessian_from_rows(rows).double()
         err = float((H[e].double() - ref).norm() / ref.norm())
         assert err < 1e-5, (form, e, err)
+
+
+@pytest.mark.parametrize("c", [5, 64])  # odd c: the element-wise path; c % 4 == 0 after squaring: float4
+def test_merge_pieces_entry_point_order_and_bits(c):
+    """gq_hessian_merge_pieces through the C ABI: each target gets its pieces added one
+    after another in list order (bit-identical to sequential adds), other slabs untouched."""
+    import ctypes
+
+    from mlx_gptq_b200 import _lib
+
+    g = torch.Generator(device="cuda").manual_seed(c)
+    H = torch.randn(7, c, c, generator=g, device="cuda") * torch.logspace(-3, 3, 7, device="cuda")[:, None, None]
+    targets, lists = [0, 2], [[5, 3, 6], [4]]
+    want = H.clone()
+    for t, ps in zip(targets, lists):
+        for p in ps:
+            want[t] += want[p]
+    dev = lambda v: torch.tensor(v, dtype=torch.int64, device="cuda")
+    tg, ptr, pcs = dev(targets), dev([0, 3, 4]), dev([5, 3, 6, 4])
+    p = lambda t: ctypes.c_void_p(t.data_ptr())
+    st = _lib.lib().gq_hessian_merge_pieces(p(H), c, 2, p(tg), p(ptr), p(pcs), None)
+    torch.cuda.synchronize()
+    assert st == _lib.GQ_OK
+    assert torch.equal(H, want)
