@@ -164,10 +164,11 @@ int gq_mx_prepare_hinv(const float* H, int64_t B, int64_t C, float damp, float* 
  * attempts. SYNCHRONIZES `stream` after each attempt to read the per-item
  * status. Returns GQ_ERR_NOT_PD if an item still fails (info[b] != 0).
  * H: fp32 [B, C, C] (C % 64 == 0); U: fp32 [B, C, C] (upper; lower part zero);
- * info: int32 [B]; damp_used: fp32 [B] (nullable). */
+ * info: int32 [B]; damp_used: fp32 [B] (nullable). status: optional device int32;
+ * a bounded wait of the tensor-core GEMMs that gives up writes GQ_ERR_TIMEOUT there. */
 size_t gq_prepare_hinv_workspace_size(int64_t B, int64_t C);
 int gq_prepare_hinv(const float* H, int64_t B, int64_t C, float damp, float* U, int32_t* info, float* damp_used,
-                    void* workspace, size_t workspace_bytes, void* stream);
+                    void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
 
 /* MXFP GPTQ (gptq.py:69-180): per 32-column group, sequential GPTQ with a fixed
  * E8M0 scale (groupwise: the RTN scale; safe-scale-search: the scale offset with
@@ -226,11 +227,12 @@ int gq_gptq_mxfp_noalloc(const void* W, int w_dtype, const float* H, const float
  *    untouched originals for rel_err (nullable).
  * U: from gq_prepare_hinv. q: uint8 [B, R, C]; scales / biases: [B, R, C/G] of
  * storage_dtype (GQ_BF16 / GQ_F16 / GQ_F32); rel_err fp32 [B] (nullable).
- * G % 32 == 0 and G <= 256. */
+ * G % 32 == 0 and G <= 256. status: optional device int32 (as in gq_prepare_hinv). */
 size_t gq_gptq_affine_workspace_size(int64_t B, int64_t R, int64_t C, int group_size, int block_size);
 int gq_gptq_affine(float* W, const void* W_orig, int w_dtype, const float* U, int64_t B, int64_t R, int64_t C,
                    int bits, int group_size, int block_size, int clip, int storage_dtype, uint8_t* q, void* scales,
-                   void* biases, float* rel_err, void* workspace, size_t workspace_bytes, void* stream);
+                   void* biases, float* rel_err, void* workspace, size_t workspace_bytes, int32_t* status,
+                   void* stream);
 
 /* The float32 GEMM the affine solver runs its trailing updates and factor
  * products on, exposed for testing: per batch item z = outer * n_inner + inner,

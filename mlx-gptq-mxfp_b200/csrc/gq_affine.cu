@@ -344,9 +344,9 @@ static int launch_gemm(const GemmBatch& p, bool trans_a, bool trans_b, int64_t b
 // Products whose tiles fill the 128 x 128 tensor-core tile go to tc_gemm (TMA-fed
 // tcgen05, gq_tc_gemm.cu); smaller ones and layouts a tensor map cannot describe to
 // the mma.sync kernels above.
-static int gemm(const GemmBatch& p, bool trans_a, bool trans_b, int64_t batches, cudaStream_t s) {
+static int gemm(const GemmBatch& p, bool trans_a, bool trans_b, int64_t batches, int32_t* status, cudaStream_t s) {
   if (p.M >= 128 && p.N >= 128 && tc_gemm_usable(p, trans_a, trans_b))
-    return tc_gemm(p, trans_a, trans_b, batches, nullptr, s);
+    return tc_gemm(p, trans_a, trans_b, batches, status, s);
   return launch_gemm(p, trans_a, trans_b, batches, s);
 }
 
@@ -815,7 +815,8 @@ extern "C" size_t gq_prepare_hinv_workspace_size(int64_t B, int64_t C) {
 }
 
 extern "C" int gq_prepare_hinv(const float* H, int64_t B, int64_t C, float damp, float* U, int32_t* info,
-                               float* damp_used, void* workspace, size_t workspace_bytes, void* stream) {
+                               float* damp_used, void* workspace, size_t workspace_bytes, int32_t* status,
+                               void* stream) {
   GQ_REQUIRE(H && U && info, "gq_prepare_hinv: null pointer");
   GQ_REQUIRE(B > 0 && C > 0 && C % NB == 0, "gq_prepare_hinv: C=%lld must be a positive multiple of %d",
              (long long)C, NB);
@@ -885,7 +886,7 @@ extern "C" int gq_prepare_hinv(const float* H, int64_t B, int64_t C, float damp,
         g.alpha = 1.0f;
         g.beta = 0.0f;
         g.skip = st.skip;
-        int r = tc_gemm(g, false, true, B, nullptr, s);
+        int r = tc_gemm(g, false, true, B, status, s);
         if (r != GQ_OK) return r;
         if (side_pending) GQ_CUDA_TRY(cudaStreamWaitEvent(s, ev_side, 0));
         // next block column: A[i][k+1] -= L[i][k] L[k+1][k]^T, i > k
@@ -896,7 +897,7 @@ extern "C" int gq_prepare_hinv(const float* H, int64_t B, int64_t C, float damp,
         u.Cm = Hr + int64_t(k + 1) * NB * C + int64_t(k + 1) * NB;
         u.alpha = -1.0f;
         u.beta = 1.0f;
-        r = tc_gemm(u, false, true, B, nullptr, s);
+        r = tc_gemm(u, false, true, B, status, s);
         if (r != GQ_OK) return r;
         side_pending = false;
         if (m > 1) {
@@ -908,7 +909,7 @@ extern "C" int gq_prepare_hinv(const float* H, int64_t B, int64_t C, float damp,
           w.Bm = w.A;
           w.Cm = Hr + int64_t(k + 2) * NB * C + int64_t(k + 2) * NB;
           w.M = w.N = (m - 1) * NB;
-          r = tc_gemm(w, false, true, B, nullptr, side, true);
+          r = tc_gemm(w, false, true, B, status, side, true);
           if (r != GQ_OK) return r;
           GQ_CUDA_TRY(cudaEventRecord(ev_side, side));
           side_pending = true;
@@ -966,7 +967,7 @@ extern "C" int gq_prepare_hinv(const float* H, int64_t B, int64_t C, float damp,
       g1.alpha = 1.0f;
       g1.beta = 0.0f;
       g1.skip = st.info;
-      int r = gemm(g1, true, true, B * npairs, s);
+      int r = gemm(g1, true, true, B * npairs, status, s);
       if (r != GQ_OK) return r;
       GemmBatch g2 = g1;  // Linv(r0.., c0..) = -Dinv * X, X(t, c) = Xt[c][t]
       g2.A = U + r0 * C + r0;
@@ -976,7 +977,7 @@ extern "C" int gq_prepare_hinv(const float* H, int64_t B, int64_t C, float damp,
       g2.N = int(sz);
       g2.K = int(dsz);
       g2.alpha = -1.0f;
-      r = gemm(g2, false, true, B * npairs, s);
+      r = gemm(g2, false, true, B * npairs, status, s);
       if (r != GQ_OK) return r;
     }
   }
@@ -994,7 +995,7 @@ extern "C" size_t gq_gptq_affine_workspace_size(int64_t B, int64_t R, int64_t C,
 extern "C" int gq_gptq_affine(float* W, const void* W_orig, int w_dtype, const float* U, int64_t B, int64_t R,
                               int64_t C, int bits, int group_size, int block_size, int clip, int storage_dtype,
                               uint8_t* q, void* scales, void* biases, float* rel_err, void* workspace,
-                              size_t workspace_bytes, void* stream) {
+                              size_t workspace_bytes, int32_t* status, void* stream) {
   GQ_REQUIRE(W && U && q && scales && biases, "gq_gptq_affine: null pointer");
   GQ_REQUIRE(bits >= 1 && bits <= 8, "gq_gptq_affine: bits %d", bits);
   GQ_REQUIRE(group_size == 32 || group_size == 64 || group_size == 128 || group_size == 256,
@@ -1063,7 +1064,7 @@ extern "C" int gq_gptq_affine(float* W, const void* W_orig, int w_dtype, const f
       g.K = int(bs);
       g.alpha = -1.0f;
       g.beta = 1.0f;
-      r = gemm(g, false, false, B, s);
+      r = gemm(g, false, false, B, status, s);
       if (r != GQ_OK) return r;
     }
   }

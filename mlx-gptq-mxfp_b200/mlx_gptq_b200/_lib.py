@@ -45,12 +45,12 @@ SIGNATURES = {
     "gq_dead_columns": (I32, [P, I64, I64, P, P]),
     "gq_mx_prepare_hinv": (I32, [P, I64, I64, F32, P, P, P, P]),
     "gq_prepare_hinv_workspace_size": (SZ, [I64, I64]),
-    "gq_prepare_hinv": (I32, [P, I64, I64, F32, P, P, P, P, SZ, P]),
+    "gq_prepare_hinv": (I32, [P, I64, I64, F32, P, P, P, P, SZ, P, P]),
     "gq_gptq_mxfp_workspace_size": (SZ, [I64, I64, I64]),
     "gq_gptq_mxfp": (I32, [P, I32, P, P, P, P, I64, I64, I64, I32, I32, P, P, P, P, I32, P, P, SZ, P]),
     "gq_gptq_mxfp_noalloc": (I32, [P, I32, P, P, P, P, I64, I64, I64, I32, I32, P, P, P, P, I32, P, P]),
     "gq_gptq_affine_workspace_size": (SZ, [I64, I64, I64, I32, I32]),
-    "gq_gptq_affine": (I32, [P, P, I32, P, I64, I64, I64, I32, I32, I32, I32, I32, P, P, P, P, P, SZ, P]),
+    "gq_gptq_affine": (I32, [P, P, I32, P, I64, I64, I64, I32, I32, I32, I32, I32, P, P, P, P, P, SZ, P, P]),
     "gq_gemm_f32": (I32, [P, P, P, I64, I64, I64, I64, I64, I64, I32, I32, I64, I64, I64, I64, I64, I64, I64, I64,
                           F32, F32, P, I32, P, P]),
     "gq_prepare_weights": (I32, [P, I32, P, I64, I64, I64, P, P]),

@@ -64,10 +64,11 @@ def _prepare_hinv(H: torch.Tensor, damp: float, max_attempts: int = 6) -> torch.
     ws = torch.empty(L.lib().gq_prepare_hinv_workspace_size(B, Cf), dtype=torch.uint8, device=dev)
     L.raise_on_device_timeout(dev)  # a Hessian formed on this device finished every wait
     st = L.lib().gq_prepare_hinv(L.ptr(Hf), B, Cf, float(damp), L.ptr(U), L.ptr(info), L.ptr(used),
-                                 L.ptr(ws), ws.numel(), L.stream_ptr(dev))
+                                 L.ptr(ws), ws.numel(), L.ptr(L.status_word(dev)), L.stream_ptr(dev))
     if st == L.GQ_ERR_NOT_PD:
         raise _not_pd_error(Hc, info != 0, B)
     L.check(st, "_prepare_hinv")
+    L.raise_on_device_timeout(dev)  # the factor's tensor-core GEMMs finished every wait
     esc = used > damp
     if bool(esc.any()):
         log.warning("cholesky failed for %d/%d matrices, damp -> %.3g", int(esc.sum()), B, float(used.max()))
@@ -137,7 +138,8 @@ def _solve_affine(W: torch.Tensor, W_orig: torch.Tensor | None, H: torch.Tensor,
     L.check(lib.gq_gptq_affine(L.ptr(W), L.ptr(W_orig), L.DTYPE_CODE[W_orig.dtype] if W_orig is not None else 0,
                                L.ptr(U), B, R, C, bits, group_size, block_size, L.CLIP_CODE[clip],
                                L.DTYPE_CODE[storage_dtype], L.ptr(q), L.ptr(scales), L.ptr(biases), L.ptr(rel),
-                               L.ptr(ws), ws.numel(), stream), "gptq affine")
+                               L.ptr(ws), ws.numel(), L.ptr(L.status_word(dev)), stream), "gptq affine")
+    L.raise_on_device_timeout(dev)  # the trailing updates finished every wait
     return q, scales, biases, W, rel
 
 

@@ -63,7 +63,7 @@ def test_argument_errors_without_gpu(lib):
     assert st == _lib.GQ_ERR_ARG
     st = lib.gq_gptq_mxfp(p, 0, p, p, None, None, 1, 8, 64, 1, 7, p, None, p, None, 0, None, None, 0, None)
     assert st == _lib.GQ_ERR_ARG and b"algorithm" in lib.gq_last_error()
-    st = lib.gq_gptq_affine(p, None, 0, p, 1, 8, 96, 4, 64, 128, 1, 1, p, p, p, None, None, 0, None)
+    st = lib.gq_gptq_affine(p, None, 0, p, 1, 8, 96, 4, 64, 128, 1, 1, p, p, p, None, None, 0, None, None)
     assert st == _lib.GQ_ERR_ARG  # 96 not divisible by 64
 
 
