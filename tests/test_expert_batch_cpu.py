@@ -20,6 +20,22 @@ def test_plan_experts_balances_a_skewed_batch():
     assert all(sum(1 for e in s if counts[e] == 500_000) == 1 for s in shares)  # one heavy expert each
 
 
+def test_plan_experts_charges_experts_without_tokens():
+    """An expert without tokens costs its RTN fallback, so the rank that takes it gets
+    fewer routed tokens than a rank without one."""
+    from mlx_gptq_b200.expert_batch import RTN_FALLBACK_UNITS, SOLVE_UNITS_PER_ELEM, plan_experts
+
+    counts = [30_000] * 8 + [0]
+    shares = plan_experts(counts, 3, (2048, 768), 4_718_592)
+    per_token = 2048 ** 2 + 768 ** 2
+    cost = lambda sh: sum(counts[e] * per_token + SOLVE_UNITS_PER_ELEM * 4_718_592 +
+                          (RTN_FALLBACK_UNITS if counts[e] == 0 else 0) for e in sh)
+    holder = next(sh for sh in shares if 8 in sh)
+    assert sorted(e for sh in shares for e in sh) == list(range(9))
+    assert max(map(cost, shares)) - min(map(cost, shares)) <= cost([0])  # LPT: within one item
+    assert sum(counts[e] for e in holder) <= min(sum(counts[e] for e in sh) for sh in shares if 8 not in sh)
+
+
 def test_piece_layout_cuts_heavy_experts_and_keeps_rows():
     from mlx_gptq_b200.expert_batch import piece_layout
 
