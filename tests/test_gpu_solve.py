@@ -249,3 +249,23 @@ def test_affine_columns_not_a_multiple_of_64(C):
     oq, os_, ob, oWdq, orel = og.solve_gptq(W, H.copy(), 4, 32, mode="affine")
     assert (q.cpu().numpy() == oq).mean() >= 0.999
     np.testing.assert_allclose(rel.cpu().numpy(), orel, rtol=1e-3)
+
+
+@pytest.mark.parametrize("group_size", [32, 64, 128, 256])
+def test_affine_256_column_blocks_vs_oracle(group_size):
+    """block_size 256 (gptq.py:183-272 with blocksize=256): the column loop's 16-lanes-per-row
+    form and its trailing updates against the oracle at the same block size, at the
+    solver tolerances (codes >= 99.9%, proxy loss within 0.5%)."""
+    from mlx_gptq_b200.gptq import gptq_quantize
+
+    W, H = _correlated(2, 96, 512, 2048, seed=21 + group_size)
+    Wg, Hg = _cuda(W.copy()), _cuda(H.copy())
+    q, s, b, Wdq, _ = gptq_quantize(Wg, Hg, 4, group_size, block_size=256)
+    Wo, Ho = W.copy(), H.copy()
+    ref = ogptq.gptq_quantize(Wo, Ho, 4, group_size, block_size=256)
+    ref_q, ref_Wdq = ref[0], ref[3]
+    agree = (q.cpu().numpy() == ref_q).mean()
+    assert agree >= CODE_AGREEMENT, agree
+    ours = ogptq.proxy_loss(W, Wdq.cpu().numpy(), H)
+    theirs = ogptq.proxy_loss(W, ref_Wdq, H)
+    np.testing.assert_allclose(ours, theirs, rtol=PROXY_RTOL)
