@@ -171,11 +171,12 @@ class C3Step:
 
     def launches(self) -> int:
         """Kernels of this library per step: per parameter the row pass (gate_up: the
-        routed-row gather; down: the partial-step tails) and the Hessian, dead columns,
-        block factors, column loop, rel_err reduction, and RTN when this rank has
-        experts without tokens."""
+        routed-row gather; down: the partial-step tails) and the Hessian, the piece merge
+        when an expert was cut into pieces, dead columns, block factors, column loop,
+        rel_err reduction, and RTN when this rank has experts without tokens."""
         rtn = 1 if any(c == 0 for c in self.inp.counts_mine) else 0
-        return 2 * (2 + 4 + rtn)
+        merges = sum(1 for lay in (self.lay_gu, self.lay_dn) if lay.extra)
+        return 2 * (2 + 4 + rtn) + merges
 
     def run(self, record: bool = False, X=None, W_gu=None, W_dn=None, acts=None, tok=None, ready=None):
         from mlx_gptq_b200.expert_batch import expert_hessians
