@@ -104,3 +104,17 @@ def test_span_layout_covers_each_expert_once():
     for i, c in enumerate(counts):
         covered = sorted(r for a, k in rows[i] for r in range(a, a + k))
         assert covered == list(range(int(offsets[i]), int(offsets[i]) + c))
+
+
+def test_merge_plan_groups_pieces_by_expert_in_order():
+    """The merge plan handed to gq_hessian_merge_pieces: one target per expert with extra
+    pieces, its pieces in piece order, CSR pointers consistent; None without pieces."""
+    from mlx_gptq_b200.expert_batch import PieceLayout
+
+    lay = PieceLayout(n=4, extra=[(0, 1), (2, 1), (0, 2), (0, 3), (2, 2)], offsets=torch.zeros(10, dtype=torch.int64))
+    t, ptr, pieces = lay.merge_plan("cpu")
+    assert t.tolist() == [0, 2]
+    assert ptr.tolist() == [0, 3, 5]
+    assert pieces.tolist() == [4, 6, 7, 5, 8]  # expert 0: pieces 4, 6, 7; expert 2: pieces 5, 8
+    assert lay.merge_plan("cpu") is lay.merge  # built once
+    assert PieceLayout(n=2, extra=[], offsets=torch.zeros(3, dtype=torch.int64)).merge_plan("cpu") is None
