@@ -442,6 +442,41 @@ def extra_c2(device, steps, warmup, peak_tf, peak_hbm, src):
                                      "bytes_per_step": col_bytes, "peak_source": f"{src} hbm_gbs"}}
 
 
+def trailing_update_roofline(device, steps, peak_hbm, src):
+    """The affine trailing update W[:, i2:] -= Err U[i1:i2, i2:] alone (tc_gemm_kernel through
+    the gq_gemm_f32 hook, the engine solve_gptq uses) at a C1-sized block: M = 4096 rows,
+    N = 3072 columns, K = 128; W rotates over four 64 MB matrices so the slice is not
+    L2-resident between launches. HBM roofline on the W slice read and written once."""
+    import ctypes
+
+    from mlx_gptq_b200 import _lib as L
+
+    R, C, K, i2 = 4096, 4096, 128, 1024
+    N = C - i2
+    g = torch.Generator(device=device).manual_seed(3)
+    Ws = [torch.randn(R, C, generator=g, device=device) for _ in range(4)]
+    Err = torch.randn(R, K, generator=g, device=device) * 1e-3
+    Ub = torch.randn(K, C, generator=g, device=device)
+    p = lambda t: ctypes.c_void_p(t.data_ptr())
+    it = [0]
+
+    def launch():
+        W = Ws[it[0] % 4]
+        it[0] += 1
+        L.check(L.lib().gq_gemm_f32(p(Err), p(Ub[:, i2:]), p(W[:, i2:]), R, N, K, K, C, C, 0, 0, 1, 1, 0, 0, 0, 0, 0, 0,
+                                    -1.0, 1.0, None, 1, L.ptr(L.status_word(device)), L.stream_ptr(device)),
+                "trailing update")
+
+    ms = _timed(launch, steps, 4)
+    L.raise_on_device_timeout(device)
+    nbytes = 2.0 * R * N * 4
+    return {"kernel": "tc_gemm_kernel (tcgen05 kind::tf32 3xTF32, TMA reduce-add into W), M 4096 N 3072 K 128",
+            "bound": "hbm", "achieved": nbytes / (ms / 1e3) / 1e9, "peak": peak_hbm, "unit": "GB/s",
+            "frac": nbytes / (ms / 1e3) / 1e9 / peak_hbm, "bytes_per_launch": nbytes, "ms_per_launch": ms,
+            "tflops": 2.0 * R * N * K / (ms / 1e3) / 1e12, "peak_source": f"{src} hbm_gbs",
+            "l2": "W rotates over four 64 MB matrices (256 MB > L2)"}
+
+
 def extra_c1(device, steps, warmup, peak_tf, src):
     """C1: H from X [524288, 4096], then solve_gptq affine 4-bit g64 mse
     (factor, column loop, lazy trailing update)."""
@@ -463,7 +498,7 @@ def extra_c1(device, steps, warmup, peak_tf, src):
             "roofline_hessian": {"achieved": flop / (hess_ms / 1e3) / 1e12, "peak": peak_tf, "unit": "TFLOP/s",
                                  "frac": flop / (hess_ms / 1e3) / 1e12 / peak_tf},
             "roofline_affine": {"kernel": "gq_gptq_affine + gq_prepare_hinv (whole solve_gptq)",
-                                "bound": "tensor (3xTF32 mma.sync trailing update) / latency (factor chain)",
+                                "bound": "hbm (tcgen05 3xTF32 trailing update, TMA reduce-add into W) / latency (factor chain)",
                                 "trailing_update_flop": trailing,
                                 "achieved": trailing / (solve_ms / 1e3) / 1e12, "unit": "TFLOP/s",
                                 "note": "trailing-update FLOP over the whole solve's time (factor + column loop + "
@@ -967,6 +1002,8 @@ def run_c3(args, ws, rank, local):
         from mlx_gptq_b200.artifacts import unpack_nibbles
 
         line["roofline_pack"] = extra_pack(device, peak_hbm, src, unpack_nibbles(outs[0]).reshape(-1, C3_H))
+        torch.cuda.empty_cache()
+        line["roofline_trailing_update"] = trailing_update_roofline(device, 20, peak_hbm, src)
     if ws == 1 and not args.no_cpu_baseline:
         del step, inp
         torch.cuda.empty_cache()
